@@ -1,0 +1,215 @@
+/*
+ * mgpu_cuda.h - C ABI of the B200 (sm_100a) matmul path that replaces MVLM's OpenCL
+ * GEMM/GEMV dispatch.  Plain pointers, sizes and opaque handles only.
+ *
+ * Each entry point cites the reference interface it stands in for (paths relative to the
+ * drxddy/MVLM project root).  The C++ mirror with the reference's own names and types
+ * (mgpu::dispatch_gemm_image, cl_mem, cl_event, ...) is include/mgpu_compute.hpp.
+ *
+ * Conventions (the reference's, src/engine/compute.cpp:12-17):
+ *   - Functions returning a handle return NULL on error; the reason is in
+ *     mgpu_last_error() / mgpu_last_error_string() (thread-local).  Nothing aborts.
+ *   - Work is enqueued in order on the device's single stream (the reference's one in-order
+ *     queue, src/engine/device.cpp:297-300); no call synchronises implicitly except
+ *     mgpu_buf_read/write, mgpu_wait_event and mgpu_finish.
+ *   - A device handle is used by one host thread at a time.
+ */
+#ifndef MGPU_CUDA_H
+#define MGPU_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element / block types.  Values are ggml's GGMLType (src/models/gguf_loader.h:12-30);
+ * BF16 carries ggml's value 30, which the reference's enum does not list. */
+enum mgpu_type {
+    MGPU_F32 = 0,
+    MGPU_F16 = 1,
+    MGPU_Q4_0 = 2,
+    MGPU_Q8_0 = 8,
+    MGPU_BF16 = 30
+};
+
+/* Storage order of a 2-D weight.
+ * KN: B[K][N] row-major, the orientation the reference kernels read (gemm.cl:28,159,221).
+ * NK: W[N][K] rows, GGUF-native (ne0 = K fastest); the only order for Q4_0/Q8_0. */
+enum mgpu_layout {
+    MGPU_LAYOUT_KN = 0,
+    MGPU_LAYOUT_NK = 1
+};
+
+/* Error codes returned by mgpu_last_error(). */
+enum mgpu_status {
+    MGPU_OK = 0,
+    MGPU_ERR_INVALID_ARG = 1,   /* null handle, bad shape / type / layout / alignment */
+    MGPU_ERR_UNSUPPORTED = 2,   /* valid request this build does not implement */
+    MGPU_ERR_CUDA = 3,          /* a CUDA runtime / driver call failed */
+    MGPU_ERR_OUT_OF_MEMORY = 4,
+    MGPU_ERR_DEVICE_TIMEOUT = 5 /* a kernel's bounded wait expired; its output is invalid */
+};
+
+typedef struct mgpu_device mgpu_device; /* replaces DeviceInfo (src/engine/device.h:13-55) */
+typedef struct mgpu_buf mgpu_buf;       /* replaces cl_mem */
+typedef struct mgpu_event mgpu_event;   /* replaces cl_event */
+typedef void* mgpu_program;             /* replaces cl_program; accepted and ignored */
+
+/* Binary-compatible with TensorInfo (src/models/gguf_loader.h:51-58), so a caller can pass
+ * the reference loader's `const TensorInfo*` directly. */
+typedef struct mgpu_tensor_info {
+    char name[256];
+    uint32_t n_dims;
+    uint64_t dims[4];
+    uint32_t type;
+    uint64_t offset;
+    size_t data_size;
+} mgpu_tensor_info;
+
+/* ---------------------------------------------------------------- errors ---------- */
+int mgpu_last_error(void);
+const char* mgpu_last_error_string(void);
+void mgpu_clear_error(void);
+
+/* ---------------------------------------------------------------- device ---------- */
+/* init_device (src/engine/device.h:58): select CUDA device `ordinal`, create the in-order
+ * stream and the per-device status word.  NULL on failure. */
+mgpu_device* mgpu_init_device(int ordinal);
+void mgpu_release_device(mgpu_device* dev);
+int mgpu_device_ordinal(const mgpu_device* dev);
+int mgpu_device_sm_count(const mgpu_device* dev);
+size_t mgpu_device_l2_bytes(const mgpu_device* dev);
+/* The cudaStream_t all dispatches are enqueued on.  mgpu_set_stream replaces it (the caller
+ * keeps ownership of a stream it passes in; NULL restores the device's own stream). */
+void* mgpu_device_stream(const mgpu_device* dev);
+int mgpu_set_stream(mgpu_device* dev, void* cuda_stream);
+/* 0: dispatches return NULL (no event recorded, like passing no event in OpenCL);
+ * 1: dispatches return a completion event; 2 (default): a profiling event whose
+ * mgpu_profile_end gives the launch's device time, like CL_QUEUE_PROFILING_ENABLE. */
+int mgpu_set_event_mode(mgpu_device* dev, int mode);
+/* clFinish: wait for all enqueued work, then report any kernel status (timeouts). */
+int mgpu_finish(mgpu_device* dev);
+
+/* ---------------------------------------------------------------- memory ---------- */
+/* create_buffer (src/engine/memory.h:19): device allocation, optionally filled from host. */
+mgpu_buf* mgpu_create_buffer(mgpu_device* dev, size_t bytes, const void* host_src);
+/* create_weight_image (src/engine/memory.h:16, memory.cpp:28-79): fp16 weight of `rows` x
+ * `cols` (the reference kernels read it as B[K=rows][N=cols]).  Stored KN with the row pitch
+ * padded with zeros to a multiple of 8 elements (the reference pads to 4 for RGBA texels). */
+mgpu_buf* mgpu_create_weight_image(mgpu_device* dev, int rows, int cols, const uint16_t* data);
+/* Wrap caller-owned device memory (e.g. a torch tensor's data_ptr); not freed on release. */
+mgpu_buf* mgpu_wrap_buffer(mgpu_device* dev, void* device_ptr, size_t bytes);
+/* A sub-range view of a buffer (shares memory; released independently). */
+mgpu_buf* mgpu_buf_view(mgpu_buf* buf, size_t offset, size_t bytes);
+/* Tag a buffer's contents: element/block type, layout, logical rows x cols and row pitch in
+ * elements (0 = dense).  Untagged buffers are MGPU_F16 / KN, which is what the reference's
+ * cl_mem arguments hold. */
+int mgpu_buf_set_format(mgpu_buf* buf, int type, int layout, int64_t rows, int64_t cols, int64_t ld);
+void* mgpu_buf_device_ptr(const mgpu_buf* buf);
+size_t mgpu_buf_bytes(const mgpu_buf* buf);
+/* Blocking host<->device copies (clEnqueueWrite/ReadBuffer with blocking=CL_TRUE). */
+int mgpu_buf_write(mgpu_buf* buf, size_t offset, const void* src, size_t bytes);
+int mgpu_buf_read(const mgpu_buf* buf, size_t offset, void* dst, size_t bytes);
+/* Stream-ordered copies (clEnqueueWrite/ReadBuffer with blocking=CL_FALSE); host memory
+ * should be pinned (mgpu_host_alloc) for the copy to be asynchronous. */
+int mgpu_buf_write_async(mgpu_buf* buf, size_t offset, const void* src, size_t bytes);
+int mgpu_buf_read_async(const mgpu_buf* buf, size_t offset, void* dst, size_t bytes);
+void* mgpu_host_alloc(size_t bytes);
+void mgpu_host_free(void* p);
+void mgpu_release_buffer(mgpu_buf* buf);
+
+/* upload_weight_image / upload_weight_buffer (src/models/moondream2.cpp:62-95): copy a GGUF
+ * tensor's packed bytes to the device unchanged (Q4_0 18-byte / Q8_0 34-byte blocks stay
+ * packed) and tag it NK with rows = dims[1], cols = dims[0]. */
+mgpu_buf* mgpu_upload_weight(mgpu_device* dev, const mgpu_tensor_info* tensor, const void* host_data);
+
+/* ---------------------------------------------------------------- dispatch -------- */
+/* src/engine/compute.h:16-18 gemm_naive, :21-23 gemm_tiled, :26-28 gemm_image:
+ * C[M,N] = A[M,K] * B[K,N].  All three run the same tcgen05 GEMM; A, B fp16 or bf16 (same
+ * type), B layout KN or NK, C fp16 / bf16 / fp32, fp32 accumulation.  Returns the event. */
+mgpu_event* mgpu_dispatch_gemm_naive(const mgpu_device* dev, mgpu_program program, mgpu_buf* A,
+                                     mgpu_buf* B, mgpu_buf* C, int M, int N, int K);
+mgpu_event* mgpu_dispatch_gemm_tiled(const mgpu_device* dev, mgpu_program program, mgpu_buf* A,
+                                     mgpu_buf* B, mgpu_buf* C, int M, int N, int K);
+mgpu_event* mgpu_dispatch_gemm_image(const mgpu_device* dev, mgpu_program program, mgpu_buf* A,
+                                     mgpu_buf* B_img, mgpu_buf* C, int M, int N, int K);
+/* src/engine/compute.h:31-33 gemv: y[1,N] = x[1,K] * W[K,N].  x fp16/bf16/fp32; W any type
+ * (f32/f16/bf16 in KN or NK, Q4_0/Q8_0 in NK); y fp16/bf16/fp32; fp32 accumulation. */
+mgpu_event* mgpu_dispatch_gemv(const mgpu_device* dev, mgpu_program program, mgpu_buf* x,
+                               mgpu_buf* W_img, mgpu_buf* y, int N, int K);
+/* src/engine/compute.h:101-105 patch_embed: image [C,H,W] (fp16) -> patches
+ * [(H/ph)*(W/pw), embed_dim] = im2col(image) * proj_weight[C*ph*pw, embed_dim] + bias. */
+mgpu_event* mgpu_dispatch_patch_embed(const mgpu_device* dev, mgpu_program program, mgpu_buf* image,
+                                      mgpu_buf* proj_weight, mgpu_buf* proj_bias, mgpu_buf* patches,
+                                      int C, int H, int W, int patch_h, int patch_w, int embed_dim);
+/* src/engine/compute.h:128-131 vision_proj: output[num_patches, llm_dim] =
+ * visual_tokens[num_patches, vision_dim] * proj_weight + proj_bias (bias may be NULL). */
+mgpu_event* mgpu_dispatch_vision_proj(const mgpu_device* dev, mgpu_program program,
+                                      mgpu_buf* visual_tokens, mgpu_buf* proj_weight,
+                                      mgpu_buf* proj_bias, mgpu_buf* output, int num_patches,
+                                      int vision_dim, int llm_dim);
+
+/* New (no reference counterpart: the reference has no quantised kernels, README.md:57).
+ * y[1,N] = x[1,K] * dequant(W)^T with W packed GGUF blocks [N][K/32] of `type`. */
+mgpu_event* mgpu_gemv_q(const mgpu_device* dev, mgpu_buf* x, mgpu_buf* W, mgpu_buf* y, int N, int K,
+                        int type);
+/* C[M,N] = A[M,K] * dequant(W)^T (+ bias[N] if non-NULL), W packed [N][K/32] blocks, A
+ * fp16/bf16; the blocks are dequantised to A's type inside the GEMM's weight loads. */
+mgpu_event* mgpu_gemm_q(const mgpu_device* dev, mgpu_buf* A, mgpu_buf* W, mgpu_buf* C, int M, int N,
+                        int K, int type, mgpu_buf* bias);
+/* General entry: C = A * op(B) + bias, every operand's type/layout taken from its tag. */
+mgpu_event* mgpu_gemm(const mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N,
+                      int K, mgpu_buf* bias);
+/* out[n] = dequant(W)[n] for n elements (out fp32, fp16 or bf16 per its tag). */
+mgpu_event* mgpu_dequant(const mgpu_device* dev, mgpu_buf* W, mgpu_buf* out, int64_t n, int type);
+
+/* ---------------------------------------------------------------- events ---------- */
+int mgpu_wait_event(mgpu_event* ev);                 /* clWaitForEvents(1, &ev) */
+void mgpu_release_event(mgpu_event* ev);             /* clReleaseEvent */
+double mgpu_profile_end(mgpu_event* ev);             /* profile_end (src/engine/profiler.h:16): ms */
+float mgpu_event_elapsed_ms(mgpu_event* start, mgpu_event* end);
+/* Record a marker event on the device stream now (also inside a graph capture, where it
+ * becomes a node of the graph); mgpu_event_elapsed_ms(a, b) gives the device time between
+ * two markers.  Release with mgpu_release_event. */
+mgpu_event* mgpu_record_event(mgpu_device* dev);
+
+/* ---------------------------------------------------------------- graphs ---------- */
+/* CUDA-graph capture of a dispatch sequence on the device's stream (no reference
+ * counterpart: the reference planned Qualcomm recordable queues, README.md:121-129, and
+ * waits on the host after every op).  Between begin and end, dispatches are recorded, not
+ * run; they must not grow the device's scratch (run each one once before capturing).
+ * Dispatches return NULL while capturing. */
+int mgpu_capture_begin(mgpu_device* dev);
+typedef struct mgpu_graph mgpu_graph;
+mgpu_graph* mgpu_capture_end(mgpu_device* dev);
+int mgpu_graph_launch(mgpu_graph* graph);
+void mgpu_graph_release(mgpu_graph* graph);
+
+/* Failure-detection self test: launches one CTA that waits on an mbarrier nobody arrives
+ * on, with a wait limit of `limit_ns`.  The wait expires, the kernel records
+ * MGPU_ERR_DEVICE_TIMEOUT in the device status word and exits; the next mgpu_finish then
+ * reports MGPU_ERR_DEVICE_TIMEOUT.  Returns the launch status. */
+int mgpu_selftest_bounded_wait(mgpu_device* dev, uint64_t limit_ns);
+
+/* ---------------------------------------------------------------- ggml table ------ */
+size_t mgpu_ggml_type_size(int type);       /* ggml_type_size (gguf_loader.h:79) */
+int mgpu_ggml_type_block_size(int type);    /* ggml_type_block_size (gguf_loader.h:82) */
+
+/* ---------------------------------------------------------------- synthetic data --- */
+/* Device-side seeded generators used by the benchmark (no reference counterpart): the
+ * SplitMix64 stream of element i is seeded with seed + i, so results do not depend on the
+ * launch shape. */
+int mgpu_fill_uniform(const mgpu_device* dev, mgpu_buf* out, int64_t n, uint64_t seed, float lo,
+                      float hi);
+int mgpu_fill_normal(const mgpu_device* dev, mgpu_buf* out, int64_t n, uint64_t seed, float sigma);
+/* fp32 -> GGUF Q4_0 / Q8_0 blocks on the device (ggml reference quantiser). */
+int mgpu_quantize(const mgpu_device* dev, mgpu_buf* src_f32, mgpu_buf* dst_blocks, int64_t n, int type);
+/* Element-type conversion of n values between two buffers (f32/f16/bf16). */
+int mgpu_convert(const mgpu_device* dev, mgpu_buf* src, mgpu_buf* dst, int64_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MGPU_CUDA_H */

@@ -1,0 +1,528 @@
+// gemm_tc.cu - tcgen05 tensor-core GEMM for sm_100a (replaces gemm_naive / gemm_tiled /
+// gemm_image, src/kernels/gemm.cl:26-200, and the GEMM math of patch_embed / vision_proj,
+// src/kernels/vision.cl:118-197, :402-441).
+//
+// C[M,N] = A[M,K] * op(B) (+ bias[N]), fp16 or bf16 operands, fp32 accumulation in TMEM.
+//
+// One persistent CTA per SM walks output tiles of 128 x BN (BN = 256 or 128), K in steps
+// of 64 (one 128-byte swizzle atom of 16-bit elements).  Warp roles:
+//   warp 0      TMA producer: A tiles (and 16-bit B tiles) with cp.async.bulk.tensor, 128B
+//               swizzle, into a ring of smem stages; OOB boxes are zero-filled, which pads
+//               ragged M, N and K.
+//   warp 1      allocates TMEM (2 x BN fp32 columns: a double-buffered accumulator) and one
+//               elected lane issues tcgen05.mma (M=128, N=BN, K=16 per instruction) and
+//               tcgen05.commit to release stages / publish finished accumulators.
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns per warp, + bias, convert,
+//               store; overlaps the next tile's main loop through the second accumulator.
+//   warps 6-13  (Q8_0 / Q4_0 B only) dequantisers: read the packed GGUF blocks of the B
+//               tile straight from global memory, decode them exactly in fp32, round to the
+//               operand type and write them into the stage in the same 128B-swizzled
+//               K-major layout TMA would have produced, then fence.proxy.async + arrive.
+// B layouts: NK (K-major, e.g. GGUF F16 tensors) and KN (MN-major: the reference kernels'
+// B[K][N], read by tcgen05 with the B-transpose bit).  No cluster multicast anywhere.
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace mgpu_dev;
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+constexpr int kABytes = BM * BK * 2;  // 16 KB
+constexpr int kSmemBudget = 200 * 1024;
+enum BMode { B_TMA_K = 0, B_TMA_MN = 1, B_Q8 = 2, B_Q4 = 3 };
+constexpr int kDqWarps = 8;
+
+__host__ __device__ constexpr int gemm_threads(int bmode) { return 192 + (bmode >= B_Q8 ? kDqWarps * 32 : 0); }
+__host__ __device__ constexpr int stage_bytes(int bn) { return kABytes + bn * BK * 2; }
+__host__ __device__ constexpr int num_stages(int bn) { return kSmemBudget / stage_bytes(bn); }
+
+struct GemmArgs {
+    int M, N, K, num_kb, tiles_m, tiles_n;
+    void* C;
+    int64_t ldc;
+    int c_type;
+    const void* bias;
+    int bias_type;
+    const uint8_t* Bq;   // packed GGUF rows (quantised modes)
+    int64_t bq_row_bytes;
+    const uint8_t* bq_end;
+    int* status;
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float bias_at(const void* bias, int type, int n) {
+    if (type == MGPU_F32) return reinterpret_cast<const float*>(bias)[n];
+    if (type == MGPU_F16) return __half2float(reinterpret_cast<const __half*>(bias)[n]);
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
+}
+
+__device__ __forceinline__ void store_out(void* C, int type, size_t idx, float v) {
+    if (type == MGPU_F32) reinterpret_cast<float*>(C)[idx] = v;
+    else if (type == MGPU_F16) reinterpret_cast<__half*>(C)[idx] = __float2half_rn(v);
+    else reinterpret_cast<__nv_bfloat16*>(C)[idx] = __float2bfloat16_rn(v);
+}
+
+// Raw words of one packed block (Q4_0: 5 words / 18 bytes, Q8_0: 9 words / 34 bytes) from a
+// 2-byte-aligned address: the aligned words that cover it plus the realignment selector.
+template <int NW>
+struct RawBlock {
+    uint32_t w[NW];
+    uint32_t par;  // 0 or 2: byte offset of the block inside w[0]
+    bool valid;
+};
+
+template <int NW, int BB>
+__device__ __forceinline__ void load_block(RawBlock<NW>& rb, const uint8_t* p, const uint8_t* end, bool valid) {
+    rb.valid = valid;
+    rb.par = 0;
+    if (!valid) return;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    rb.par = (uint32_t)(a & 3u);
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(a & ~(uintptr_t)3);
+    if (reinterpret_cast<const uint8_t*>(wp + NW) <= end) {
+#pragma unroll
+        for (int i = 0; i < NW; ++i) rb.w[i] = __ldg(wp + i);
+    } else {
+        // Last block of the buffer: do not read the 2 bytes past its end.
+        const uint16_t* hp = reinterpret_cast<const uint16_t*>(p);
+        uint16_t h[2 * NW];
+#pragma unroll
+        for (int i = 0; i < 2 * NW; ++i) h[i] = (i < BB / 2) ? __ldg(hp + i) : (uint16_t)0;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) rb.w[i] = (uint32_t)h[2 * i] | ((uint32_t)h[2 * i + 1] << 16);
+        rb.par = 0;
+    }
+}
+
+#define MAGIC_F(v, byte_sel) __uint_as_float(prmt((v), 0x4B000000u, 0x7540u | (byte_sel)))
+
+// Decode one block into 32 values of T (4 x 16 bytes) and store them to the four swizzled
+// 16-byte chunks `dst[0..3]`.
+template <int BMODE, typename T, int NW>
+__device__ __forceinline__ void decode_store(const RawBlock<NW>& rb, uint4* const (&dst)[4]) {
+    if (!rb.valid) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) *dst[j] = make_uint4(0, 0, 0, 0);
+        return;
+    }
+    const uint32_t sel = rb.par ? 0x7654u : 0x5432u;
+    const uint32_t dsel = rb.par ? 0x4432u : 0x4410u;
+    const float d = __half2float(__ushort_as_half((unsigned short)prmt(rb.w[0], 0u, dsel)));
+    const float2 dd = make_float2(d, d);
+    if constexpr (BMODE == B_Q4) {
+        const float2 off = make_float2(-8388616.0f, -8388616.0f);
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const uint32_t q = prmt(rb.w[m], rb.w[m + 1], sel);
+            lo[m] = q & 0x0F0F0F0Fu;
+            hi[m] = (q >> 4) & 0x0F0F0F0Fu;
+        }
+        // chunk 0: lo of qs[0..7], chunk 1: lo of qs[8..15], chunk 2/3: hi of the same
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t* src = (j < 2) ? lo : hi;
+            const int w0 = (j & 1) * 2;
+            uint32_t o[4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t v = src[w0 + h];
+                const float2 a = __fmul2_rn(__fadd2_rn(make_float2(MAGIC_F(v, 0), MAGIC_F(v, 1)), off), dd);
+                const float2 b = __fmul2_rn(__fadd2_rn(make_float2(MAGIC_F(v, 2), MAGIC_F(v, 3)), off), dd);
+                o[2 * h] = pack2<T>(a.x, a.y);
+                o[2 * h + 1] = pack2<T>(b.x, b.y);
+            }
+            *dst[j] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    } else {
+        const float2 off = make_float2(-8388736.0f, -8388736.0f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t o[4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int m = 2 * j + h;
+                const uint32_t v = prmt(rb.w[m], rb.w[m + 1], sel) ^ 0x80808080u;
+                const float2 a = __fmul2_rn(__fadd2_rn(make_float2(MAGIC_F(v, 0), MAGIC_F(v, 1)), off), dd);
+                const float2 b = __fmul2_rn(__fadd2_rn(make_float2(MAGIC_F(v, 2), MAGIC_F(v, 3)), off), dd);
+                o[2 * h] = pack2<T>(a.x, a.y);
+                o[2 * h + 1] = pack2<T>(b.x, b.y);
+            }
+            *dst[j] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
+template <int BN, int BMODE, typename T>
+__global__ void __launch_bounds__(gemm_threads(BMODE), 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
+    constexpr int S = num_stages(BN);
+    constexpr int SB = stage_bytes(BN);
+    constexpr uint32_t kTmemCols = 2 * BN;
+    constexpr bool kQuant = BMODE >= B_Q8;
+    constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+    constexpr uint32_t kIdesc = idesc_f16(kBf16, false, BMODE == B_TMA_MN, BM, BN);
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t full_bar[S];
+    __shared__ __align__(8) uint64_t empty_bar[S];
+    __shared__ __align__(8) uint64_t tfull_bar[2];
+    __shared__ __align__(8) uint64_t tempty_bar[2];
+    __shared__ __align__(8) uint64_t drain_bar;
+    __shared__ uint32_t tmem_base_slot;
+    __shared__ volatile int abort_flag;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int total_tiles = g.tiles_m * g.tiles_n;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full_bar[s], 1 + (kQuant ? kDqWarps : 0));
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull_bar[a], 1);
+            mbar_init(&tempty_bar[a], 4);
+        }
+        mbar_init(&drain_bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tensormap(&tmA);
+        if (!kQuant) prefetch_tensormap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < total_tiles && !abort_flag; tile += gridDim.x) {
+                const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
+                for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
+                    const uint32_t s = it % S, ph = (it / S) & 1u;
+                    if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
+                    uint8_t* a_dst = smem + s * SB;
+                    uint8_t* b_dst = a_dst + kABytes;
+                    const uint32_t tx = kABytes + (kQuant ? 0u : (uint32_t)(BN * BK * 2));
+                    mbar_arrive_expect_tx(&full_bar[s], tx);
+                    tma_load_2d(a_dst, &tmA, kb * BK, m_blk * BM, &full_bar[s]);
+                    if constexpr (BMODE == B_TMA_K) {
+                        tma_load_2d(b_dst, &tmB, kb * BK, n_blk * BN, &full_bar[s]);
+                    } else if constexpr (BMODE == B_TMA_MN) {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_2d(b_dst + j * 8192, &tmB, n_blk * BN + j * 64, kb * BK, &full_bar[s]);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            uint32_t it = 0, tcount = 0;
+            bool issued = false;
+            for (int tile = blockIdx.x; tile < total_tiles && !abort_flag; tile += gridDim.x, ++tcount) {
+                const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
+                if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, g.status)) { abort_flag = 1; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
+                    const uint32_t s = it % S, ph = (it / S) & 1u;
+                    if (!mbar_wait(&full_bar[s], ph, g.status)) { abort_flag = 1; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + s * SB);
+                    const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        const uint64_t adesc = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
+                        uint64_t bdesc;
+                        if constexpr (BMODE == B_TMA_MN)
+                            bdesc = smem_desc(b_addr + k * 2048, 8192, 1024, kSwizzle128B);
+                        else
+                            bdesc = smem_desc(b_addr + k * 32, 16, 1024, kSwizzle128B);
+                        umma_f16(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    issued = true;
+                    umma_commit(&empty_bar[s]);
+                }
+                if (abort_flag) break;
+                umma_commit(&tfull_bar[acc]);
+            }
+            if (issued) {
+                // All MMAs retire before TMEM is released.
+                umma_commit(&drain_bar);
+                mbar_wait(&drain_bar, 0, g.status);
+            }
+        }
+    } else if (warp < 6) {
+        // ---------------------------------------------------------------- epilogue
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        uint32_t tcount = 0;
+        const bool vec_ok = (g.ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0);
+        for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tcount) {
+            const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
+            const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
+            if (abort_flag || !mbar_wait(&tfull_bar[acc], acc_ph, g.status)) { abort_flag = 1; break; }
+            tc_fence_after();
+            const int row = m_blk * BM + q * 32 + lane;
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 32; ++cc) {
+                float v[32];
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cc * 32, v);
+                const int n0 = n_blk * BN + cc * 32;
+                if (g.bias) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (n0 + i < g.N) v[i] += bias_at(g.bias, g.bias_type, n0 + i);
+                }
+                if (row < g.M && n0 < g.N) {
+                    const size_t base = (size_t)row * g.ldc + n0;
+                    if (vec_ok && n0 + 32 <= g.N && g.c_type != MGPU_F32) {
+                        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(g.C) + base);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            uint32_t o[4];
+#pragma unroll
+                            for (int h = 0; h < 4; ++h)
+                                o[h] = (g.c_type == MGPU_BF16) ? pack2<__nv_bfloat16>(v[8 * j + 2 * h], v[8 * j + 2 * h + 1])
+                                                               : pack2<__half>(v[8 * j + 2 * h], v[8 * j + 2 * h + 1]);
+                            dst[j] = make_uint4(o[0], o[1], o[2], o[3]);
+                        }
+                    } else if (vec_ok && n0 + 32 <= g.N) {
+                        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(g.C) + base);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (n0 + i < g.N) store_out(g.C, g.c_type, base + i, v[i]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        }
+    } else if constexpr (kQuant) {
+        // ---------------------------------------------------------------- dequantisers
+        constexpr int BB = (BMODE == B_Q4) ? 18 : 34;
+        constexpr int NW = (BMODE == B_Q4) ? 5 : 9;
+        constexpr int UPT = (2 * BN) / (kDqWarps * 32);  // blocks (units) per thread per stage
+        const int dt = tid - 192;
+        const int nbk = (g.K + 31) / 32;  // blocks per row
+        RawBlock<NW> raw[UPT];
+        uint32_t it = 0;
+        // prefetch helper: units u = dt + 256 v -> row u >> 1 of the tile, k-block 2 kb + (u & 1)
+        auto load_stage = [&](int tile, int kb) {
+            const int n_blk = tile / g.tiles_m;
+#pragma unroll
+            for (int v = 0; v < UPT; ++v) {
+                const int u = dt + v * kDqWarps * 32;
+                const int n = n_blk * BN + (u >> 1);
+                const int kq = kb * 2 + (u & 1);
+                const bool ok = n < g.N && kq < nbk;
+                load_block<NW, BB>(raw[v], g.Bq + (size_t)n * g.bq_row_bytes + (size_t)kq * BB, g.bq_end, ok);
+            }
+        };
+        int tile = blockIdx.x, kb = 0;
+        if (tile < total_tiles) load_stage(tile, 0);
+        while (tile < total_tiles && !abort_flag) {
+            const uint32_t s = it % S, ph = (it / S) & 1u;
+            RawBlock<NW> cur[UPT];
+#pragma unroll
+            for (int v = 0; v < UPT; ++v) cur[v] = raw[v];
+            // advance and prefetch the next stage's blocks before waiting for this slot
+            int ntile = tile, nkb = kb + 1;
+            if (nkb == g.num_kb) { nkb = 0; ntile += gridDim.x; }
+            if (ntile < total_tiles) load_stage(ntile, nkb);
+            if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
+            uint8_t* b_dst = smem + s * SB + kABytes;
+#pragma unroll
+            for (int v = 0; v < UPT; ++v) {
+                const int u = dt + v * kDqWarps * 32;
+                const int r = u >> 1, half = u & 1;
+                uint8_t* row_base = b_dst + (r >> 3) * 1024 + (r & 7) * 128;
+                uint4* dst[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dst[j] = reinterpret_cast<uint4*>(row_base + (((half * 4 + j) ^ (r & 7)) << 4));
+                decode_store<BMODE, T, NW>(cur[v], dst);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_bar[s]);
+            tile = ntile;
+            kb = nkb;
+            ++it;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ host side --------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D map over a 16-bit row-major matrix: inner dim `cols` (contiguous), outer `rows`,
+// row pitch `ld` elements, box {box_cols, box_rows}, 128B swizzle.
+bool make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int BMODE, typename T>
+cudaError_t launch_gemm(const mgpu_k::LaunchCtx& c, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g) {
+    auto kern = gemm_tc_kernel<BN, BMODE, T>;
+    const int smem = num_stages(BN) * stage_bytes(BN) + 1024;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    const int tiles = g.tiles_m * g.tiles_n;
+    const int grid = tiles < c.sm_count ? tiles : c.sm_count;
+    kern<<<grid, gemm_threads(BMODE), smem, c.stream>>>(ma, mb, g);
+    return cudaGetLastError();
+}
+
+template <int BN, typename T>
+cudaError_t launch_mode(const mgpu_k::LaunchCtx& c, int bmode, const CUtensorMap& ma, const CUtensorMap& mb,
+                        const GemmArgs& g) {
+    switch (bmode) {
+        case B_TMA_K: return launch_gemm<BN, B_TMA_K, T>(c, ma, mb, g);
+        case B_TMA_MN: return launch_gemm<BN, B_TMA_MN, T>(c, ma, mb, g);
+        case B_Q8: return launch_gemm<BN, B_Q8, T>(c, ma, mb, g);
+        default: return launch_gemm<BN, B_Q4, T>(c, ma, mb, g);
+    }
+}
+
+bool is16(int t) { return t == MGPU_F16 || t == MGPU_BF16; }
+
+}  // namespace
+
+namespace mgpu_k {
+
+const char* gemm_check(const GemmOperand& A, const GemmOperand& B, const GemmOperand& C, int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0) return "M, N, K must be positive";
+    if (!is16(A.type)) return "A must be fp16 or bf16";
+    if (!(is16(C.type) || C.type == MGPU_F32)) return "C must be fp16, bf16 or fp32";
+    if (C.ld < N) return "C row pitch smaller than N";
+    if ((reinterpret_cast<uintptr_t>(A.ptr) & 15) || (A.ld * 2) % 16) return "A must be 16-byte aligned with a row pitch that is a multiple of 8 elements";
+    if (A.ld < K) return "A row pitch smaller than K";
+    if (B.type == MGPU_Q4_0 || B.type == MGPU_Q8_0) {
+        if (B.layout != MGPU_LAYOUT_NK) return "quantised B must be in GGUF [N][K/32] layout";
+        if (K % 32) return "quantised B needs K % 32 == 0";
+        if (B.ld & 1) return "quantised row bytes must be even";
+        return nullptr;
+    }
+    if (B.type != A.type) return "A and B must have the same 16-bit type";
+    if ((reinterpret_cast<uintptr_t>(B.ptr) & 15) || (B.ld * 2) % 16) return "B must be 16-byte aligned with a row pitch that is a multiple of 8 elements";
+    if (B.layout == MGPU_LAYOUT_NK && B.ld < K) return "B row pitch smaller than K";
+    if (B.layout == MGPU_LAYOUT_KN && B.ld < N) return "B row pitch smaller than N";
+    if (!get_encode_fn()) return "cuTensorMapEncodeTiled unavailable";
+    return nullptr;
+}
+
+cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
+                 const void* bias, int bias_type, int M, int N, int K) {
+    if (gemm_check(A, B, C, M, N, K)) return cudaErrorInvalidValue;
+    int bmode;
+    if (B.type == MGPU_Q8_0) bmode = B_Q8;
+    else if (B.type == MGPU_Q4_0) bmode = B_Q4;
+    else bmode = (B.layout == MGPU_LAYOUT_NK) ? B_TMA_K : B_TMA_MN;
+
+    // Pick BN by the estimated makespan over the SMs (tile time ~ BN + fixed overhead).
+    const int tiles_m = (M + BM - 1) / BM;
+    auto makespan = [&](int bn) {
+        const long tiles = (long)tiles_m * ((N + bn - 1) / bn);
+        const long waves = (tiles + c.sm_count - 1) / c.sm_count;
+        return waves * (bn + 32);
+    };
+    const int BN = makespan(128) < makespan(256) ? 128 : 256;
+
+    GemmArgs g;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.num_kb = (K + BK - 1) / BK;
+    g.tiles_m = tiles_m;
+    g.tiles_n = (N + BN - 1) / BN;
+    g.C = const_cast<void*>(C.ptr);
+    g.ldc = C.ld;
+    g.c_type = C.type;
+    g.bias = bias;
+    g.bias_type = bias_type;
+    g.Bq = nullptr;
+    g.bq_row_bytes = 0;
+    g.bq_end = nullptr;
+    g.status = c.status;
+
+    CUtensorMap ma, mb;
+    memset(&mb, 0, sizeof(mb));
+    if (!make_map(&ma, A.ptr, M, K, A.ld, BK, BM)) return cudaErrorInvalidValue;
+    if (bmode == B_TMA_K) {
+        if (!make_map(&mb, B.ptr, N, K, B.ld, BK, BN)) return cudaErrorInvalidValue;
+    } else if (bmode == B_TMA_MN) {
+        if (!make_map(&mb, B.ptr, K, N, B.ld, 64, BK)) return cudaErrorInvalidValue;
+    } else {
+        g.Bq = reinterpret_cast<const uint8_t*>(B.ptr);
+        g.bq_row_bytes = B.ld;
+        g.bq_end = g.Bq + (size_t)N * B.ld;
+    }
+    const bool bf16 = A.type == MGPU_BF16;
+    if (BN == 256)
+        return bf16 ? launch_mode<256, __nv_bfloat16>(c, bmode, ma, mb, g) : launch_mode<256, __half>(c, bmode, ma, mb, g);
+    return bf16 ? launch_mode<128, __nv_bfloat16>(c, bmode, ma, mb, g) : launch_mode<128, __half>(c, bmode, ma, mb, g);
+}
+
+}  // namespace mgpu_k

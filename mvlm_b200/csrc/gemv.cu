@@ -1,0 +1,549 @@
+// gemv.cu - decode-phase GEMV kernels for sm_100a (replaces gemv, src/kernels/gemm.cl:219-270).
+//
+// gemv_q_stream: y = dequant(W) . x for GGUF Q4_0 / Q8_0 weights kept packed in their
+//   [N][K/32] block layout.  Each CTA owns an even share of the rows.  One producer thread
+//   streams the CTA's contiguous byte range from HBM into a 4-stage shared-memory ring with
+//   cp.async.bulk (the 1-D TMA engine, 16-byte granular, no registers held in flight); 8
+//   consumer warps decode the 18 / 34-byte blocks out of shared memory.  Each consumer thread
+//   owns one 32-element block column for the whole launch, so its 32 activations stay in
+//   registers; weights are turned into exact fp32 (q-8 or q) with one PRMT per element
+//   (2^23 + q bit pattern) and one packed FADD2, and accumulated with packed FFMA2.  Row sums
+//   are reduced across lanes with a transposing shuffle butterfly.
+// gemv_nk: dense [N][K] rows (GGUF F32/F16/BF16 tensors): warp per row group, 16-byte loads.
+// gemv_kn: dense [K][N] (the reference kernels' orientation): columns across lanes, K split
+//   across CTAs; fp32 partials go to scratch and the last CTA of each column tile sums them
+//   in split order, so the result is deterministic.
+// gemv_q_generic: any K that is a multiple of 32 (row starts need not be 16-byte aligned).
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace mgpu_dev;
+
+namespace {
+
+constexpr int kConsumerThreads = 256;
+constexpr int kGemvThreads = kConsumerThreads + 32;
+constexpr int kGemvStages = 4;
+constexpr uint32_t kGemvSmemBudget = 200 * 1024;
+
+template <int QT> struct QTraits;
+template <> struct QTraits<MGPU_Q4_0> {
+    static constexpr int kBlockBytes = 18;
+    static constexpr int kWords = 5;  // 20 aligned bytes cover an 18-byte block at offset 0 or 2
+};
+template <> struct QTraits<MGPU_Q8_0> {
+    static constexpr int kBlockBytes = 34;
+    static constexpr int kWords = 9;
+};
+
+// 2^23 + b as an fp32 bit pattern for byte `b` (0..255) of `v`: exact, one PRMT.
+#define MAGIC_F(v, byte_sel) __uint_as_float(prmt((v), 0x4B000000u, 0x7540u | (byte_sel)))
+
+// Dot product of one Q4_0 block with 32 activations (pairs xp[0..15]).  w holds the 20
+// aligned bytes that contain the block; `sel` realigns the 16 quant bytes, `dsel` extracts
+// the fp16 scale.  Elements 0..15 are the low nibbles of qs[0..15], 16..31 the high ones.
+__device__ __forceinline__ float q4_0_block_dot(const uint32_t (&w)[5], uint32_t sel, uint32_t dsel,
+                                                const float2 (&xp)[16]) {
+    const float d = __half2float(__ushort_as_half((unsigned short)prmt(w[0], 0u, dsel)));
+    const float2 off = make_float2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
+    float2 s = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const uint32_t q = prmt(w[m], w[m + 1], sel);
+        const uint32_t lo = q & 0x0F0F0F0Fu;
+        const uint32_t hi = (q >> 4) & 0x0F0F0F0Fu;
+        s = __ffma2_rn(xp[2 * m], __fadd2_rn(make_float2(MAGIC_F(lo, 0), MAGIC_F(lo, 1)), off), s);
+        s = __ffma2_rn(xp[2 * m + 1], __fadd2_rn(make_float2(MAGIC_F(lo, 2), MAGIC_F(lo, 3)), off), s);
+        s = __ffma2_rn(xp[8 + 2 * m], __fadd2_rn(make_float2(MAGIC_F(hi, 0), MAGIC_F(hi, 1)), off), s);
+        s = __ffma2_rn(xp[9 + 2 * m], __fadd2_rn(make_float2(MAGIC_F(hi, 2), MAGIC_F(hi, 3)), off), s);
+    }
+    return d * (s.x + s.y);
+}
+
+// Same for Q8_0: 32 signed bytes; q ^ 0x80 = q + 128 is placed in the mantissa, then
+// -(2^23 + 128) restores q exactly.
+__device__ __forceinline__ float q8_0_block_dot(const uint32_t (&w)[9], uint32_t sel, uint32_t dsel,
+                                                const float2 (&xp)[16]) {
+    const float d = __half2float(__ushort_as_half((unsigned short)prmt(w[0], 0u, dsel)));
+    const float2 off = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+    float2 s = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        const uint32_t q = prmt(w[m], w[m + 1], sel) ^ 0x80808080u;
+        s = __ffma2_rn(xp[2 * m], __fadd2_rn(make_float2(MAGIC_F(q, 0), MAGIC_F(q, 1)), off), s);
+        s = __ffma2_rn(xp[2 * m + 1], __fadd2_rn(make_float2(MAGIC_F(q, 2), MAGIC_F(q, 3)), off), s);
+    }
+    return d * (s.x + s.y);
+}
+
+template <int QT, int NW>
+__device__ __forceinline__ float q_block_dot(const uint32_t (&w)[NW], uint32_t sel, uint32_t dsel,
+                                             const float2 (&xp)[16]) {
+    if constexpr (QT == MGPU_Q4_0) return q4_0_block_dot(w, sel, dsel, xp);
+    else return q8_0_block_dot(w, sel, dsel, xp);
+}
+
+// Load 32 activations starting at element `k0` as fp32 pairs.
+template <typename XT>
+__device__ __forceinline__ void load_x32(const XT* __restrict__ x, int k0, float2 (&xp)[16]) {
+    if constexpr (sizeof(XT) == 4) {
+        const float4* p = reinterpret_cast<const float4*>(x + k0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float4 v = __ldg(p + i);
+            xp[2 * i] = make_float2(v.x, v.y);
+            xp[2 * i + 1] = make_float2(v.z, v.w);
+        }
+    } else {
+        const uint4* p = reinterpret_cast<const uint4*>(x + k0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint4 v = __ldg(p + i);
+            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                XT lo, hi;
+                uint16_t l16 = (uint16_t)(u[j] & 0xFFFF), h16 = (uint16_t)(u[j] >> 16);
+                memcpy(&lo, &l16, 2);
+                memcpy(&hi, &h16, 2);
+                xp[4 * i + j] = make_float2(to_f32<XT>(lo), to_f32<XT>(hi));
+            }
+        }
+    }
+}
+
+// Transposing butterfly: v[0..R) per lane in, the 32-lane sum of row `row` out, where lanes
+// with lane % (32 / R) == 0 hold distinct rows.
+template <int R>
+__device__ __forceinline__ float warp_reduce_rows(float (&v)[R], int lane, int& row) {
+    constexpr int LOG = (R == 1) ? 0 : (R == 2) ? 1 : (R == 4) ? 2 : 3;
+    row = 0;
+#pragma unroll
+    for (int step = 0; step < LOG; ++step) {
+        const int h = R >> (step + 1);
+        const int off = 16 >> step;
+        const bool up = (lane & off) != 0;
+#pragma unroll
+        for (int k = 0; k < (R >> 1); ++k) {
+            if (k < h) {
+                const float send = up ? v[k] : v[k + h];
+                const float keep = up ? v[k + h] : v[k];
+                v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+        }
+        if (up) row += h;
+    }
+#pragma unroll
+    for (int off = 16 >> LOG; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    return v[0];
+}
+
+struct GemvQArgs {
+    const uint8_t* W;
+    const void* x;
+    void* y;
+    int N;
+    int nb;             // blocks per row (K / 32); 32 <= nb <= 256, nb % 32 == 0
+    uint32_t row_bytes; // nb * block bytes, a multiple of 16
+    uint32_t stage_stride;
+    int* status;
+};
+
+template <int QT, int RPT, typename XT, typename YT>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_q_stream(GemvQArgs a) {
+    constexpr int BB = QTraits<QT>::kBlockBytes;
+    constexpr int NW = QTraits<QT>::kWords;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full_bar[kGemvStages];
+    __shared__ __align__(8) uint64_t empty_bar[kGemvStages];
+    __shared__ float wsum[2][8][RPT];
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nb = a.nb;
+    const int RP = kConsumerThreads / nb;  // rows decoded per step
+    const int TR = RP * RPT;               // rows per chunk
+    const int G = gridDim.x;
+    const int r0 = (int)((long long)a.N * blockIdx.x / G);
+    const int r1 = (int)((long long)a.N * (blockIdx.x + 1) / G);
+    const int nchunks = (r1 - r0 + TR - 1) / TR;
+
+    if (tid == 0) {
+        for (int s = 0; s < kGemvStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], kConsumerThreads / 32);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerThreads / 32) {
+        // ---- producer: stream this CTA's rows chunk by chunk ----
+        if (lane == 0) {
+            int c = 0;
+            for (; c < nchunks; ++c) {
+                const int s = c % kGemvStages;
+                const uint32_t ph = (uint32_t)(c / kGemvStages) & 1u;
+                if (!mbar_wait(&empty_bar[s], ph ^ 1u, a.status)) break;
+                const int row = r0 + c * TR;
+                const uint32_t bytes = (uint32_t)min(TR, r1 - row) * a.row_bytes;
+                mbar_arrive_expect_tx(&full_bar[s], bytes);
+                bulk_g2s(smem + (size_t)s * a.stage_stride, a.W + (size_t)row * a.row_bytes, bytes, &full_bar[s]);
+            }
+            if (c < nchunks) {
+                // Timed out: let the copies already issued land before the CTA exits.
+                for (int k = max(0, c - kGemvStages); k < c; ++k)
+                    mbar_wait(&full_bar[k % kGemvStages], (uint32_t)(k / kGemvStages) & 1u, nullptr);
+            }
+        }
+        return;
+    }
+
+    // ---- consumers ----
+    const int col = tid % nb;  // block column owned by this thread for the whole launch
+    float2 xp[16];
+    load_x32<XT>(reinterpret_cast<const XT*>(a.x), col * 32, xp);
+    const uint32_t par = (uint32_t)(tid * BB) & 3u;  // block starts at byte 0 or 2 of a word
+    const uint32_t sel = par ? 0x7654u : 0x5432u;
+    const uint32_t dsel = par ? 0x4432u : 0x4410u;
+    const uint32_t toff = (uint32_t)(tid * BB) - par;
+    const int wpr = nb >> 5;  // warps per row slot
+    YT* __restrict__ y = reinterpret_cast<YT*>(a.y);
+
+    for (int c = 0; c < nchunks; ++c) {
+        const int s = c % kGemvStages;
+        const uint32_t ph = (uint32_t)(c / kGemvStages) & 1u;
+        if (!mbar_wait(&full_bar[s], ph, a.status)) return;
+        const uint8_t* st = smem + (size_t)s * a.stage_stride + toff;
+        float acc[RPT];
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) {
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(st + i * (kConsumerThreads * BB));
+            uint32_t w[NW];
+#pragma unroll
+            for (int q = 0; q < NW; ++q) w[q] = wp[q];
+            acc[i] = q_block_dot<QT, NW>(w, sel, dsel, xp);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[s]);
+
+        int ri;
+        const float v = warp_reduce_rows<RPT>(acc, lane, ri);
+        if ((lane & ((32 / RPT) - 1)) == 0) wsum[c & 1][warp][ri] = v;
+        named_barrier_sync(1, kConsumerThreads);
+        if (tid < TR) {
+            const int slot = tid % RP, i = tid / RP;
+            float sum = 0.0f;
+            for (int w = slot * wpr; w < (slot + 1) * wpr; ++w) sum += wsum[c & 1][w][i];
+            const int row = r0 + c * TR + tid;
+            if (row < r1) y[row] = from_f32<YT>(sum);
+        }
+    }
+}
+
+// Fallback for rows that are not 16-byte aligned or K outside [1024, 8192]: one warp per
+// row, byte loads.
+template <int QT, typename XT, typename YT>
+__global__ void __launch_bounds__(256) gemv_q_generic(const uint8_t* __restrict__ W, const XT* __restrict__ x,
+                                                      YT* __restrict__ y, int N, int nb, size_t row_bytes) {
+    constexpr int BB = QTraits<QT>::kBlockBytes;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= N) return;
+    const uint8_t* row = W + (size_t)warp * row_bytes;
+    float acc = 0.0f;
+    for (int b = lane; b < nb; b += 32) {
+        const uint8_t* p = row + (size_t)b * BB;
+        const float d = __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+        float s = 0.0f;
+        if constexpr (QT == MGPU_Q4_0) {
+            for (int j = 0; j < 16; ++j) {
+                const uint8_t q = p[2 + j];
+                s = fmaf(to_f32<XT>(x[b * 32 + j]), (float)((int)(q & 0xF) - 8), s);
+                s = fmaf(to_f32<XT>(x[b * 32 + j + 16]), (float)((int)(q >> 4) - 8), s);
+            }
+        } else {
+            for (int j = 0; j < 32; ++j) s = fmaf(to_f32<XT>(x[b * 32 + j]), (float)(int8_t)p[2 + j], s);
+        }
+        acc = fmaf(d, s, acc);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) y[warp] = from_f32<YT>(acc);
+}
+
+// ------------------------------------------------------------------ dense NK ---------
+// Warp per ROWS rows; each lane streams 16-byte chunks along K.  K % (16 / sizeof(WT)) == 0
+// and 16-byte aligned rows, otherwise scalar.
+template <typename WT, typename XT, typename YT, int ROWS>
+__global__ void __launch_bounds__(256) gemv_nk_dense(const WT* __restrict__ W, int64_t ldw,
+                                                     const XT* __restrict__ x, YT* __restrict__ y, int N,
+                                                     int K, int vec) {
+    constexpr int EPV = 16 / sizeof(WT);  // elements per 16-byte vector
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int row0 = warp * ROWS;
+    if (row0 >= N) return;
+    float acc[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
+    if (vec) {
+        const int nvec = K / EPV;
+        for (int v = lane; v < nvec; v += 32) {
+            float xv[EPV];
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) xv[e] = to_f32<XT>(x[v * EPV + e]);
+            uint4 wv[ROWS];
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+                wv[r] = (row0 + r < N) ? __ldg(reinterpret_cast<const uint4*>(W + (size_t)(row0 + r) * ldw) + v)
+                                       : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) {
+                const WT* we = reinterpret_cast<const WT*>(&wv[r]);
+#pragma unroll
+                for (int e = 0; e < EPV; ++e) acc[r] = fmaf(xv[e], to_f32<WT>(we[e]), acc[r]);
+            }
+        }
+    } else {
+        for (int k = lane; k < K; k += 32) {
+            const float xv = to_f32<XT>(x[k]);
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r)
+                if (row0 + r < N) acc[r] = fmaf(xv, to_f32<WT>(W[(size_t)(row0 + r) * ldw + k]), acc[r]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+            if (row0 + r < N) y[row0 + r] = from_f32<YT>(acc[r]);
+    }
+}
+
+// ------------------------------------------------------------------ dense KN ---------
+// CTA = 256 threads over a tile of 256 columns x kchunk rows of K; thread handles COLS
+// consecutive columns of kchunk/8 rows.  Partials of split s go to partials[s][N]; the last
+// CTA of a column tile (atomic ticket) sums splits 0..S-1 in order and resets the ticket.
+constexpr int kKnCols = 256;
+template <typename WT, typename XT, typename YT>
+__global__ void __launch_bounds__(256) gemv_kn_split(const WT* __restrict__ W, int64_t ldw,
+                                                     const XT* __restrict__ x, YT* __restrict__ y, int N,
+                                                     int K, int kchunk, float* __restrict__ partials,
+                                                     unsigned int* __restrict__ counters) {
+    constexpr int CPT = 8;  // columns per thread (contiguous)
+    __shared__ float red[8][kKnCols];
+    __shared__ unsigned int ticket;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int col_tile = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
+    const int n0 = col_tile * kKnCols + lane * CPT;
+    const int k_begin = split * kchunk;
+    const int k_end = min(K, k_begin + kchunk);
+    float acc[CPT];
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) acc[i] = 0.0f;
+    const bool full_vec = (n0 + CPT <= N) && ((ldw * sizeof(WT)) % 16 == 0) &&
+                          ((reinterpret_cast<uintptr_t>(W) & 15) == 0);
+    for (int k = k_begin + warp; k < k_end; k += 8) {
+        const float xv = to_f32<XT>(x[k]);
+        const WT* wr = W + (size_t)k * ldw + n0;
+        if (full_vec) {
+            WT wv[CPT];
+#pragma unroll
+            for (int v = 0; v < (int)(CPT * sizeof(WT) / 16); ++v)
+                reinterpret_cast<uint4*>(wv)[v] = __ldg(reinterpret_cast<const uint4*>(wr) + v);
+#pragma unroll
+            for (int i = 0; i < CPT; ++i) acc[i] = fmaf(xv, to_f32<WT>(wv[i]), acc[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < CPT; ++i)
+                if (n0 + i < N) acc[i] = fmaf(xv, to_f32<WT>(wr[i]), acc[i]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) red[warp][lane * CPT + i] = acc[i];
+    __syncthreads();
+    {
+        const int n = col_tile * kKnCols + tid;
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) s += red[w][tid];
+        if (n < N) partials[(size_t)split * N + n] = s;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) ticket = atomicAdd(&counters[col_tile], 1u);
+    __syncthreads();
+    if (ticket != (unsigned)(splits - 1)) return;
+    __threadfence();
+    const int n = col_tile * kKnCols + tid;
+    if (n < N) {
+        float s = 0.0f;
+        for (int sp = 0; sp < splits; ++sp) s += __ldcg(partials + (size_t)sp * N + n);
+        y[n] = from_f32<YT>(s);
+    }
+    if (tid == 0) counters[col_tile] = 0u;
+}
+
+// ------------------------------------------------------------------ dispatch helpers --
+template <template <typename, typename> class F, typename... Args>
+cudaError_t dispatch_xy(int xtype, int ytype, Args&&... args) {
+#define MGPU_Y(XT)                                                                          \
+    switch (ytype) {                                                                        \
+        case MGPU_F32: return F<XT, float>::run(args...);                                  \
+        case MGPU_F16: return F<XT, __half>::run(args...);                                 \
+        case MGPU_BF16: return F<XT, __nv_bfloat16>::run(args...);                         \
+        default: return cudaErrorInvalidValue;                                             \
+    }
+    switch (xtype) {
+        case MGPU_F32: MGPU_Y(float)
+        case MGPU_F16: MGPU_Y(__half)
+        case MGPU_BF16: MGPU_Y(__nv_bfloat16)
+        default: return cudaErrorInvalidValue;
+    }
+#undef MGPU_Y
+}
+
+template <int QT>
+struct GemvQLaunch {
+    template <typename XT, typename YT>
+    struct F {
+        static cudaError_t run(const mgpu_k::LaunchCtx& c, const uint8_t* W, const void* x, void* y, int N,
+                               int K) {
+            constexpr int BB = QTraits<QT>::kBlockBytes;
+            const int nb = K / 32;
+            const size_t row_bytes = (size_t)nb * BB;
+            const bool fast = (nb % 32 == 0) && nb <= 256 && (row_bytes % 16 == 0) &&
+                              ((reinterpret_cast<uintptr_t>(W) & 15) == 0) &&
+                              ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+            if (!fast) {
+                const int blocks = (N * 32 + 255) / 256;
+                gemv_q_generic<QT, XT, YT><<<blocks, 256, 0, c.stream>>>(W, (const XT*)x, (YT*)y, N, nb, row_bytes);
+                return cudaGetLastError();
+            }
+            const int RP = kConsumerThreads / nb;
+            const int G = max(1, min(c.sm_count, (N + RP - 1) / RP));
+            const int rows_per_cta = (N + G - 1) / G;
+            // Largest rows-per-thread (8,4,2,1) whose chunk fits the CTA's share and the ring.
+            int rpt = 8;
+            while (rpt > 1 && (RP * rpt > rows_per_cta ||
+                               (size_t)kGemvStages * RP * rpt * row_bytes > kGemvSmemBudget))
+                rpt >>= 1;
+            GemvQArgs a;
+            a.W = W;
+            a.x = x;
+            a.y = y;
+            a.N = N;
+            a.nb = nb;
+            a.row_bytes = (uint32_t)row_bytes;
+            a.stage_stride = (uint32_t)((RP * rpt * row_bytes + 1023) / 1024 * 1024);
+            a.status = c.status;
+            const size_t smem = (size_t)kGemvStages * a.stage_stride;
+            switch (rpt) {
+                case 8: return launch<8, XT, YT>(c, a, G, smem);
+                case 4: return launch<4, XT, YT>(c, a, G, smem);
+                case 2: return launch<2, XT, YT>(c, a, G, smem);
+                default: return launch<1, XT, YT>(c, a, G, smem);
+            }
+        }
+        template <int RPT, typename XT2, typename YT2>
+        static cudaError_t launch(const mgpu_k::LaunchCtx& c, const GemvQArgs& a, int G, size_t smem) {
+            auto kern = gemv_q_stream<QT, RPT, XT2, YT2>;
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            kern<<<G, kGemvThreads, smem, c.stream>>>(a);
+            return cudaGetLastError();
+        }
+    };
+};
+
+template <typename WT>
+struct GemvNkLaunch {
+    template <typename XT, typename YT>
+    struct F {
+        static cudaError_t run(const mgpu_k::LaunchCtx& c, const void* W, int64_t ldw, const void* x, void* y,
+                               int N, int K) {
+            constexpr int ROWS = 4;
+            constexpr int EPV = 16 / sizeof(WT);
+            const int vec = (K % EPV == 0) && ((ldw * (int64_t)sizeof(WT)) % 16 == 0) &&
+                            ((reinterpret_cast<uintptr_t>(W) & 15) == 0);
+            const int warps = (N + ROWS - 1) / ROWS;
+            const int blocks = (warps * 32 + 255) / 256;
+            gemv_nk_dense<WT, XT, YT, ROWS><<<blocks, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x,
+                                                                         (YT*)y, N, K, vec);
+            return cudaGetLastError();
+        }
+    };
+};
+
+template <typename WT>
+struct GemvKnLaunch {
+    template <typename XT, typename YT>
+    struct F {
+        static cudaError_t run(const mgpu_k::LaunchCtx& c, const void* W, int64_t ldw, const void* x, void* y,
+                               int N, int K, float* partials, unsigned int* counters) {
+            int splits = 1;
+            mgpu_k::gemv_kn_scratch_bytes(N, K, c.sm_count, &splits);
+            const int kchunk = (K + splits - 1) / splits;
+            dim3 grid((N + kKnCols - 1) / kKnCols, splits);
+            gemv_kn_split<WT, XT, YT><<<grid, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x, (YT*)y, N, K,
+                                                                 kchunk, partials, counters);
+            return cudaGetLastError();
+        }
+    };
+};
+
+}  // namespace
+
+namespace mgpu_k {
+
+cudaError_t gemv_q(const LaunchCtx& c, int qtype, const uint8_t* W, int xtype, const void* x, int ytype,
+                   void* y, int N, int K) {
+    if (N <= 0) return cudaSuccess;
+    if (qtype == MGPU_Q4_0)
+        return dispatch_xy<GemvQLaunch<MGPU_Q4_0>::F>(xtype, ytype, c, W, x, y, N, K);
+    if (qtype == MGPU_Q8_0)
+        return dispatch_xy<GemvQLaunch<MGPU_Q8_0>::F>(xtype, ytype, c, W, x, y, N, K);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t gemv_nk(const LaunchCtx& c, int wtype, const void* W, int64_t ldw, int xtype, const void* x,
+                    int ytype, void* y, int N, int K) {
+    if (N <= 0) return cudaSuccess;
+    switch (wtype) {
+        case MGPU_F32: return dispatch_xy<GemvNkLaunch<float>::F>(xtype, ytype, c, W, ldw, x, y, N, K);
+        case MGPU_F16: return dispatch_xy<GemvNkLaunch<__half>::F>(xtype, ytype, c, W, ldw, x, y, N, K);
+        case MGPU_BF16: return dispatch_xy<GemvNkLaunch<__nv_bfloat16>::F>(xtype, ytype, c, W, ldw, x, y, N, K);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+size_t gemv_kn_scratch_bytes(int N, int K, int sm_count, int* splits_out) {
+    // Enough CTAs for ~4 per SM, each with at least 64 rows of K.
+    const int col_tiles = (N + kKnCols - 1) / kKnCols;
+    int splits = (4 * sm_count + col_tiles - 1) / col_tiles;
+    splits = max(1, min(splits, (K + 63) / 64));
+    if (splits_out) *splits_out = splits;
+    return (size_t)col_tiles * sizeof(unsigned int) + (size_t)splits * N * sizeof(float) + 256;
+}
+
+cudaError_t gemv_kn(const LaunchCtx& c, int wtype, const void* W, int64_t ldw, int xtype, const void* x,
+                    int ytype, void* y, int N, int K, float* partials, unsigned int* counters) {
+    if (N <= 0) return cudaSuccess;
+    switch (wtype) {
+        case MGPU_F32:
+            return dispatch_xy<GemvKnLaunch<float>::F>(xtype, ytype, c, W, ldw, x, y, N, K, partials, counters);
+        case MGPU_F16:
+            return dispatch_xy<GemvKnLaunch<__half>::F>(xtype, ytype, c, W, ldw, x, y, N, K, partials, counters);
+        case MGPU_BF16:
+            return dispatch_xy<GemvKnLaunch<__nv_bfloat16>::F>(xtype, ytype, c, W, ldw, x, y, N, K, partials,
+                                                              counters);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace mgpu_k

@@ -1,0 +1,55 @@
+// kernels.h - host-side launchers of the sm_100a kernels (internal to libmgpu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace mgpu_k {
+
+struct LaunchCtx {
+    cudaStream_t stream;
+    int sm_count;
+    int* status;      // per-device status word (MGPU_ERR_DEVICE_TIMEOUT on a bounded-wait expiry)
+    void* workspace;  // per-device scratch arena, zero-initialised once, kept zero by its users
+    size_t workspace_bytes;
+};
+
+// ---------------------------------------------------------------- GEMV (gemv.cu) ----
+// y[N] = W[N][K] (GGUF blocks of qtype) . x[K]
+cudaError_t gemv_q(const LaunchCtx& c, int qtype, const uint8_t* W, int xtype, const void* x, int ytype,
+                   void* y, int N, int K);
+// y[N] = W[N][K] . x[K] for dense W (f32 / f16 / bf16), row pitch ldw elements
+cudaError_t gemv_nk(const LaunchCtx& c, int wtype, const void* W, int64_t ldw, int xtype, const void* x,
+                    int ytype, void* y, int N, int K);
+// y[N] = x[K] . W[K][N] for dense W (reference orientation), row pitch ldw elements.  Split
+// over K with fp32 partials in scratch and a last-CTA reduction in fixed order.
+cudaError_t gemv_kn(const LaunchCtx& c, int wtype, const void* W, int64_t ldw, int xtype, const void* x,
+                    int ytype, void* y, int N, int K, float* partials, unsigned int* counters);
+size_t gemv_kn_scratch_bytes(int N, int K, int sm_count, int* splits_out);
+
+// ---------------------------------------------------------------- misc (misc.cu) ----
+cudaError_t dequant(const LaunchCtx& c, int qtype, const uint8_t* W, int otype, void* out, int64_t n);
+cudaError_t quantize(const LaunchCtx& c, int qtype, const float* src, uint8_t* dst, int64_t n);
+cudaError_t fill_uniform(const LaunchCtx& c, int otype, void* out, int64_t n, uint64_t seed, float lo, float hi);
+cudaError_t fill_normal(const LaunchCtx& c, int otype, void* out, int64_t n, uint64_t seed, float sigma);
+cudaError_t convert(const LaunchCtx& c, int itype, const void* in, int otype, void* out, int64_t n);
+// One CTA waits on an mbarrier that never completes, bounded by limit_ns.
+cudaError_t selftest_bounded_wait(const LaunchCtx& c, uint64_t limit_ns);
+// patches[p][k] (k < kpad, zero for k >= C*ph*pw) from image [C][H][W]; same element type
+cudaError_t im2col(const LaunchCtx& c, int type, const void* img, void* patches, int C, int H, int W, int ph,
+                   int pw, int kpad);
+
+// ---------------------------------------------------------------- GEMM (gemm_tc.cu) --
+struct GemmOperand {
+    const void* ptr;
+    int type;     // MGPU_F16 / MGPU_BF16 / MGPU_Q4_0 / MGPU_Q8_0 / MGPU_F32 (C only)
+    int layout;   // MGPU_LAYOUT_KN / MGPU_LAYOUT_NK (B only)
+    int64_t ld;   // row pitch in elements (dense) or bytes (quantised rows)
+};
+// C[M,N] = A[M,K] * op(B) (+ bias[N]); A row-major [M][lda].
+cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
+                 const void* bias, int bias_type, int M, int N, int K);
+// Why a GEMM request cannot run (nullptr when it can).
+const char* gemm_check(const GemmOperand& A, const GemmOperand& B, const GemmOperand& C, int M, int N, int K);
+
+}  // namespace mgpu_k

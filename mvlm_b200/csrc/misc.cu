@@ -1,0 +1,207 @@
+// misc.cu - element-wise device kernels around the matmul path: GGUF block dequantisation
+// (standalone, for testing the in-kernel decoders), the ggml reference quantiser (to build
+// synthetic GGUF weights on the device for benchmarks), seeded generators, type
+// conversion and the patch_embed im2col gather (vision.cl:154-176 order).
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace mgpu_dev;
+
+namespace {
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t& s) {
+    uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+template <typename T> __device__ __forceinline__ void store_as(void* out, int64_t i, float v) {
+    reinterpret_cast<T*>(out)[i] = from_f32<T>(v);
+}
+__device__ __forceinline__ void store_typed(int otype, void* out, int64_t i, float v) {
+    if (otype == MGPU_F32) store_as<float>(out, i, v);
+    else if (otype == MGPU_F16) store_as<__half>(out, i, v);
+    else store_as<__nv_bfloat16>(out, i, v);
+}
+__device__ __forceinline__ float load_typed(int itype, const void* in, int64_t i) {
+    if (itype == MGPU_F32) return reinterpret_cast<const float*>(in)[i];
+    if (itype == MGPU_F16) return __half2float(reinterpret_cast<const __half*>(in)[i]);
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(in)[i]);
+}
+
+// One thread per 32-element block: w = (q - 8) * d (Q4_0) or q * d (Q8_0), exact in fp32.
+__global__ void dequant_kernel(int qtype, const uint8_t* __restrict__ W, int otype, void* out, int64_t nblocks) {
+    const int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    if (qtype == MGPU_Q4_0) {
+        const uint8_t* p = W + b * 18;
+        const float d = __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+        for (int j = 0; j < 16; ++j) {
+            store_typed(otype, out, b * 32 + j, (float)((int)(p[2 + j] & 0xF) - 8) * d);
+            store_typed(otype, out, b * 32 + j + 16, (float)((int)(p[2 + j] >> 4) - 8) * d);
+        }
+    } else {
+        const uint8_t* p = W + b * 34;
+        const float d = __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+        for (int j = 0; j < 32; ++j) store_typed(otype, out, b * 32 + j, (float)(int8_t)p[2 + j] * d);
+    }
+}
+
+// ggml reference quantiser, one thread per block.  __fmul_rn / __fadd_rn keep the
+// multiply and the +8.5 as two roundings (no FMA contraction), as the reference does.
+__global__ void quantize_kernel(int qtype, const float* __restrict__ src, uint8_t* __restrict__ dst, int64_t nblocks) {
+    const int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    const float* v = src + b * 32;
+    if (qtype == MGPU_Q4_0) {
+        float amax = 0.0f, vmax = 0.0f;
+        for (int j = 0; j < 32; ++j) {
+            const float a = fabsf(v[j]);
+            if (amax < a) { amax = a; vmax = v[j]; }
+        }
+        const float d = __fdiv_rn(vmax, -8.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        uint8_t* o = dst + b * 18;
+        const unsigned short dh = __half_as_ushort(__float2half_rn(d));
+        o[0] = (uint8_t)(dh & 0xFF);
+        o[1] = (uint8_t)(dh >> 8);
+        for (int j = 0; j < 16; ++j) {
+            int q0 = (int)__fadd_rn(__fmul_rn(v[j], id), 8.5f);
+            int q1 = (int)__fadd_rn(__fmul_rn(v[j + 16], id), 8.5f);
+            q0 = min(q0, 15);
+            q1 = min(q1, 15);
+            o[2 + j] = (uint8_t)(q0 | (q1 << 4));
+        }
+    } else {
+        float amax = 0.0f;
+        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        uint8_t* o = dst + b * 34;
+        const unsigned short dh = __half_as_ushort(__float2half_rn(d));
+        o[0] = (uint8_t)(dh & 0xFF);
+        o[1] = (uint8_t)(dh >> 8);
+        for (int j = 0; j < 32; ++j) o[2 + j] = (uint8_t)(int8_t)roundf(__fmul_rn(v[j], id));
+    }
+}
+
+__global__ void fill_uniform_kernel(int otype, void* out, int64_t n, uint64_t seed, float lo, float hi) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        uint64_t s = seed + (uint64_t)i;
+        const float u = (float)(splitmix64(s) >> 40) * (1.0f / 16777216.0f);  // [0, 1)
+        store_typed(otype, out, i, lo + (hi - lo) * u);
+    }
+}
+
+__global__ void fill_normal_kernel(int otype, void* out, int64_t n, uint64_t seed, float sigma) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        uint64_t s = seed + (uint64_t)i * 0x2545F4914F6CDD1Dull;
+        const float u1 = ((float)(splitmix64(s) >> 40) + 1.0f) * (1.0f / 16777216.0f);  // (0, 1]
+        const float u2 = (float)(splitmix64(s) >> 40) * (1.0f / 16777216.0f);
+        store_typed(otype, out, i, sigma * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
+    }
+}
+
+__global__ void convert_kernel(int itype, const void* in, int otype, void* out, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        store_typed(otype, out, i, load_typed(itype, in, i));
+}
+
+// patches[p][k]: p over the (H/ph) x (W/pw) grid row-major, k = c*ph*pw + py*pw + px,
+// zero for k in [C*ph*pw, kpad).  16-bit element copy (no rounding).
+template <typename T>
+__global__ void im2col_kernel(const T* __restrict__ img, T* __restrict__ patches, int C, int H, int W, int ph,
+                              int pw, int kpad, int64_t total) {
+    const int gw = W / pw;
+    const int pd = C * ph * pw;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t p = i / kpad;
+        const int k = (int)(i % kpad);
+        T v;
+        if (k < pd) {
+            const int c = k / (ph * pw), r = k % (ph * pw), py = r / pw, px = r % pw;
+            const int pr = (int)(p / gw), pc = (int)(p % gw);
+            v = img[(size_t)c * H * W + (size_t)(pr * ph + py) * W + (pc * pw + px)];
+        } else {
+            v = from_f32<T>(0.0f);
+        }
+        patches[i] = v;
+    }
+}
+
+// Waits for a phase of an mbarrier on which no thread ever arrives: the bounded wait must
+// expire, record the timeout in *status and return.
+__global__ void selftest_wait_kernel(int* status, uint64_t limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, status, limit_ns);
+}
+
+int grid_for(int64_t n, int sm_count) {
+    const int64_t want = (n + 255) / 256;
+    const int64_t cap = (int64_t)sm_count * 16;
+    return (int)(want < cap ? want : cap);
+}
+
+}  // namespace
+
+namespace mgpu_k {
+
+cudaError_t dequant(const LaunchCtx& c, int qtype, const uint8_t* W, int otype, void* out, int64_t n) {
+    const int64_t nb = n / 32;
+    if (nb <= 0) return cudaSuccess;
+    dequant_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, c.stream>>>(qtype, W, otype, out, nb);
+    return cudaGetLastError();
+}
+
+cudaError_t quantize(const LaunchCtx& c, int qtype, const float* src, uint8_t* dst, int64_t n) {
+    const int64_t nb = n / 32;
+    if (nb <= 0) return cudaSuccess;
+    quantize_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, c.stream>>>(qtype, src, dst, nb);
+    return cudaGetLastError();
+}
+
+cudaError_t fill_uniform(const LaunchCtx& c, int otype, void* out, int64_t n, uint64_t seed, float lo, float hi) {
+    if (n <= 0) return cudaSuccess;
+    fill_uniform_kernel<<<grid_for(n, c.sm_count), 256, 0, c.stream>>>(otype, out, n, seed, lo, hi);
+    return cudaGetLastError();
+}
+
+cudaError_t fill_normal(const LaunchCtx& c, int otype, void* out, int64_t n, uint64_t seed, float sigma) {
+    if (n <= 0) return cudaSuccess;
+    fill_normal_kernel<<<grid_for(n, c.sm_count), 256, 0, c.stream>>>(otype, out, n, seed, sigma);
+    return cudaGetLastError();
+}
+
+cudaError_t convert(const LaunchCtx& c, int itype, const void* in, int otype, void* out, int64_t n) {
+    if (n <= 0) return cudaSuccess;
+    convert_kernel<<<grid_for(n, c.sm_count), 256, 0, c.stream>>>(itype, in, otype, out, n);
+    return cudaGetLastError();
+}
+
+cudaError_t selftest_bounded_wait(const LaunchCtx& c, uint64_t limit_ns) {
+    selftest_wait_kernel<<<1, 32, 0, c.stream>>>(c.status, limit_ns);
+    return cudaGetLastError();
+}
+
+cudaError_t im2col(const LaunchCtx& c, int type, const void* img, void* patches, int C, int H, int W, int ph,
+                   int pw, int kpad) {
+    const int64_t total = (int64_t)(H / ph) * (W / pw) * kpad;
+    if (total <= 0) return cudaSuccess;
+    const int g = grid_for(total, c.sm_count);
+    if (type == MGPU_F16)
+        im2col_kernel<__half><<<g, 256, 0, c.stream>>>((const __half*)img, (__half*)patches, C, H, W, ph, pw, kpad, total);
+    else if (type == MGPU_BF16)
+        im2col_kernel<__nv_bfloat16><<<g, 256, 0, c.stream>>>((const __nv_bfloat16*)img, (__nv_bfloat16*)patches, C, H,
+                                                             W, ph, pw, kpad, total);
+    else
+        return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+}  // namespace mgpu_k

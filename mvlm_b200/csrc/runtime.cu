@@ -1,0 +1,846 @@
+// runtime.cu - host runtime behind include/mgpu_cuda.h: device / stream context, buffers,
+// events, thread-local error state, argument validation and kernel dispatch.
+//
+// Replaces, for the matmul path, MVLM's src/engine/device.cpp (context + single in-order
+// profiling queue, :141-304), src/engine/memory.cpp (buffers and weight images, :28-111),
+// src/engine/compute.cpp (GEMM/GEMV dispatch, :28-152, and the patch_embed / vision_proj
+// dispatch, :474-510, :621-651) and src/engine/profiler.cpp (event timing, :25-53).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/mgpu_cuda.h"
+#include "kernels.h"
+
+struct mgpu_event;
+
+struct mgpu_device {
+    int ordinal;
+    cudaStream_t own_stream;
+    cudaStream_t stream;
+    int sm_count;
+    size_t l2_bytes;
+    int* d_status;
+    int event_mode;
+    void* workspace;
+    size_t workspace_bytes;
+    bool capturing;
+    int saved_event_mode;
+    std::vector<mgpu_event*> event_pool;
+};
+
+struct mgpu_buf {
+    mgpu_device* dev;
+    void* ptr;
+    size_t bytes;
+    bool owned;
+    int type;
+    int layout;
+    int64_t rows, cols, ld;
+};
+
+struct mgpu_graph {
+    mgpu_device* dev;
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+};
+
+struct mgpu_event {
+    mgpu_device* dev;
+    cudaEvent_t start;
+    cudaEvent_t end;
+    bool timed;
+};
+
+namespace {
+
+thread_local int t_err = MGPU_OK;
+thread_local char t_msg[512] = "";
+
+void set_error(int code, const char* fmt, ...) {
+    t_err = code;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_msg, sizeof(t_msg), fmt, ap);
+    va_end(ap);
+    fprintf(stderr, "mgpu error %d: %s\n", code, t_msg);
+}
+
+bool cuda_ok(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return true;
+    set_error(e == cudaErrorMemoryAllocation ? MGPU_ERR_OUT_OF_MEMORY : MGPU_ERR_CUDA, "%s: %s", what,
+              cudaGetErrorString(e));
+    return false;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int ordinal) {
+        cudaGetDevice(&prev);
+        if (prev != ordinal) cudaSetDevice(ordinal);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+size_t elem_size(int type) {
+    switch (type) {
+        case MGPU_F32: return 4;
+        case MGPU_F16:
+        case MGPU_BF16: return 2;
+        default: return 0;
+    }
+}
+bool is_float_type(int t) { return t == MGPU_F32 || t == MGPU_F16 || t == MGPU_BF16; }
+bool is_quant_type(int t) { return t == MGPU_Q4_0 || t == MGPU_Q8_0; }
+size_t quant_row_bytes(int t, int64_t k) { return (size_t)((k + 31) / 32) * (t == MGPU_Q4_0 ? 18 : 34); }
+
+// Scratch arena layout: [0, kScratchOffset) holds the split-K tickets of gemv_kn, which
+// must stay zero between launches (the kernel resets them); everything after it is free
+// for per-call use (split-K partials, im2col patches, staged operands), in stream order.
+constexpr size_t kScratchOffset = 64 * 1024;
+
+mgpu_k::LaunchCtx ctx_of(const mgpu_device* d) {
+    mgpu_k::LaunchCtx c;
+    c.stream = d->stream;
+    c.sm_count = d->sm_count;
+    c.status = d->d_status;
+    c.workspace = d->workspace;
+    c.workspace_bytes = d->workspace_bytes;
+    return c;
+}
+
+// Grow the per-device scratch arena (zero-filled).  Synchronises the stream when it grows.
+bool ensure_workspace(mgpu_device* d, size_t bytes) {
+    if (bytes <= d->workspace_bytes) return true;
+    if (d->capturing) {
+        set_error(MGPU_ERR_INVALID_ARG, "scratch must grow (%zu bytes) during graph capture: run the dispatch once "
+                  "before capturing it", bytes);
+        return false;
+    }
+    size_t want = std::max(bytes, d->workspace_bytes * 2);
+    want = (want + 4095) & ~(size_t)4095;
+    if (!cuda_ok(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize")) return false;
+    if (d->workspace) cudaFree(d->workspace);
+    d->workspace = nullptr;
+    d->workspace_bytes = 0;
+    if (!cuda_ok(cudaMalloc(&d->workspace, want), "cudaMalloc(workspace)")) return false;
+    if (!cuda_ok(cudaMemsetAsync(d->workspace, 0, want, d->stream), "cudaMemsetAsync(workspace)")) return false;
+    d->workspace_bytes = want;
+    return true;
+}
+
+mgpu_event* event_begin(mgpu_device* d) {
+    if (d->event_mode == 0) return nullptr;
+    mgpu_event* ev = nullptr;
+    if (!d->event_pool.empty()) {
+        ev = d->event_pool.back();
+        d->event_pool.pop_back();
+    } else {
+        ev = new mgpu_event();
+        ev->dev = d;
+        cudaEventCreate(&ev->start);
+        cudaEventCreate(&ev->end);
+    }
+    ev->timed = d->event_mode == 2;
+    if (ev->timed) cudaEventRecord(ev->start, d->stream);
+    return ev;
+}
+
+mgpu_event* event_end(mgpu_device* d, mgpu_event* ev) {
+    if (ev) cudaEventRecord(ev->end, d->stream);
+    return ev;
+}
+
+bool check_status(mgpu_device* d) {
+    int st = 0;
+    if (!cuda_ok(cudaMemcpy(&st, d->d_status, sizeof(int), cudaMemcpyDeviceToHost), "read status")) return false;
+    if (st != 0) {
+        cudaMemset(d->d_status, 0, sizeof(int));
+        set_error(st, "a kernel's bounded wait expired (device status %d); its output is invalid", st);
+        return false;
+    }
+    return true;
+}
+
+#define REQUIRE(cond, ...)                               \
+    do {                                                 \
+        if (!(cond)) {                                   \
+            set_error(MGPU_ERR_INVALID_ARG, __VA_ARGS__); \
+            return nullptr;                              \
+        }                                                \
+    } while (0)
+
+int64_t ld_or(const mgpu_buf* b, int64_t dflt) { return b->ld > 0 ? b->ld : dflt; }
+
+// Validate and enqueue one GEMM; false (with the error set) when it cannot run.
+bool gemm_checked(mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N, int K, mgpu_buf* bias,
+                  const char* who, size_t scratch_base = kScratchOffset) {
+#define GREQ(cond, ...)                                  \
+    do {                                                 \
+        if (!(cond)) {                                   \
+            set_error(MGPU_ERR_INVALID_ARG, __VA_ARGS__); \
+            return false;                                \
+        }                                                \
+    } while (0)
+    GREQ(dev && A && B && C, "%s: null argument", who);
+    GREQ(M > 0 && N > 0 && K > 0, "%s: M=%d N=%d K=%d must be positive", who, M, N, K);
+    mgpu_k::GemmOperand a{A->ptr, A->type, MGPU_LAYOUT_KN, ld_or(A, K)};
+    mgpu_k::GemmOperand b{B->ptr, B->type, B->layout, 0};
+    if (is_quant_type(B->type)) b.ld = ld_or(B, (int64_t)quant_row_bytes(B->type, K));
+    else b.ld = ld_or(B, B->layout == MGPU_LAYOUT_NK ? K : N);
+    mgpu_k::GemmOperand c{C->ptr, C->type, MGPU_LAYOUT_KN, ld_or(C, N)};
+    GREQ(A->type == MGPU_F16 || A->type == MGPU_BF16, "%s: A must be fp16 or bf16", who);
+    if (is_quant_type(B->type))
+        GREQ(B->bytes >= (size_t)N * b.ld, "%s: B buffer too small", who);
+    else if (B->layout == MGPU_LAYOUT_NK)
+        GREQ(B->bytes >= ((size_t)(N - 1) * b.ld + K) * 2, "%s: B buffer too small for N=%d K=%d", who, N, K);
+    else
+        GREQ(B->bytes >= ((size_t)(K - 1) * b.ld + N) * 2, "%s: B buffer too small for K=%d N=%d", who, K, N);
+    GREQ(A->bytes >= ((size_t)(M - 1) * a.ld + K) * 2, "%s: A buffer too small for M=%d K=%d", who, M, K);
+    // TMA needs 16-byte aligned bases and row pitches.  The reference accepts any M, N, K, so
+    // 16-bit operands whose rows are not 16-byte aligned are first copied into the scratch
+    // arena with the pitch rounded up to 8 elements (the pad is never read: the tensor maps
+    // keep the logical extents and zero-fill beyond them).
+    auto misaligned = [](const void* p, int64_t ld) { return ((uintptr_t)p & 15) || (ld * 2) % 16; };
+    const bool stage_a = misaligned(a.ptr, a.ld);
+    const bool stage_b = !is_quant_type(B->type) && misaligned(b.ptr, b.ld);
+    if (stage_a || stage_b) {
+        const int64_t a_ld = (K + 7) / 8 * 8;
+        const int64_t b_rows = B->layout == MGPU_LAYOUT_NK ? N : K, b_cols = B->layout == MGPU_LAYOUT_NK ? K : N;
+        const int64_t b_ld = (b_cols + 7) / 8 * 8;
+        const size_t a_bytes = stage_a ? (((size_t)M * a_ld * 2 + 255) & ~(size_t)255) : 0;
+        const size_t b_bytes = stage_b ? (size_t)b_rows * b_ld * 2 : 0;
+        if (!ensure_workspace(dev, scratch_base + a_bytes + b_bytes)) return false;
+        char* ws = (char*)dev->workspace + scratch_base;
+        if (stage_a) {
+            if (!cuda_ok(cudaMemcpy2DAsync(ws, a_ld * 2, a.ptr, a.ld * 2, (size_t)K * 2, M, cudaMemcpyDeviceToDevice,
+                                           dev->stream), "stage A"))
+                return false;
+            a.ptr = ws;
+            a.ld = a_ld;
+        }
+        if (stage_b) {
+            GREQ(B->bytes >= ((size_t)(b_rows - 1) * b.ld + b_cols) * 2, "%s: B buffer too small", who);
+            if (!cuda_ok(cudaMemcpy2DAsync(ws + a_bytes, b_ld * 2, b.ptr, b.ld * 2, (size_t)b_cols * 2, b_rows,
+                                           cudaMemcpyDeviceToDevice, dev->stream), "stage B"))
+                return false;
+            b.ptr = ws + a_bytes;
+            b.ld = b_ld;
+        }
+    }
+    const char* why = mgpu_k::gemm_check(a, b, c, M, N, K);
+    GREQ(!why, "%s: %s", who, why ? why : "");
+    GREQ(C->bytes >= ((size_t)(M - 1) * c.ld + N) * elem_size(C->type), "%s: C buffer too small", who);
+    if (bias)
+        GREQ(is_float_type(bias->type) && bias->bytes >= (size_t)N * elem_size(bias->type),
+             "%s: bias must hold N float values", who);
+#undef GREQ
+    cudaError_t e = mgpu_k::gemm(ctx_of(dev), a, b, c, bias ? bias->ptr : nullptr, bias ? bias->type : 0, M, N, K);
+    return cuda_ok(e, who);
+}
+
+mgpu_event* run_gemm(const mgpu_device* cdev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N, int K,
+                     mgpu_buf* bias, const char* who) {
+    REQUIRE(cdev, "%s: null device", who);
+    mgpu_device* dev = const_cast<mgpu_device*>(cdev);
+    DeviceGuard g(dev->ordinal);
+    mgpu_event* ev = event_begin(dev);
+    if (!gemm_checked(dev, A, B, C, M, N, K, bias, who)) {
+        if (ev) dev->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(dev, ev);
+}
+
+}  // namespace
+
+extern "C" {
+
+int mgpu_last_error(void) { return t_err; }
+const char* mgpu_last_error_string(void) { return t_msg; }
+void mgpu_clear_error(void) {
+    t_err = MGPU_OK;
+    t_msg[0] = 0;
+}
+
+// ------------------------------------------------------------------ device -----------
+mgpu_device* mgpu_init_device(int ordinal) {
+    int n = 0;
+    if (!cuda_ok(cudaGetDeviceCount(&n), "cudaGetDeviceCount")) return nullptr;
+    if (ordinal < 0 || ordinal >= n) {
+        set_error(MGPU_ERR_INVALID_ARG, "device ordinal %d out of range (%d devices)", ordinal, n);
+        return nullptr;
+    }
+    DeviceGuard g(ordinal);
+    cudaDeviceProp p;
+    if (!cuda_ok(cudaGetDeviceProperties(&p, ordinal), "cudaGetDeviceProperties")) return nullptr;
+    if (p.major != 10) {
+        set_error(MGPU_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", ordinal,
+                  p.major, p.minor);
+        return nullptr;
+    }
+    mgpu_device* d = new mgpu_device();
+    d->ordinal = ordinal;
+    d->sm_count = p.multiProcessorCount;
+    d->l2_bytes = (size_t)p.l2CacheSize;
+    d->event_mode = 2;
+    d->workspace = nullptr;
+    d->workspace_bytes = 0;
+    d->capturing = false;
+    d->saved_event_mode = 2;
+    if (!cuda_ok(cudaStreamCreateWithFlags(&d->own_stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
+        !cuda_ok(cudaMalloc(&d->d_status, 256), "cudaMalloc(status)") ||
+        !cuda_ok(cudaMemset(d->d_status, 0, 256), "cudaMemset(status)")) {
+        delete d;
+        return nullptr;
+    }
+    d->stream = d->own_stream;
+    return d;
+}
+
+void mgpu_release_device(mgpu_device* d) {
+    if (!d) return;
+    DeviceGuard g(d->ordinal);
+    cudaStreamSynchronize(d->stream);
+    for (mgpu_event* ev : d->event_pool) {
+        cudaEventDestroy(ev->start);
+        cudaEventDestroy(ev->end);
+        delete ev;
+    }
+    if (d->workspace) cudaFree(d->workspace);
+    cudaFree(d->d_status);
+    cudaStreamDestroy(d->own_stream);
+    delete d;
+}
+
+int mgpu_device_ordinal(const mgpu_device* d) { return d ? d->ordinal : -1; }
+int mgpu_device_sm_count(const mgpu_device* d) { return d ? d->sm_count : 0; }
+size_t mgpu_device_l2_bytes(const mgpu_device* d) { return d ? d->l2_bytes : 0; }
+void* mgpu_device_stream(const mgpu_device* d) { return d ? (void*)d->stream : nullptr; }
+
+int mgpu_set_stream(mgpu_device* d, void* s) {
+    if (!d) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_set_stream: null device");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    d->stream = s ? (cudaStream_t)s : d->own_stream;
+    return MGPU_OK;
+}
+
+int mgpu_set_event_mode(mgpu_device* d, int mode) {
+    if (!d || mode < 0 || mode > 2) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_set_event_mode: bad arguments");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    d->event_mode = mode;
+    return MGPU_OK;
+}
+
+int mgpu_finish(mgpu_device* d) {
+    if (!d) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_finish: null device");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(d->ordinal);
+    if (!cuda_ok(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize")) return t_err;
+    if (!check_status(d)) return t_err;
+    return MGPU_OK;
+}
+
+// ------------------------------------------------------------------ memory -----------
+static mgpu_buf* new_buf(mgpu_device* d, void* p, size_t bytes, bool owned) {
+    mgpu_buf* b = new mgpu_buf();
+    b->dev = d;
+    b->ptr = p;
+    b->bytes = bytes;
+    b->owned = owned;
+    b->type = MGPU_F16;
+    b->layout = MGPU_LAYOUT_KN;
+    b->rows = b->cols = b->ld = 0;
+    return b;
+}
+
+mgpu_buf* mgpu_create_buffer(mgpu_device* d, size_t bytes, const void* host_src) {
+    REQUIRE(d && bytes > 0, "mgpu_create_buffer: null device or zero size");
+    DeviceGuard g(d->ordinal);
+    void* p = nullptr;
+    // Allocation rounded up to 256 bytes so that 16-byte vector / bulk reads of the last
+    // row never leave the allocation.
+    if (!cuda_ok(cudaMalloc(&p, (bytes + 255) & ~(size_t)255), "cudaMalloc")) return nullptr;
+    if (host_src && !cuda_ok(cudaMemcpy(p, host_src, bytes, cudaMemcpyHostToDevice), "cudaMemcpy")) {
+        cudaFree(p);
+        return nullptr;
+    }
+    return new_buf(d, p, bytes, true);
+}
+
+mgpu_buf* mgpu_create_weight_image(mgpu_device* d, int rows, int cols, const uint16_t* data) {
+    REQUIRE(d && rows > 0 && cols > 0, "mgpu_create_weight_image: bad arguments");
+    const int64_t ld = (cols + 7) / 8 * 8;
+    mgpu_buf* b = mgpu_create_buffer(d, (size_t)rows * ld * 2, nullptr);
+    if (!b) return nullptr;
+    DeviceGuard g(d->ordinal);
+    if (!cuda_ok(cudaMemset(b->ptr, 0, b->bytes), "cudaMemset") ||
+        (data && !cuda_ok(cudaMemcpy2D(b->ptr, ld * 2, data, (size_t)cols * 2, (size_t)cols * 2, rows,
+                                       cudaMemcpyHostToDevice),
+                          "cudaMemcpy2D"))) {
+        mgpu_release_buffer(b);
+        return nullptr;
+    }
+    b->type = MGPU_F16;
+    b->layout = MGPU_LAYOUT_KN;
+    b->rows = rows;
+    b->cols = cols;
+    b->ld = ld;
+    return b;
+}
+
+mgpu_buf* mgpu_wrap_buffer(mgpu_device* d, void* device_ptr, size_t bytes) {
+    REQUIRE(d && device_ptr && bytes > 0, "mgpu_wrap_buffer: bad arguments");
+    return new_buf(d, device_ptr, bytes, false);
+}
+
+mgpu_buf* mgpu_buf_view(mgpu_buf* b, size_t offset, size_t bytes) {
+    REQUIRE(b && bytes > 0 && offset + bytes <= b->bytes, "mgpu_buf_view: range outside the buffer");
+    mgpu_buf* v = new_buf(b->dev, (char*)b->ptr + offset, bytes, false);
+    v->type = b->type;
+    v->layout = b->layout;
+    return v;
+}
+
+int mgpu_buf_set_format(mgpu_buf* b, int type, int layout, int64_t rows, int64_t cols, int64_t ld) {
+    if (!b || !(is_float_type(type) || is_quant_type(type)) || (layout != MGPU_LAYOUT_KN && layout != MGPU_LAYOUT_NK) ||
+        rows < 0 || cols < 0 || ld < 0) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_buf_set_format: bad arguments");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    b->type = type;
+    b->layout = layout;
+    b->rows = rows;
+    b->cols = cols;
+    b->ld = ld;
+    return MGPU_OK;
+}
+
+void* mgpu_buf_device_ptr(const mgpu_buf* b) { return b ? b->ptr : nullptr; }
+size_t mgpu_buf_bytes(const mgpu_buf* b) { return b ? b->bytes : 0; }
+
+int mgpu_buf_write(mgpu_buf* b, size_t off, const void* src, size_t bytes) {
+    if (!b || !src || off + bytes > b->bytes) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_buf_write: range outside the buffer");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(b->dev->ordinal);
+    if (!cuda_ok(cudaMemcpyAsync((char*)b->ptr + off, src, bytes, cudaMemcpyHostToDevice, b->dev->stream), "write") ||
+        !cuda_ok(cudaStreamSynchronize(b->dev->stream), "write sync"))
+        return t_err;
+    return MGPU_OK;
+}
+
+int mgpu_buf_read(const mgpu_buf* b, size_t off, void* dst, size_t bytes) {
+    if (!b || !dst || off + bytes > b->bytes) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_buf_read: range outside the buffer");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(b->dev->ordinal);
+    if (!cuda_ok(cudaMemcpyAsync(dst, (const char*)b->ptr + off, bytes, cudaMemcpyDeviceToHost, b->dev->stream), "read") ||
+        !cuda_ok(cudaStreamSynchronize(b->dev->stream), "read sync"))
+        return t_err;
+    if (!check_status(b->dev)) return t_err;
+    return MGPU_OK;
+}
+
+int mgpu_buf_write_async(mgpu_buf* b, size_t off, const void* src, size_t bytes) {
+    if (!b || !src || off + bytes > b->bytes) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_buf_write_async: range outside the buffer");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(b->dev->ordinal);
+    if (!cuda_ok(cudaMemcpyAsync((char*)b->ptr + off, src, bytes, cudaMemcpyHostToDevice, b->dev->stream), "write_async"))
+        return t_err;
+    return MGPU_OK;
+}
+
+int mgpu_buf_read_async(const mgpu_buf* b, size_t off, void* dst, size_t bytes) {
+    if (!b || !dst || off + bytes > b->bytes) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_buf_read_async: range outside the buffer");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(b->dev->ordinal);
+    if (!cuda_ok(cudaMemcpyAsync(dst, (const char*)b->ptr + off, bytes, cudaMemcpyDeviceToHost, b->dev->stream), "read_async"))
+        return t_err;
+    return MGPU_OK;
+}
+
+void* mgpu_host_alloc(size_t bytes) {
+    void* p = nullptr;
+    if (!cuda_ok(cudaMallocHost(&p, bytes), "cudaMallocHost")) return nullptr;
+    return p;
+}
+void mgpu_host_free(void* p) {
+    if (p) cudaFreeHost(p);
+}
+
+void mgpu_release_buffer(mgpu_buf* b) {
+    if (!b) return;
+    if (b->owned && b->ptr) {
+        DeviceGuard g(b->dev->ordinal);
+        cudaStreamSynchronize(b->dev->stream);
+        cudaFree(b->ptr);
+    }
+    delete b;
+}
+
+mgpu_buf* mgpu_upload_weight(mgpu_device* d, const mgpu_tensor_info* t, const void* host) {
+    REQUIRE(d && t && host, "mgpu_upload_weight: null argument");
+    REQUIRE(t->n_dims >= 1 && t->n_dims <= 4, "mgpu_upload_weight: '%s' has %u dims", t->name, t->n_dims);
+    REQUIRE(is_float_type((int)t->type) || is_quant_type((int)t->type),
+            "mgpu_upload_weight: '%s' has unsupported type %u", t->name, t->type);
+    const int64_t cols = (int64_t)t->dims[0];
+    int64_t rows = 1;
+    for (uint32_t i = 1; i < t->n_dims; ++i) rows *= (int64_t)t->dims[i];
+    if (is_quant_type((int)t->type)) REQUIRE(cols % 32 == 0, "mgpu_upload_weight: '%s' ne0 %% 32 != 0", t->name);
+    const size_t row_bytes = is_quant_type((int)t->type) ? quant_row_bytes((int)t->type, cols) : (size_t)cols * elem_size((int)t->type);
+    REQUIRE(t->data_size >= (size_t)rows * row_bytes, "mgpu_upload_weight: '%s' data_size %zu < %zu", t->name,
+            t->data_size, (size_t)rows * row_bytes);
+    mgpu_buf* b = mgpu_create_buffer(d, t->data_size, host);
+    if (!b) return nullptr;
+    b->type = (int)t->type;
+    b->layout = MGPU_LAYOUT_NK;
+    b->rows = rows;
+    b->cols = cols;
+    b->ld = is_quant_type((int)t->type) ? (int64_t)row_bytes : cols;
+    return b;
+}
+
+// ------------------------------------------------------------------ dispatch ---------
+mgpu_event* mgpu_dispatch_gemm_naive(const mgpu_device* d, mgpu_program, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C,
+                                     int M, int N, int K) {
+    return run_gemm(d, A, B, C, M, N, K, nullptr, "dispatch_gemm_naive");
+}
+mgpu_event* mgpu_dispatch_gemm_tiled(const mgpu_device* d, mgpu_program, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C,
+                                     int M, int N, int K) {
+    return run_gemm(d, A, B, C, M, N, K, nullptr, "dispatch_gemm_tiled");
+}
+mgpu_event* mgpu_dispatch_gemm_image(const mgpu_device* d, mgpu_program, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C,
+                                     int M, int N, int K) {
+    return run_gemm(d, A, B, C, M, N, K, nullptr, "dispatch_gemm_image");
+}
+mgpu_event* mgpu_gemm(const mgpu_device* d, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N, int K,
+                      mgpu_buf* bias) {
+    return run_gemm(d, A, B, C, M, N, K, bias, "mgpu_gemm");
+}
+mgpu_event* mgpu_gemm_q(const mgpu_device* d, mgpu_buf* A, mgpu_buf* W, mgpu_buf* C, int M, int N, int K, int type,
+                        mgpu_buf* bias) {
+    REQUIRE(W && is_quant_type(type), "mgpu_gemm_q: type must be Q4_0 or Q8_0");
+    REQUIRE(W->type == type || W->type == MGPU_F16, "mgpu_gemm_q: W is tagged with type %d, not %d", W->type, type);
+    W->type = type;
+    W->layout = MGPU_LAYOUT_NK;
+    return run_gemm(d, A, W, C, M, N, K, bias, "mgpu_gemm_q");
+}
+
+mgpu_event* mgpu_dispatch_gemv(const mgpu_device* cd, mgpu_program, mgpu_buf* x, mgpu_buf* W, mgpu_buf* y, int N,
+                               int K) {
+    REQUIRE(cd && x && W && y, "dispatch_gemv: null argument");
+    REQUIRE(N > 0 && K > 0, "dispatch_gemv: N=%d K=%d", N, K);
+    mgpu_device* d = const_cast<mgpu_device*>(cd);
+    REQUIRE(is_float_type(x->type) && is_float_type(y->type), "dispatch_gemv: x and y must be f32/f16/bf16");
+    REQUIRE(x->bytes >= (size_t)K * elem_size(x->type), "dispatch_gemv: x holds fewer than K=%d values", K);
+    REQUIRE(y->bytes >= (size_t)N * elem_size(y->type), "dispatch_gemv: y holds fewer than N=%d values", N);
+    DeviceGuard g(d->ordinal);
+    cudaError_t e;
+    mgpu_event* ev = nullptr;
+    if (is_quant_type(W->type)) {
+        REQUIRE(W->layout == MGPU_LAYOUT_NK, "dispatch_gemv: quantised W must be GGUF [N][K/32]");
+        REQUIRE(K % 32 == 0, "dispatch_gemv: quantised W needs K %% 32 == 0 (K=%d)", K);
+        const int64_t rb = ld_or(W, (int64_t)quant_row_bytes(W->type, K));
+        REQUIRE(rb == (int64_t)quant_row_bytes(W->type, K), "dispatch_gemv: quantised rows must be dense");
+        REQUIRE(W->bytes >= (size_t)N * rb, "dispatch_gemv: W holds fewer than N=%d rows", N);
+        ev = event_begin(d);
+        e = mgpu_k::gemv_q(ctx_of(d), W->type, (const uint8_t*)W->ptr, x->type, x->ptr, y->type, y->ptr, N, K);
+    } else if (W->layout == MGPU_LAYOUT_NK) {
+        const int64_t ld = ld_or(W, K);
+        REQUIRE(ld >= K && W->bytes >= ((size_t)(N - 1) * ld + K) * elem_size(W->type), "dispatch_gemv: W too small");
+        ev = event_begin(d);
+        e = mgpu_k::gemv_nk(ctx_of(d), W->type, W->ptr, ld, x->type, x->ptr, y->type, y->ptr, N, K);
+    } else {
+        const int64_t ld = ld_or(W, N);
+        REQUIRE(ld >= N && W->bytes >= ((size_t)(K - 1) * ld + N) * elem_size(W->type), "dispatch_gemv: W too small");
+        const size_t need = mgpu_k::gemv_kn_scratch_bytes(N, K, d->sm_count, nullptr);
+        REQUIRE((size_t)((N + 255) / 256) * 4 <= kScratchOffset, "dispatch_gemv: N=%d too large for KN layout", N);
+        if (!ensure_workspace(d, kScratchOffset + need)) return nullptr;
+        unsigned int* counters = (unsigned int*)d->workspace;
+        float* partials = (float*)((char*)d->workspace + kScratchOffset);
+        ev = event_begin(d);
+        e = mgpu_k::gemv_kn(ctx_of(d), W->type, W->ptr, ld, x->type, x->ptr, y->type, y->ptr, N, K, partials, counters);
+    }
+    if (!cuda_ok(e, "dispatch_gemv")) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(d, ev);
+}
+
+mgpu_event* mgpu_gemv_q(const mgpu_device* d, mgpu_buf* x, mgpu_buf* W, mgpu_buf* y, int N, int K, int type) {
+    REQUIRE(W && is_quant_type(type), "mgpu_gemv_q: type must be Q4_0 or Q8_0");
+    REQUIRE(W->type == type || W->type == MGPU_F16, "mgpu_gemv_q: W is tagged with type %d, not %d", W->type, type);
+    W->type = type;
+    W->layout = MGPU_LAYOUT_NK;
+    return mgpu_dispatch_gemv(d, nullptr, x, W, y, N, K);
+}
+
+mgpu_event* mgpu_dispatch_patch_embed(const mgpu_device* cd, mgpu_program, mgpu_buf* image, mgpu_buf* proj_weight,
+                                      mgpu_buf* proj_bias, mgpu_buf* patches, int C, int H, int W, int ph, int pw,
+                                      int embed_dim) {
+    REQUIRE(cd && image && proj_weight && patches, "dispatch_patch_embed: null argument");
+    REQUIRE(C > 0 && ph > 0 && pw > 0 && H >= ph && W >= pw && embed_dim > 0, "dispatch_patch_embed: bad shape");
+    REQUIRE(image->type == MGPU_F16 || image->type == MGPU_BF16, "dispatch_patch_embed: image must be fp16/bf16");
+    REQUIRE(image->bytes >= (size_t)C * H * W * 2, "dispatch_patch_embed: image smaller than C*H*W");
+    mgpu_device* d = const_cast<mgpu_device*>(cd);
+    const int P = (H / ph) * (W / pw);
+    const int pd = C * ph * pw;
+    const int kpad = (pd + 7) / 8 * 8;
+    const size_t ws = (size_t)P * kpad * 2;
+    const size_t off = kScratchOffset;
+    DeviceGuard g(d->ordinal);
+    // Reserve room for a staged copy of proj_weight as well, so that the GEMM below never
+    // has to grow (and reallocate) the arena that already holds the patches.
+    const size_t b_stage = (size_t)pd * ((embed_dim + 7) / 8 * 8) * 2 + (size_t)embed_dim * ((pd + 7) / 8 * 8) * 2;
+    if (!ensure_workspace(d, ((off + ws + 255) & ~(size_t)255) + b_stage)) return nullptr;
+    mgpu_buf A;
+    A.dev = d;
+    A.ptr = (char*)d->workspace + off;
+    A.bytes = ws;
+    A.owned = false;
+    A.type = image->type;
+    A.layout = MGPU_LAYOUT_KN;
+    A.rows = P;
+    A.cols = pd;
+    A.ld = kpad;
+    mgpu_event* ev = event_begin(d);
+    cudaError_t e = mgpu_k::im2col(ctx_of(d), image->type, image->ptr, A.ptr, C, H, W, ph, pw, kpad);
+    if (!cuda_ok(e, "dispatch_patch_embed(im2col)")) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    if (!gemm_checked(d, &A, proj_weight, patches, P, embed_dim, pd, proj_bias, "dispatch_patch_embed",
+                      (off + ws + 255) & ~(size_t)255)) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(d, ev);
+}
+
+mgpu_event* mgpu_dispatch_vision_proj(const mgpu_device* d, mgpu_program, mgpu_buf* tokens, mgpu_buf* proj_weight,
+                                      mgpu_buf* proj_bias, mgpu_buf* output, int num_patches, int vision_dim,
+                                      int llm_dim) {
+    return run_gemm(d, tokens, proj_weight, output, num_patches, llm_dim, vision_dim, proj_bias, "dispatch_vision_proj");
+}
+
+mgpu_event* mgpu_dequant(const mgpu_device* cd, mgpu_buf* W, mgpu_buf* out, int64_t n, int type) {
+    REQUIRE(cd && W && out && is_quant_type(type) && n > 0 && n % 32 == 0, "mgpu_dequant: bad arguments");
+    REQUIRE(is_float_type(out->type), "mgpu_dequant: out must be f32/f16/bf16");
+    REQUIRE(W->bytes >= (size_t)(n / 32) * (type == MGPU_Q4_0 ? 18 : 34), "mgpu_dequant: W too small");
+    REQUIRE(out->bytes >= (size_t)n * elem_size(out->type), "mgpu_dequant: out too small");
+    mgpu_device* d = const_cast<mgpu_device*>(cd);
+    DeviceGuard g(d->ordinal);
+    mgpu_event* ev = event_begin(d);
+    if (!cuda_ok(mgpu_k::dequant(ctx_of(d), type, (const uint8_t*)W->ptr, out->type, out->ptr, n), "mgpu_dequant")) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(d, ev);
+}
+
+// ------------------------------------------------------------------ events -----------
+int mgpu_wait_event(mgpu_event* ev) {
+    if (!ev) return MGPU_OK;
+    DeviceGuard g(ev->dev->ordinal);
+    if (!cuda_ok(cudaEventSynchronize(ev->end), "cudaEventSynchronize")) return t_err;
+    if (!check_status(ev->dev)) return t_err;
+    return MGPU_OK;
+}
+
+void mgpu_release_event(mgpu_event* ev) {
+    if (ev) ev->dev->event_pool.push_back(ev);
+}
+
+double mgpu_profile_end(mgpu_event* ev) {
+    if (!ev || !ev->timed) return 0.0;
+    DeviceGuard g(ev->dev->ordinal);
+    float ms = 0.0f;
+    if (!cuda_ok(cudaEventSynchronize(ev->end), "cudaEventSynchronize")) return 0.0;
+    if (!cuda_ok(cudaEventElapsedTime(&ms, ev->start, ev->end), "cudaEventElapsedTime")) return 0.0;
+    return (double)ms;
+}
+
+float mgpu_event_elapsed_ms(mgpu_event* a, mgpu_event* b) {
+    if (!a || !b) return 0.0f;
+    DeviceGuard g(a->dev->ordinal);
+    float ms = 0.0f;
+    cudaEventSynchronize(b->end);
+    if (!cuda_ok(cudaEventElapsedTime(&ms, a->end, b->end), "cudaEventElapsedTime")) return 0.0f;
+    return ms;
+}
+
+mgpu_event* mgpu_record_event(mgpu_device* d) {
+    REQUIRE(d, "mgpu_record_event: null device");
+    DeviceGuard g(d->ordinal);
+    mgpu_event* ev = nullptr;
+    if (!d->event_pool.empty()) {
+        ev = d->event_pool.back();
+        d->event_pool.pop_back();
+    } else {
+        ev = new mgpu_event();
+        ev->dev = d;
+        cudaEventCreate(&ev->start);
+        cudaEventCreate(&ev->end);
+    }
+    ev->timed = false;
+    const unsigned flags = d->capturing ? cudaEventRecordExternal : cudaEventRecordDefault;
+    if (!cuda_ok(cudaEventRecordWithFlags(ev->end, d->stream, flags), "cudaEventRecordWithFlags")) {
+        d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return ev;
+}
+
+// ------------------------------------------------------------------ graphs -----------
+int mgpu_capture_begin(mgpu_device* d) {
+    if (!d || d->capturing) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_capture_begin: null device or capture already open");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(d->ordinal);
+    if (!cuda_ok(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture"))
+        return t_err;
+    d->capturing = true;
+    d->saved_event_mode = d->event_mode;
+    d->event_mode = 0;
+    return MGPU_OK;
+}
+
+mgpu_graph* mgpu_capture_end(mgpu_device* d) {
+    REQUIRE(d && d->capturing, "mgpu_capture_end: no capture open");
+    DeviceGuard g(d->ordinal);
+    d->capturing = false;
+    d->event_mode = d->saved_event_mode;
+    cudaGraph_t graph = nullptr;
+    if (!cuda_ok(cudaStreamEndCapture(d->stream, &graph), "cudaStreamEndCapture")) return nullptr;
+    cudaGraphExec_t exec = nullptr;
+    if (!cuda_ok(cudaGraphInstantiate(&exec, graph, 0), "cudaGraphInstantiate")) {
+        cudaGraphDestroy(graph);
+        return nullptr;
+    }
+    mgpu_graph* gr = new mgpu_graph();
+    gr->dev = d;
+    gr->graph = graph;
+    gr->exec = exec;
+    return gr;
+}
+
+int mgpu_graph_launch(mgpu_graph* gr) {
+    if (!gr) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_graph_launch: null graph");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(gr->dev->ordinal);
+    if (!cuda_ok(cudaGraphLaunch(gr->exec, gr->dev->stream), "cudaGraphLaunch")) return t_err;
+    return MGPU_OK;
+}
+
+void mgpu_graph_release(mgpu_graph* gr) {
+    if (!gr) return;
+    DeviceGuard g(gr->dev->ordinal);
+    cudaGraphExecDestroy(gr->exec);
+    cudaGraphDestroy(gr->graph);
+    delete gr;
+}
+
+int mgpu_selftest_bounded_wait(mgpu_device* d, uint64_t limit_ns) {
+    if (!d) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_selftest_bounded_wait: null device");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(d->ordinal);
+    if (!cuda_ok(mgpu_k::selftest_bounded_wait(ctx_of(d), limit_ns), "selftest_bounded_wait")) return t_err;
+    return MGPU_OK;
+}
+
+// ------------------------------------------------------------------ ggml table -------
+size_t mgpu_ggml_type_size(int t) {
+    switch (t) {
+        case MGPU_F32: return 4;
+        case MGPU_F16: return 2;
+        case MGPU_BF16: return 2;
+        case MGPU_Q4_0: return 18;
+        case MGPU_Q8_0: return 34;
+        default: return 0;
+    }
+}
+int mgpu_ggml_type_block_size(int t) {
+    switch (t) {
+        case MGPU_F32:
+        case MGPU_F16:
+        case MGPU_BF16: return 1;
+        case MGPU_Q4_0:
+        case MGPU_Q8_0: return 32;
+        default: return 0;
+    }
+}
+
+// ------------------------------------------------------------------ synthetic data ---
+int mgpu_fill_uniform(const mgpu_device* cd, mgpu_buf* out, int64_t n, uint64_t seed, float lo, float hi) {
+    if (!cd || !out || !is_float_type(out->type) || out->bytes < (size_t)n * elem_size(out->type)) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_fill_uniform: bad arguments");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(cd->ordinal);
+    if (!cuda_ok(mgpu_k::fill_uniform(ctx_of(cd), out->type, out->ptr, n, seed, lo, hi), "fill_uniform")) return t_err;
+    return MGPU_OK;
+}
+
+int mgpu_fill_normal(const mgpu_device* cd, mgpu_buf* out, int64_t n, uint64_t seed, float sigma) {
+    if (!cd || !out || !is_float_type(out->type) || out->bytes < (size_t)n * elem_size(out->type)) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_fill_normal: bad arguments");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(cd->ordinal);
+    if (!cuda_ok(mgpu_k::fill_normal(ctx_of(cd), out->type, out->ptr, n, seed, sigma), "fill_normal")) return t_err;
+    return MGPU_OK;
+}
+
+int mgpu_quantize(const mgpu_device* cd, mgpu_buf* src, mgpu_buf* dst, int64_t n, int type) {
+    if (!cd || !src || !dst || !is_quant_type(type) || n % 32 != 0 || src->type != MGPU_F32 ||
+        src->bytes < (size_t)n * 4 || dst->bytes < (size_t)(n / 32) * (type == MGPU_Q4_0 ? 18 : 34)) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_quantize: bad arguments");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(cd->ordinal);
+    if (!cuda_ok(mgpu_k::quantize(ctx_of(cd), type, (const float*)src->ptr, (uint8_t*)dst->ptr, n), "quantize"))
+        return t_err;
+    return MGPU_OK;
+}
+
+int mgpu_convert(const mgpu_device* cd, mgpu_buf* src, mgpu_buf* dst, int64_t n) {
+    if (!cd || !src || !dst || !is_float_type(src->type) || !is_float_type(dst->type) ||
+        src->bytes < (size_t)n * elem_size(src->type) || dst->bytes < (size_t)n * elem_size(dst->type)) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_convert: bad arguments");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(cd->ordinal);
+    if (!cuda_ok(mgpu_k::convert(ctx_of(cd), src->type, src->ptr, dst->type, dst->ptr, n), "convert")) return t_err;
+    return MGPU_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,80 @@
+"""GPU parity of the standalone block decoders, the device quantiser and the generators;
+bounded-wait failure detection; CUDA-graph replay."""
+import numpy as np
+import pytest
+
+import mvlm_b200 as mg
+import oracle as O
+from tests.numerics import TOL_F32, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("qt", [O.Q4_0, O.Q8_0])
+def test_dequant_bit_exact(dev, qt):
+    g = np.load("tests/golden/gguf_quants.npz")
+    name = "q4_0" if qt == O.Q4_0 else "q8_0"
+    n = g["x"].size
+    out = dev.empty(n, mg.F32)
+    mg.dequant(dev, dev.array(g[name], qt, mg.LAYOUT_NK), out, n, qt).wait()
+    np.testing.assert_array_equal(out.read(np.float32).view(np.uint32), g[name + "_deq"].view(np.uint32))
+    for ot, conv in ((mg.F16, O.f16), (mg.BF16, O.bf16)):
+        o16 = dev.empty(n, ot)
+        mg.dequant(dev, dev.array(g[name], qt, mg.LAYOUT_NK), o16, n, qt).wait()
+        np.testing.assert_array_equal(o16.read(np.uint16), conv(g[name + "_deq"]))
+
+
+@pytest.mark.parametrize("qt", [O.Q4_0, O.Q8_0])
+def test_device_quantiser_bit_exact(dev, qt):
+    g = np.load("tests/golden/gguf_quants.npz")
+    x = g["x"]
+    name = "q4_0" if qt == O.Q4_0 else "q8_0"
+    dst = dev.create_buffer(x.size // 32 * mg.BLOCK_BYTES[qt], None)
+    dev.quantize(dev.array(x, mg.F32), dst, x.size, qt)
+    np.testing.assert_array_equal(dst.read(np.uint8), g[name])
+
+
+def test_generators_deterministic(dev):
+    n = 1 << 16
+    a, b = dev.empty(n, mg.F32), dev.empty(n, mg.F32)
+    dev.fill_normal(a, n, 1234, 0.02)
+    dev.fill_normal(b, n, 1234, 0.02)
+    va, vb = a.read(np.float32), b.read(np.float32)
+    np.testing.assert_array_equal(va, vb)
+    assert abs(va.std() - 0.02) < 0.001 and abs(va.mean()) < 0.001
+    dev.fill_uniform(a, n, 99, -1.0, 1.0)
+    u = a.read(np.float32)
+    assert u.min() >= -1.0 and u.max() < 1.0 and abs(u.mean()) < 0.02
+
+
+def test_bounded_wait_reports_timeout_and_device_recovers(dev):
+    dev.finish()
+    dev.selftest_bounded_wait(2_000_000)  # 2 ms limit on a barrier nobody arrives on
+    with pytest.raises(mg.MgpuError) as e:
+        dev.finish()
+    assert e.value.code == mg.ERR_DEVICE_TIMEOUT
+    dev.finish()  # status was consumed; the context is still usable
+    K, N = 256, 8
+    x = O.uniform(K, 1)
+    W = O.quantize(O.normal(N * K, 2, 0.02), O.Q4_0)
+    y = dev.empty(N, mg.F32)
+    mg.gemv_q(dev, dev.array(x, mg.F32), dev.array(W, mg.Q4_0, mg.LAYOUT_NK), y, N, K, mg.Q4_0).wait()
+    assert_close(y.read(np.float32), O.gemm_q(x, W, 1, N, K, O.Q4_0), TOL_F32)
+
+
+def test_graph_capture_replays_gemv(dev):
+    K, N = 2048, 6144
+    x = O.normal(K, 5, 1.0)
+    W = O.quantize(O.normal(N * K, 6, 0.02), O.Q4_0)
+    dx, dW, dy = dev.array(x, mg.F32), dev.array(W, mg.Q4_0, mg.LAYOUT_NK), dev.empty(N, mg.F32)
+    mg.gemv_q(dev, dx, dW, dy, N, K, mg.Q4_0).wait()
+    first = dy.read(np.float32)
+    dev.capture_begin()
+    mg.gemv_q(dev, dx, dW, dy, N, K, mg.Q4_0)
+    g = dev.capture_end()
+    x2 = O.normal(K, 7, 1.0)
+    dx.write(x2)
+    g.launch()
+    dev.finish()
+    assert_close(dy.read(np.float32), O.gemm_q(x2, W, 1, N, K, O.Q4_0, threads=True), TOL_F32)
+    assert not np.array_equal(first, dy.read(np.float32))
