@@ -331,37 +331,35 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         }
     } else if constexpr (kQuant) {
         // ---------------------------------------------------------------- dequantisers
+        // Stage `it` of this CTA is k-block (it % num_kb) of its (it / num_kb)-th tile.  The
+        // packed blocks of stage it+3 are loaded into registers before stage it is decoded,
+        // so three stages of global-memory latency are in flight per thread.
         constexpr int BB = (BMODE == B_Q4) ? 18 : 34;
         constexpr int NW = (BMODE == B_Q4) ? 5 : 9;
         constexpr int UPT = (2 * BN) / (kDqWarps * 32);  // blocks (units) per thread per stage
+        constexpr int NPRE = 3;
         const int dt = tid - 192;
         const int nbk = (g.K + 31) / 32;  // blocks per row
-        RawBlock<NW> raw[UPT];
-        uint32_t it = 0;
-        // prefetch helper: units u = dt + 256 v -> row u >> 1 of the tile, k-block 2 kb + (u & 1)
-        auto load_stage = [&](int tile, int kb) {
-            const int n_blk = tile / g.tiles_m;
+        const int my_tiles = total_tiles > (int)blockIdx.x ? (total_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const uint32_t n_stages = (uint32_t)my_tiles * (uint32_t)g.num_kb;
+        RawBlock<NW> raw[NPRE][UPT];
+        auto load_stage = [&](RawBlock<NW>(&dst)[UPT], uint32_t it) {
+            const bool live = it < n_stages;
+            const int tile = (int)blockIdx.x + (int)(it / g.num_kb) * (int)gridDim.x;
+            const int kb = (int)(it % g.num_kb);
+            const int n_blk = live ? tile / g.tiles_m : 0;
 #pragma unroll
             for (int v = 0; v < UPT; ++v) {
                 const int u = dt + v * kDqWarps * 32;
                 const int n = n_blk * BN + (u >> 1);
                 const int kq = kb * 2 + (u & 1);
-                const bool ok = n < g.N && kq < nbk;
-                load_block<NW, BB>(raw[v], g.Bq + (size_t)n * g.bq_row_bytes + (size_t)kq * BB, g.bq_end, ok);
+                const bool ok = live && n < g.N && kq < nbk;
+                load_block<NW, BB>(dst[v], g.Bq + (size_t)n * g.bq_row_bytes + (size_t)kq * BB, g.bq_end, ok);
             }
         };
-        int tile = blockIdx.x, kb = 0;
-        if (tile < total_tiles) load_stage(tile, 0);
-        while (tile < total_tiles && !abort_flag) {
+        auto decode_stage = [&](RawBlock<NW>(&src)[UPT], uint32_t it) -> bool {
             const uint32_t s = it % S, ph = (it / S) & 1u;
-            RawBlock<NW> cur[UPT];
-#pragma unroll
-            for (int v = 0; v < UPT; ++v) cur[v] = raw[v];
-            // advance and prefetch the next stage's blocks before waiting for this slot
-            int ntile = tile, nkb = kb + 1;
-            if (nkb == g.num_kb) { nkb = 0; ntile += gridDim.x; }
-            if (ntile < total_tiles) load_stage(ntile, nkb);
-            if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
+            if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) return false;
             uint8_t* b_dst = smem + s * SB + kABytes;
 #pragma unroll
             for (int v = 0; v < UPT; ++v) {
@@ -371,14 +369,26 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                 uint4* dst[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) dst[j] = reinterpret_cast<uint4*>(row_base + (((half * 4 + j) ^ (r & 7)) << 4));
-                decode_store<BMODE, T, NW>(cur[v], dst);
+                decode_store<BMODE, T, NW>(src[v], dst);
             }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&full_bar[s]);
-            tile = ntile;
-            kb = nkb;
-            ++it;
+            return true;
+        };
+#pragma unroll
+        for (int p = 0; p < NPRE; ++p) load_stage(raw[p], (uint32_t)p);
+        for (uint32_t it = 0; it < n_stages && !abort_flag; it += NPRE) {
+#pragma unroll
+            for (int p = 0; p < NPRE; ++p) {
+                if (it + p < n_stages) {
+                    RawBlock<NW> cur[UPT];
+#pragma unroll
+                    for (int v = 0; v < UPT; ++v) cur[v] = raw[p][v];
+                    load_stage(raw[p], it + p + NPRE);
+                    if (!decode_stage(cur, it + p)) { abort_flag = 1; break; }
+                }
+            }
         }
     }
 

@@ -5,10 +5,14 @@
 //   streams the CTA's contiguous byte range from HBM into a 4-stage shared-memory ring with
 //   cp.async.bulk (the 1-D TMA engine, 16-byte granular, no registers held in flight); 8
 //   consumer warps decode the 18 / 34-byte blocks out of shared memory.  Each consumer thread
-//   owns one 32-element block column for the whole launch, so its 32 activations stay in
-//   registers; weights are turned into exact fp32 (q-8 or q) with one PRMT per element
-//   (2^23 + q bit pattern) and one packed FADD2, and accumulated with packed FFMA2.  Row sums
-//   are reduced across lanes with a transposing shuffle butterfly.
+//   owns one 32-element block column for the whole launch, so its 32 activations (and their
+//   sum) stay in registers.  Q4_0: each nibble becomes the exact fp32 0.5 + q/256 with one
+//   PRMT; a block's sum_k x_k (q_k - 8) is 256 * sum_k x_k f_k - 136 * sum_k x_k, one packed
+//   FFMA2 per two weights.  Q8_0: q + 128 becomes the exact 2^23 + q + 128 with one PRMT and
+//   one packed FADD2 restores q.  Row sums are reduced across lanes with a transposing
+//   shuffle butterfly.  Two CTAs per SM; launched with programmatic dependent launch: the
+//   producer starts streaming weights while the previous kernel drains, and the consumers
+//   execute griddepcontrol.wait before reading x (which the previous kernel may write).
 // gemv_nk: dense [N][K] rows (GGUF F32/F16/BF16 tensors): warp per row group, 16-byte loads.
 // gemv_kn: dense [K][N] (the reference kernels' orientation): columns across lanes, K split
 //   across CTAs; fp32 partials go to scratch and the last CTA of each column tile sums them
@@ -24,7 +28,8 @@ namespace {
 constexpr int kConsumerThreads = 256;
 constexpr int kGemvThreads = kConsumerThreads + 32;
 constexpr int kGemvStages = 4;
-constexpr uint32_t kGemvSmemBudget = 200 * 1024;
+constexpr int kGemvCtasPerSm = 2;
+constexpr uint32_t kGemvSmemBudget = 100 * 1024;  // per CTA: two CTAs share an SM
 
 template <int QT> struct QTraits;
 template <> struct QTraits<MGPU_Q4_0> {
@@ -42,44 +47,47 @@ template <> struct QTraits<MGPU_Q8_0> {
 // Dot product of one Q4_0 block with 32 activations (pairs xp[0..15]).  w holds the 20
 // aligned bytes that contain the block; `sel` realigns the 16 quant bytes, `dsel` extracts
 // the fp16 scale.  Elements 0..15 are the low nibbles of qs[0..15], 16..31 the high ones.
+// Each nibble q becomes f = 0.5 + q/256 exactly (bits 0x3F0q0000, one PRMT); with
+// xcorr = -136 * sum(x) of the block: sum x (q - 8) = 256 * sum x f + xcorr.
+#define HALF_F(v, byte_sel) __uint_as_float(prmt((v), 0x3F000000u, 0x7044u | ((byte_sel) << 8)))
 __device__ __forceinline__ float q4_0_block_dot(const uint32_t (&w)[5], uint32_t sel, uint32_t dsel,
-                                                const float2 (&xp)[16]) {
+                                                const float2 (&xp)[16], float xcorr) {
     const float d = __half2float(__ushort_as_half((unsigned short)prmt(w[0], 0u, dsel)));
-    const float2 off = make_float2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
-    float2 s = make_float2(0.0f, 0.0f);
+    float2 s0 = make_float2(0.0f, 0.0f), s1 = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
         const uint32_t q = prmt(w[m], w[m + 1], sel);
         const uint32_t lo = q & 0x0F0F0F0Fu;
         const uint32_t hi = (q >> 4) & 0x0F0F0F0Fu;
-        s = __ffma2_rn(xp[2 * m], __fadd2_rn(make_float2(MAGIC_F(lo, 0), MAGIC_F(lo, 1)), off), s);
-        s = __ffma2_rn(xp[2 * m + 1], __fadd2_rn(make_float2(MAGIC_F(lo, 2), MAGIC_F(lo, 3)), off), s);
-        s = __ffma2_rn(xp[8 + 2 * m], __fadd2_rn(make_float2(MAGIC_F(hi, 0), MAGIC_F(hi, 1)), off), s);
-        s = __ffma2_rn(xp[9 + 2 * m], __fadd2_rn(make_float2(MAGIC_F(hi, 2), MAGIC_F(hi, 3)), off), s);
+        s0 = __ffma2_rn(xp[2 * m], make_float2(HALF_F(lo, 0), HALF_F(lo, 1)), s0);
+        s1 = __ffma2_rn(xp[8 + 2 * m], make_float2(HALF_F(hi, 0), HALF_F(hi, 1)), s1);
+        s0 = __ffma2_rn(xp[2 * m + 1], make_float2(HALF_F(lo, 2), HALF_F(lo, 3)), s0);
+        s1 = __ffma2_rn(xp[9 + 2 * m], make_float2(HALF_F(hi, 2), HALF_F(hi, 3)), s1);
     }
-    return d * (s.x + s.y);
+    const float sum = (s0.x + s0.y) + (s1.x + s1.y);
+    return d * fmaf(256.0f, sum, xcorr);
 }
 
-// Same for Q8_0: 32 signed bytes; q ^ 0x80 = q + 128 is placed in the mantissa, then
-// -(2^23 + 128) restores q exactly.
+// Same for Q8_0: 32 signed bytes; q ^ 0x80 = q + 128 is placed in the mantissa of 2^23,
+// then -(2^23 + 128) restores q exactly.
 __device__ __forceinline__ float q8_0_block_dot(const uint32_t (&w)[9], uint32_t sel, uint32_t dsel,
                                                 const float2 (&xp)[16]) {
     const float d = __half2float(__ushort_as_half((unsigned short)prmt(w[0], 0u, dsel)));
     const float2 off = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-    float2 s = make_float2(0.0f, 0.0f);
+    float2 s0 = make_float2(0.0f, 0.0f), s1 = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
         const uint32_t q = prmt(w[m], w[m + 1], sel) ^ 0x80808080u;
-        s = __ffma2_rn(xp[2 * m], __fadd2_rn(make_float2(MAGIC_F(q, 0), MAGIC_F(q, 1)), off), s);
-        s = __ffma2_rn(xp[2 * m + 1], __fadd2_rn(make_float2(MAGIC_F(q, 2), MAGIC_F(q, 3)), off), s);
+        s0 = __ffma2_rn(xp[2 * m], __fadd2_rn(make_float2(MAGIC_F(q, 0), MAGIC_F(q, 1)), off), s0);
+        s1 = __ffma2_rn(xp[2 * m + 1], __fadd2_rn(make_float2(MAGIC_F(q, 2), MAGIC_F(q, 3)), off), s1);
     }
-    return d * (s.x + s.y);
+    return d * ((s0.x + s0.y) + (s1.x + s1.y));
 }
 
 template <int QT, int NW>
 __device__ __forceinline__ float q_block_dot(const uint32_t (&w)[NW], uint32_t sel, uint32_t dsel,
-                                             const float2 (&xp)[16]) {
-    if constexpr (QT == MGPU_Q4_0) return q4_0_block_dot(w, sel, dsel, xp);
+                                             const float2 (&xp)[16], float xcorr) {
+    if constexpr (QT == MGPU_Q4_0) return q4_0_block_dot(w, sel, dsel, xp, xcorr);
     else return q8_0_block_dot(w, sel, dsel, xp);
 }
 
@@ -150,7 +158,7 @@ struct GemvQArgs {
 };
 
 template <int QT, int RPT, typename XT, typename YT>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_q_stream(GemvQArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(GemvQArgs a) {
     constexpr int BB = QTraits<QT>::kBlockBytes;
     constexpr int NW = QTraits<QT>::kWords;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -174,11 +182,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_q_stream(GemvQArgs a) {
             mbar_init(&empty_bar[s], kConsumerThreads / 32);
         }
         fence_mbar_init();
+        // Dependent kernels may be scheduled now; they only read this kernel's output after
+        // their own griddepcontrol.wait.
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     }
     __syncthreads();
 
     if (warp == kConsumerThreads / 32) {
         // ---- producer: stream this CTA's rows chunk by chunk ----
+        // Weights are never written by the preceding kernel, so streaming starts before
+        // griddepcontrol.wait and overlaps the previous kernel's tail.
         if (lane == 0) {
             int c = 0;
             for (; c < nchunks; ++c) {
@@ -200,9 +213,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_q_stream(GemvQArgs a) {
     }
 
     // ---- consumers ----
+    // x (and y) may belong to the preceding kernel of the stream: wait for it to complete.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int col = tid % nb;  // block column owned by this thread for the whole launch
     float2 xp[16];
     load_x32<XT>(reinterpret_cast<const XT*>(a.x), col * 32, xp);
+    float xsum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) xsum += xp[i].x + xp[i].y;
+    const float xcorr = -136.0f * xsum;
     const uint32_t par = (uint32_t)(tid * BB) & 3u;  // block starts at byte 0 or 2 of a word
     const uint32_t sel = par ? 0x7654u : 0x5432u;
     const uint32_t dsel = par ? 0x4432u : 0x4410u;
@@ -222,7 +241,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_q_stream(GemvQArgs a) {
             uint32_t w[NW];
 #pragma unroll
             for (int q = 0; q < NW; ++q) w[q] = wp[q];
-            acc[i] = q_block_dot<QT, NW>(w, sel, dsel, xp);
+            acc[i] = q_block_dot<QT, NW>(w, sel, dsel, xp, xcorr);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[s]);
@@ -426,7 +445,7 @@ struct GemvQLaunch {
                 return cudaGetLastError();
             }
             const int RP = kConsumerThreads / nb;
-            const int G = max(1, min(c.sm_count, (N + RP - 1) / RP));
+            const int G = max(1, min(c.sm_count * kGemvCtasPerSm, (N + RP - 1) / RP));
             const int rows_per_cta = (N + G - 1) / G;
             // Largest rows-per-thread (8,4,2,1) whose chunk fits the CTA's share and the ring.
             int rpt = 8;
@@ -455,8 +474,17 @@ struct GemvQLaunch {
             auto kern = gemv_q_stream<QT, RPT, XT2, YT2>;
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (e != cudaSuccess) return e;
-            kern<<<G, kGemvThreads, smem, c.stream>>>(a);
-            return cudaGetLastError();
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(G);
+            cfg.blockDim = dim3(kGemvThreads);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = c.stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            return cudaLaunchKernelEx(&cfg, kern, a);
         }
     };
 };

@@ -62,27 +62,29 @@ __global__ void quantize_kernel(int qtype, const float* __restrict__ src, uint8_
         }
         const float d = __fdiv_rn(vmax, -8.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        uint8_t* o = dst + b * 18;
-        const unsigned short dh = __half_as_ushort(__float2half_rn(d));
-        o[0] = (uint8_t)(dh & 0xFF);
-        o[1] = (uint8_t)(dh >> 8);
+        uint8_t qs[16];
         for (int j = 0; j < 16; ++j) {
             int q0 = (int)__fadd_rn(__fmul_rn(v[j], id), 8.5f);
             int q1 = (int)__fadd_rn(__fmul_rn(v[j + 16], id), 8.5f);
             q0 = min(q0, 15);
             q1 = min(q1, 15);
-            o[2 + j] = (uint8_t)(q0 | (q1 << 4));
+            qs[j] = (uint8_t)(q0 | (q1 << 4));
         }
+        uint16_t* o = reinterpret_cast<uint16_t*>(dst + b * 18);  // blocks start on 2-byte boundaries
+        o[0] = __half_as_ushort(__float2half_rn(d));
+        for (int j = 0; j < 8; ++j) o[1 + j] = (uint16_t)(qs[2 * j] | ((uint16_t)qs[2 * j + 1] << 8));
     } else {
         float amax = 0.0f;
         for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
         const float d = __fdiv_rn(amax, 127.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        uint8_t* o = dst + b * 34;
-        const unsigned short dh = __half_as_ushort(__float2half_rn(d));
-        o[0] = (uint8_t)(dh & 0xFF);
-        o[1] = (uint8_t)(dh >> 8);
-        for (int j = 0; j < 32; ++j) o[2 + j] = (uint8_t)(int8_t)roundf(__fmul_rn(v[j], id));
+        uint16_t* o = reinterpret_cast<uint16_t*>(dst + b * 34);
+        o[0] = __half_as_ushort(__float2half_rn(d));
+        for (int j = 0; j < 16; ++j) {
+            const uint8_t q0 = (uint8_t)(int8_t)roundf(__fmul_rn(v[2 * j], id));
+            const uint8_t q1 = (uint8_t)(int8_t)roundf(__fmul_rn(v[2 * j + 1], id));
+            o[1 + j] = (uint16_t)(q0 | ((uint16_t)q1 << 8));
+        }
     }
 }
 

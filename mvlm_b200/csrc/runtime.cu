@@ -172,6 +172,14 @@ bool check_status(mgpu_device* d) {
     return true;
 }
 
+// Entry points that return a handle clear the thread-local error first, so that a NULL
+// return with mgpu_last_error() == MGPU_OK means "no event recorded", never a stale error.
+#define API_ENTRY() \
+    do {            \
+        t_err = MGPU_OK; \
+        t_msg[0] = 0;    \
+    } while (0)
+
 #define REQUIRE(cond, ...)                               \
     do {                                                 \
         if (!(cond)) {                                   \
@@ -251,6 +259,7 @@ bool gemm_checked(mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M
 
 mgpu_event* run_gemm(const mgpu_device* cdev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N, int K,
                      mgpu_buf* bias, const char* who) {
+    API_ENTRY();
     REQUIRE(cdev, "%s: null device", who);
     mgpu_device* dev = const_cast<mgpu_device*>(cdev);
     DeviceGuard g(dev->ordinal);
@@ -275,6 +284,7 @@ void mgpu_clear_error(void) {
 
 // ------------------------------------------------------------------ device -----------
 mgpu_device* mgpu_init_device(int ordinal) {
+    API_ENTRY();
     int n = 0;
     if (!cuda_ok(cudaGetDeviceCount(&n), "cudaGetDeviceCount")) return nullptr;
     if (ordinal < 0 || ordinal >= n) {
@@ -371,6 +381,7 @@ static mgpu_buf* new_buf(mgpu_device* d, void* p, size_t bytes, bool owned) {
 }
 
 mgpu_buf* mgpu_create_buffer(mgpu_device* d, size_t bytes, const void* host_src) {
+    API_ENTRY();
     REQUIRE(d && bytes > 0, "mgpu_create_buffer: null device or zero size");
     DeviceGuard g(d->ordinal);
     void* p = nullptr;
@@ -385,6 +396,7 @@ mgpu_buf* mgpu_create_buffer(mgpu_device* d, size_t bytes, const void* host_src)
 }
 
 mgpu_buf* mgpu_create_weight_image(mgpu_device* d, int rows, int cols, const uint16_t* data) {
+    API_ENTRY();
     REQUIRE(d && rows > 0 && cols > 0, "mgpu_create_weight_image: bad arguments");
     const int64_t ld = (cols + 7) / 8 * 8;
     mgpu_buf* b = mgpu_create_buffer(d, (size_t)rows * ld * 2, nullptr);
@@ -406,11 +418,13 @@ mgpu_buf* mgpu_create_weight_image(mgpu_device* d, int rows, int cols, const uin
 }
 
 mgpu_buf* mgpu_wrap_buffer(mgpu_device* d, void* device_ptr, size_t bytes) {
+    API_ENTRY();
     REQUIRE(d && device_ptr && bytes > 0, "mgpu_wrap_buffer: bad arguments");
     return new_buf(d, device_ptr, bytes, false);
 }
 
 mgpu_buf* mgpu_buf_view(mgpu_buf* b, size_t offset, size_t bytes) {
+    API_ENTRY();
     REQUIRE(b && bytes > 0 && offset + bytes <= b->bytes, "mgpu_buf_view: range outside the buffer");
     mgpu_buf* v = new_buf(b->dev, (char*)b->ptr + offset, bytes, false);
     v->type = b->type;
@@ -502,6 +516,7 @@ void mgpu_release_buffer(mgpu_buf* b) {
 }
 
 mgpu_buf* mgpu_upload_weight(mgpu_device* d, const mgpu_tensor_info* t, const void* host) {
+    API_ENTRY();
     REQUIRE(d && t && host, "mgpu_upload_weight: null argument");
     REQUIRE(t->n_dims >= 1 && t->n_dims <= 4, "mgpu_upload_weight: '%s' has %u dims", t->name, t->n_dims);
     REQUIRE(is_float_type((int)t->type) || is_quant_type((int)t->type),
@@ -526,22 +541,27 @@ mgpu_buf* mgpu_upload_weight(mgpu_device* d, const mgpu_tensor_info* t, const vo
 // ------------------------------------------------------------------ dispatch ---------
 mgpu_event* mgpu_dispatch_gemm_naive(const mgpu_device* d, mgpu_program, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C,
                                      int M, int N, int K) {
+    API_ENTRY();
     return run_gemm(d, A, B, C, M, N, K, nullptr, "dispatch_gemm_naive");
 }
 mgpu_event* mgpu_dispatch_gemm_tiled(const mgpu_device* d, mgpu_program, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C,
                                      int M, int N, int K) {
+    API_ENTRY();
     return run_gemm(d, A, B, C, M, N, K, nullptr, "dispatch_gemm_tiled");
 }
 mgpu_event* mgpu_dispatch_gemm_image(const mgpu_device* d, mgpu_program, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C,
                                      int M, int N, int K) {
+    API_ENTRY();
     return run_gemm(d, A, B, C, M, N, K, nullptr, "dispatch_gemm_image");
 }
 mgpu_event* mgpu_gemm(const mgpu_device* d, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N, int K,
                       mgpu_buf* bias) {
+    API_ENTRY();
     return run_gemm(d, A, B, C, M, N, K, bias, "mgpu_gemm");
 }
 mgpu_event* mgpu_gemm_q(const mgpu_device* d, mgpu_buf* A, mgpu_buf* W, mgpu_buf* C, int M, int N, int K, int type,
                         mgpu_buf* bias) {
+    API_ENTRY();
     REQUIRE(W && is_quant_type(type), "mgpu_gemm_q: type must be Q4_0 or Q8_0");
     REQUIRE(W->type == type || W->type == MGPU_F16, "mgpu_gemm_q: W is tagged with type %d, not %d", W->type, type);
     W->type = type;
@@ -551,6 +571,7 @@ mgpu_event* mgpu_gemm_q(const mgpu_device* d, mgpu_buf* A, mgpu_buf* W, mgpu_buf
 
 mgpu_event* mgpu_dispatch_gemv(const mgpu_device* cd, mgpu_program, mgpu_buf* x, mgpu_buf* W, mgpu_buf* y, int N,
                                int K) {
+    API_ENTRY();
     REQUIRE(cd && x && W && y, "dispatch_gemv: null argument");
     REQUIRE(N > 0 && K > 0, "dispatch_gemv: N=%d K=%d", N, K);
     mgpu_device* d = const_cast<mgpu_device*>(cd);
@@ -592,6 +613,7 @@ mgpu_event* mgpu_dispatch_gemv(const mgpu_device* cd, mgpu_program, mgpu_buf* x,
 }
 
 mgpu_event* mgpu_gemv_q(const mgpu_device* d, mgpu_buf* x, mgpu_buf* W, mgpu_buf* y, int N, int K, int type) {
+    API_ENTRY();
     REQUIRE(W && is_quant_type(type), "mgpu_gemv_q: type must be Q4_0 or Q8_0");
     REQUIRE(W->type == type || W->type == MGPU_F16, "mgpu_gemv_q: W is tagged with type %d, not %d", W->type, type);
     W->type = type;
@@ -602,6 +624,7 @@ mgpu_event* mgpu_gemv_q(const mgpu_device* d, mgpu_buf* x, mgpu_buf* W, mgpu_buf
 mgpu_event* mgpu_dispatch_patch_embed(const mgpu_device* cd, mgpu_program, mgpu_buf* image, mgpu_buf* proj_weight,
                                       mgpu_buf* proj_bias, mgpu_buf* patches, int C, int H, int W, int ph, int pw,
                                       int embed_dim) {
+    API_ENTRY();
     REQUIRE(cd && image && proj_weight && patches, "dispatch_patch_embed: null argument");
     REQUIRE(C > 0 && ph > 0 && pw > 0 && H >= ph && W >= pw && embed_dim > 0, "dispatch_patch_embed: bad shape");
     REQUIRE(image->type == MGPU_F16 || image->type == MGPU_BF16, "dispatch_patch_embed: image must be fp16/bf16");
@@ -644,10 +667,12 @@ mgpu_event* mgpu_dispatch_patch_embed(const mgpu_device* cd, mgpu_program, mgpu_
 mgpu_event* mgpu_dispatch_vision_proj(const mgpu_device* d, mgpu_program, mgpu_buf* tokens, mgpu_buf* proj_weight,
                                       mgpu_buf* proj_bias, mgpu_buf* output, int num_patches, int vision_dim,
                                       int llm_dim) {
+    API_ENTRY();
     return run_gemm(d, tokens, proj_weight, output, num_patches, llm_dim, vision_dim, proj_bias, "dispatch_vision_proj");
 }
 
 mgpu_event* mgpu_dequant(const mgpu_device* cd, mgpu_buf* W, mgpu_buf* out, int64_t n, int type) {
+    API_ENTRY();
     REQUIRE(cd && W && out && is_quant_type(type) && n > 0 && n % 32 == 0, "mgpu_dequant: bad arguments");
     REQUIRE(is_float_type(out->type), "mgpu_dequant: out must be f32/f16/bf16");
     REQUIRE(W->bytes >= (size_t)(n / 32) * (type == MGPU_Q4_0 ? 18 : 34), "mgpu_dequant: W too small");
@@ -694,6 +719,7 @@ float mgpu_event_elapsed_ms(mgpu_event* a, mgpu_event* b) {
 }
 
 mgpu_event* mgpu_record_event(mgpu_device* d) {
+    API_ENTRY();
     REQUIRE(d, "mgpu_record_event: null device");
     DeviceGuard g(d->ordinal);
     mgpu_event* ev = nullptr;
@@ -731,6 +757,7 @@ int mgpu_capture_begin(mgpu_device* d) {
 }
 
 mgpu_graph* mgpu_capture_end(mgpu_device* d) {
+    API_ENTRY();
     REQUIRE(d && d->capturing, "mgpu_capture_end: no capture open");
     DeviceGuard g(d->ordinal);
     d->capturing = false;
