@@ -33,12 +33,26 @@ namespace {
 constexpr int BM = 128, BK = 64;
 constexpr int kABytes = BM * BK * 2;  // 16 KB
 constexpr int kSmemBudget = 200 * 1024;
-enum BMode { B_TMA_K = 0, B_TMA_MN = 1, B_Q8 = 2, B_Q4 = 3 };
+// B operand modes: 16-bit via TMA (K-major / MN-major); GGUF blocks read with plain loads
+// (any K % 32 == 0); GGUF blocks staged by TMA in 256-k groups (K % 256 == 0).
+enum BMode { B_TMA_K = 0, B_TMA_MN = 1, B_Q8 = 2, B_Q4 = 3, B_Q8_TMA = 4, B_Q4_TMA = 5 };
+__host__ __device__ constexpr bool is_quant_mode(int m) { return m >= B_Q8; }
+__host__ __device__ constexpr bool is_packed_tma(int m) { return m >= B_Q8_TMA; }
+__host__ __device__ constexpr bool is_q4_mode(int m) { return m == B_Q4 || m == B_Q4_TMA; }
+// bytes of one 256-element group of a GGUF row (8 blocks)
+__host__ __device__ constexpr int group_bytes(int m) { return is_q4_mode(m) ? 144 : 272; }
 constexpr int kDqWarps = 8;
 
-__host__ __device__ constexpr int gemm_threads(int bmode) { return 192 + (bmode >= B_Q8 ? kDqWarps * 32 : 0); }
+__host__ __device__ constexpr int gemm_threads(int bmode) { return 192 + (is_quant_mode(bmode) ? kDqWarps * 32 : 0); }
 __host__ __device__ constexpr int stage_bytes(int bn) { return kABytes + bn * BK * 2; }
-__host__ __device__ constexpr int num_stages(int bn) { return kSmemBudget / stage_bytes(bn); }
+// packed-group ring (two slots) of the TMA-staged quantised modes
+__host__ __device__ constexpr int packed_bytes(int bn, int bmode) { return is_packed_tma(bmode) ? 2 * bn * group_bytes(bmode) : 0; }
+__host__ __device__ constexpr int num_stages(int bn, int bmode = B_TMA_K) {
+    return is_packed_tma(bmode) ? 4 : kSmemBudget / stage_bytes(bn);
+}
+__host__ __device__ constexpr int smem_bytes(int bn, int bmode) {
+    return num_stages(bn, bmode) * stage_bytes(bn) + packed_bytes(bn, bmode) + 1024;
+}
 
 struct GemmArgs {
     int M, N, K, num_kb, tiles_m, tiles_n;
@@ -125,7 +139,7 @@ __device__ __forceinline__ void decode_store(const RawBlock<NW>& rb, uint4* cons
     const uint32_t dsel = rb.par ? 0x4432u : 0x4410u;
     const float d = __half2float(__ushort_as_half((unsigned short)prmt(rb.w[0], 0u, dsel)));
     const float2 dd = make_float2(d, d);
-    if constexpr (BMODE == B_Q4) {
+    if constexpr (is_q4_mode(BMODE)) {
         const float2 off = make_float2(-8388616.0f, -8388616.0f);
         uint32_t lo[4], hi[4];
 #pragma unroll
@@ -172,10 +186,10 @@ __device__ __forceinline__ void decode_store(const RawBlock<NW>& rb, uint4* cons
 template <int BN, int BMODE, typename T>
 __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
-    constexpr int S = num_stages(BN);
+    constexpr int S = num_stages(BN, BMODE);
     constexpr int SB = stage_bytes(BN);
     constexpr uint32_t kTmemCols = 2 * BN;
-    constexpr bool kQuant = BMODE >= B_Q8;
+    constexpr bool kQuant = is_quant_mode(BMODE);
     constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
     constexpr uint32_t kIdesc = idesc_f16(kBf16, false, BMODE == B_TMA_MN, BM, BN);
 
@@ -186,6 +200,8 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
     __shared__ __align__(8) uint64_t tfull_bar[2];
     __shared__ __align__(8) uint64_t tempty_bar[2];
     __shared__ __align__(8) uint64_t drain_bar;
+    __shared__ __align__(8) uint64_t pk_full[2];
+    __shared__ __align__(8) uint64_t pk_empty[2];
     __shared__ uint32_t tmem_base_slot;
     __shared__ volatile int abort_flag;
 
@@ -194,7 +210,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full_bar[s], 1 + (kQuant ? kDqWarps : 0));
+            mbar_init(&full_bar[s], 1 + (is_packed_tma(BMODE) ? kDqWarps / 2 : kQuant ? kDqWarps : 0));
             mbar_init(&empty_bar[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -202,12 +218,16 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             mbar_init(&tempty_bar[a], 4);
         }
         mbar_init(&drain_bar, 1);
+        for (int p = 0; p < 2; ++p) {
+            mbar_init(&pk_full[p], 1);
+            mbar_init(&pk_empty[p], kDqWarps);
+        }
         abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
         prefetch_tensormap(&tmA);
-        if (!kQuant) prefetch_tensormap(&tmB);
+        if (!kQuant || is_packed_tma(BMODE)) prefetch_tensormap(&tmB);
     }
     if (warp == 1) {
         tmem_alloc(&tmem_base_slot, kTmemCols);
@@ -329,13 +349,81 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[acc]);
         }
+    } else if constexpr (is_packed_tma(BMODE)) {
+        // ---------------------------------------------------------------- dequantisers (TMA-staged)
+        // Groups of 256 k (8 GGUF blocks per row) arrive by TMA in a two-slot ring; thread
+        // (row r, half h) decodes blocks 4h..4h+3 of its row, i.e. MMA k-stages 2h and 2h+1 of
+        // the group, straight from shared memory into the swizzled B tiles.
+        constexpr int GB = group_bytes(BMODE);
+        constexpr int HB = GB / 2;         // bytes per half row
+        constexpr int HW = HB / 4;         // 32-bit words per half row (34 or 18)
+        constexpr int BB = is_q4_mode(BMODE) ? 18 : 34;
+        constexpr int NW = is_q4_mode(BMODE) ? 5 : 9;
+        static_assert(BN == 128, "packed mode uses 128-row B tiles");
+        const int dt = tid - 192;
+        const int r = dt & (BN - 1), h = dt >> 7;
+        uint8_t* pk = smem + S * SB;
+        const int groups = g.K / 256;
+        const int my_tiles = total_tiles > (int)blockIdx.x ? (total_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const uint32_t n_groups = (uint32_t)my_tiles * (uint32_t)groups;
+        auto issue_group = [&](uint32_t gi) {
+            const int tile = (int)blockIdx.x + (int)(gi / groups) * (int)gridDim.x;
+            const int grp = (int)(gi % groups);
+            const uint32_t slot = gi & 1u;
+            if (!mbar_wait(&pk_empty[slot], ((gi >> 1) & 1u) ^ 1u, g.status)) return false;
+            mbar_arrive_expect_tx(&pk_full[slot], (uint32_t)(BN * GB));
+            tma_load_2d(pk + slot * (BN * GB), &tmB, grp * (GB / 2), (tile / g.tiles_m) * BN, &pk_full[slot]);
+            return true;
+        };
+        if (dt == 0 && n_groups > 0 && !issue_group(0)) abort_flag = 1;
+        for (uint32_t gi = 0; gi < n_groups && !abort_flag; ++gi) {
+            if (dt == 0 && gi + 1 < n_groups && !issue_group(gi + 1)) { abort_flag = 1; break; }
+            const uint32_t slot = gi & 1u;
+            if (!mbar_wait(&pk_full[slot], (gi >> 1) & 1u, g.status)) { abort_flag = 1; break; }
+            uint32_t w[HW];
+            const uint2* src = reinterpret_cast<const uint2*>(pk + slot * (BN * GB) + r * GB + h * HB);
+#pragma unroll
+            for (int i = 0; i < HW / 2; ++i) {
+                const uint2 v = src[i];
+                w[2 * i] = v.x;
+                w[2 * i + 1] = v.y;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pk_empty[slot]);
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+                const uint32_t it = gi * 4 + 2 * h + jj;
+                const uint32_t s = it % S, ph = (it / S) & 1u;
+                if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
+                uint8_t* row_base = smem + s * SB + kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    constexpr int dummy = 0;
+                    (void)dummy;
+                    const int bi = 2 * jj + half;  // block within this thread's half row
+                    RawBlock<NW> rb;
+                    rb.valid = true;
+                    // block bi starts at byte BB * bi of the half row (compile-time word / parity)
+#pragma unroll
+                    for (int q = 0; q < NW; ++q) rb.w[q] = w[(BB * bi) / 4 + q];
+                    rb.par = (uint32_t)((BB * bi) & 3);
+                    uint4* dst[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) dst[j] = reinterpret_cast<uint4*>(row_base + (((half * 4 + j) ^ (r & 7)) << 4));
+                    decode_store<BMODE, T, NW>(rb, dst);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full_bar[s]);
+            }
+        }
     } else if constexpr (kQuant) {
         // ---------------------------------------------------------------- dequantisers
         // Stage `it` of this CTA is k-block (it % num_kb) of its (it / num_kb)-th tile.  The
         // packed blocks of stage it+3 are loaded into registers before stage it is decoded,
         // so three stages of global-memory latency are in flight per thread.
-        constexpr int BB = (BMODE == B_Q4) ? 18 : 34;
-        constexpr int NW = (BMODE == B_Q4) ? 5 : 9;
+        constexpr int BB = is_q4_mode(BMODE) ? 18 : 34;
+        constexpr int NW = is_q4_mode(BMODE) ? 5 : 9;
         constexpr int UPT = (2 * BN) / (kDqWarps * 32);  // blocks (units) per thread per stage
         constexpr int NPRE = 3;
         const int dt = tid - 192;
@@ -433,10 +521,25 @@ bool make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over 16-bit units without swizzle (packed GGUF rows): inner dim `cols`, outer
+// `rows`, row pitch `ld` units, box {box_cols, box_rows}.
+bool make_map_plain(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,
+                    int box_rows) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int BMODE, typename T>
 cudaError_t launch_gemm(const mgpu_k::LaunchCtx& c, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g) {
     auto kern = gemm_tc_kernel<BN, BMODE, T>;
-    const int smem = num_stages(BN) * stage_bytes(BN) + 1024;
+    const int smem = smem_bytes(BN, BMODE);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     const int tiles = g.tiles_m * g.tiles_n;
@@ -452,7 +555,13 @@ cudaError_t launch_mode(const mgpu_k::LaunchCtx& c, int bmode, const CUtensorMap
         case B_TMA_K: return launch_gemm<BN, B_TMA_K, T>(c, ma, mb, g);
         case B_TMA_MN: return launch_gemm<BN, B_TMA_MN, T>(c, ma, mb, g);
         case B_Q8: return launch_gemm<BN, B_Q8, T>(c, ma, mb, g);
-        default: return launch_gemm<BN, B_Q4, T>(c, ma, mb, g);
+        case B_Q4: return launch_gemm<BN, B_Q4, T>(c, ma, mb, g);
+        case B_Q8_TMA:
+            if constexpr (BN == 128) return launch_gemm<BN, B_Q8_TMA, T>(c, ma, mb, g);
+            return cudaErrorInvalidValue;
+        default:
+            if constexpr (BN == 128) return launch_gemm<BN, B_Q4_TMA, T>(c, ma, mb, g);
+            return cudaErrorInvalidValue;
     }
 }
 
@@ -487,8 +596,13 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
                  const void* bias, int bias_type, int M, int N, int K) {
     if (gemm_check(A, B, C, M, N, K)) return cudaErrorInvalidValue;
     int bmode;
-    if (B.type == MGPU_Q8_0) bmode = B_Q8;
-    else if (B.type == MGPU_Q4_0) bmode = B_Q4;
+    const bool quant = B.type == MGPU_Q8_0 || B.type == MGPU_Q4_0;
+    // Packed rows can be staged by TMA in 256-k groups when every group starts on a 16-byte
+    // boundary: K % 256 == 0, row pitch % 16 == 0 and a 16-byte aligned base.
+    const bool packed_ok = quant && K % 256 == 0 && B.ld % 16 == 0 && (reinterpret_cast<uintptr_t>(B.ptr) & 15) == 0 &&
+                           B.ld == (int64_t)(K / 32) * (B.type == MGPU_Q4_0 ? 18 : 34);
+    if (B.type == MGPU_Q8_0) bmode = packed_ok ? B_Q8_TMA : B_Q8;
+    else if (B.type == MGPU_Q4_0) bmode = packed_ok ? B_Q4_TMA : B_Q4;
     else bmode = (B.layout == MGPU_LAYOUT_NK) ? B_TMA_K : B_TMA_MN;
 
     // Pick BN by the estimated makespan over the SMs (tile time ~ BN + fixed overhead).
@@ -498,7 +612,7 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
         const long waves = (tiles + c.sm_count - 1) / c.sm_count;
         return waves * (bn + 32);
     };
-    const int BN = makespan(128) < makespan(256) ? 128 : 256;
+    const int BN = is_packed_tma(bmode) ? 128 : (makespan(128) < makespan(256) ? 128 : 256);
 
     GemmArgs g;
     g.M = M;
@@ -528,6 +642,11 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
         g.Bq = reinterpret_cast<const uint8_t*>(B.ptr);
         g.bq_row_bytes = B.ld;
         g.bq_end = g.Bq + (size_t)N * B.ld;
+        if (is_packed_tma(bmode)) {
+            // the packed rows as a 2-D array of 16-bit units: box = one 256-k group x BN rows
+            if (!make_map_plain(&mb, B.ptr, N, B.ld / 2, B.ld / 2, group_bytes(bmode) / 2, BN))
+                return cudaErrorInvalidValue;
+        }
     }
     const bool bf16 = A.type == MGPU_BF16;
     if (BN == 256)

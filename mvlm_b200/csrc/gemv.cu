@@ -5,14 +5,14 @@
 //   streams the CTA's contiguous byte range from HBM into a 4-stage shared-memory ring with
 //   cp.async.bulk (the 1-D TMA engine, 16-byte granular, no registers held in flight); 8
 //   consumer warps decode the 18 / 34-byte blocks out of shared memory.  Each consumer thread
-//   owns one 32-element block column for the whole launch, so its 32 activations (and their
-//   sum) stay in registers.  Q4_0: each nibble becomes the exact fp32 0.5 + q/256 with one
-//   PRMT; a block's sum_k x_k (q_k - 8) is 256 * sum_k x_k f_k - 136 * sum_k x_k, one packed
-//   FFMA2 per two weights.  Q8_0: q + 128 becomes the exact 2^23 + q + 128 with one PRMT and
-//   one packed FADD2 restores q.  Row sums are reduced across lanes with a transposing
-//   shuffle butterfly.  Two CTAs per SM; launched with programmatic dependent launch: the
-//   producer starts streaming weights while the previous kernel drains, and the consumers
-//   execute griddepcontrol.wait before reading x (which the previous kernel may write).
+//   owns one 32-element block column for the whole launch; its 32 activations are turned
+//   once into 23-bit fixed point (three byte planes), and every block's dot product is exact
+//   integer dp4a arithmetic on the packed nibbles / int8s (no per-weight unpacking), scaled
+//   once per block in fp32 by the fp16 d.  Row sums are reduced across lanes with a
+//   transposing shuffle butterfly.  Two CTAs per SM; launched with programmatic dependent
+//   launch: the producer starts streaming weights while the previous kernel drains, and the
+//   consumers execute griddepcontrol.wait before reading x (which the previous kernel may
+//   write).
 // gemv_nk: dense [N][K] rows (GGUF F32/F16/BF16 tensors): warp per row group, 16-byte loads.
 // gemv_kn: dense [K][N] (the reference kernels' orientation): columns across lanes, K split
 //   across CTAs; fp32 partials go to scratch and the last CTA of each column tile sums them
@@ -41,83 +41,175 @@ template <> struct QTraits<MGPU_Q8_0> {
     static constexpr int kWords = 9;
 };
 
-// 2^23 + b as an fp32 bit pattern for byte `b` (0..255) of `v`: exact, one PRMT.
-#define MAGIC_F(v, byte_sel) __uint_as_float(prmt((v), 0x4B000000u, 0x7540u | (byte_sel)))
+// ---- integer inner product ---------------------------------------------------------
+// Each consumer thread owns one 32-element block column for the whole launch.  Its 32
+// activations are converted once to 23-bit fixed point relative to their own max
+// (x_i = X_i * 2^(e-22), |X_i| <= 2^22) and split into three byte planes
+// X = b2 * 2^16 + b1 * 2^8 + b0 (b0, b1 unsigned, b2 signed), packed four elements per
+// word in the order the quant bytes arrive.  A block's sum_k X_k q_k is then exact integer
+// arithmetic: one dp4a per four weights and byte plane, straight on the packed nibbles
+// (Q4_0: q & 0x0F0F0F0F, and (q & 0xF0F0F0F0) = 16 * the high nibbles) or int8 (Q8_0).
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 
-// Dot product of one Q4_0 block with 32 activations (pairs xp[0..15]).  w holds the 20
-// aligned bytes that contain the block; `sel` realigns the 16 quant bytes, `dsel` extracts
-// the fp16 scale.  Elements 0..15 are the low nibbles of qs[0..15], 16..31 the high ones.
-// Each nibble q becomes f = 0.5 + q/256 exactly (bits 0x3F0q0000, one PRMT); with
-// xcorr = -136 * sum(x) of the block: sum x (q - 8) = 256 * sum x f + xcorr.
-#define HALF_F(v, byte_sel) __uint_as_float(prmt((v), 0x3F000000u, 0x7044u | ((byte_sel) << 8)))
+// The thread's activations in fixed point.  p[plane][w]: plane 0..2 = b0, b1, b2;
+// w = 0..7 = elements 4w..4w+3.  scale = 2^(e-22); xsum = sum_k X_k.
+struct XFixed {
+    uint32_t p[3][8];
+    float scale;
+    float xsum;
+};
+
+// The CTA converts all K activations once, cooperatively: thread t takes 4 consecutive
+// elements at a time, the 8 threads of a 32-element block agree on the block's exponent
+// with shuffles, and the packed byte planes go to shared memory:
+//   planes[p * (K/4) + w]  (w = word index = element / 4), bscale[b], bsum[b] per block b.
+// Consumer threads then read their own block's 24 words.  Costs one round trip to L2 plus a
+// handful of instructions per thread, instead of 32 loads and conversions per thread.
+template <typename XT>
+__device__ __forceinline__ void prepare_x(const XT* __restrict__ x, int K, uint32_t* planes, float* bscale,
+                                          float* bsum, int tid, int nthreads) {
+    // words = K / 4 is a multiple of 256 (K % 1024 == 0) and at most 2048 (K <= 8192), so each
+    // thread converts at most 8 words; all loads are issued before any is used, so the
+    // whole activation vector costs one round trip.
+    constexpr int kMaxIter = 8;
+    const int words = K / 4;
+    const int iters = words / nthreads;
+    float v[kMaxIter][4];
+#pragma unroll
+    for (int it = 0; it < kMaxIter; ++it) {
+        if (it < iters) {
+            const int w = it * nthreads + tid;
+            if constexpr (sizeof(XT) == 4) {
+                const float4 f = __ldg(reinterpret_cast<const float4*>(x) + w);
+                v[it][0] = f.x; v[it][1] = f.y; v[it][2] = f.z; v[it][3] = f.w;
+            } else {
+                const uint2 u = __ldg(reinterpret_cast<const uint2*>(x) + w);
+                const uint32_t uu[2] = {u.x, u.y};
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    XT lo, hi;
+                    uint16_t l16 = (uint16_t)(uu[j] & 0xFFFF), h16 = (uint16_t)(uu[j] >> 16);
+                    memcpy(&lo, &l16, 2);
+                    memcpy(&hi, &h16, 2);
+                    v[it][2 * j] = to_f32<XT>(lo);
+                    v[it][2 * j + 1] = to_f32<XT>(hi);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int it = 0; it < kMaxIter; ++it) {
+        if (it < iters) {
+            const int w = it * nthreads + tid;
+            float amax = fmaxf(fmaxf(fabsf(v[it][0]), fabsf(v[it][1])), fmaxf(fabsf(v[it][2]), fabsf(v[it][3])));
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            int e = 0;
+            frexpf(amax, &e);  // the block's |x| < 2^e
+            const float up = __int_as_float((127 + 22 - e) << 23);  // 2^(22-e); |e| < 100 for finite x
+            uint32_t b0 = 0, b1 = 0, b2 = 0;
+            int sum = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int X = __float2int_rn(v[it][j] * up);  // |X| <= 2^22
+                sum += X;
+                b0 |= (uint32_t)(X & 0xFF) << (8 * j);
+                b1 |= (uint32_t)((X >> 8) & 0xFF) << (8 * j);
+                b2 |= (uint32_t)((X >> 16) & 0xFF) << (8 * j);
+            }
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            planes[w] = b0;
+            planes[words + w] = b1;
+            planes[2 * words + w] = b2;
+            if ((tid & 7) == 0) {
+                bscale[w >> 3] = __int_as_float((127 + e - 22) << 23);  // 2^(e-22)
+                bsum[w >> 3] = (float)sum;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void load_xfixed(const uint32_t* planes, const float* bscale, const float* bsum,
+                                            int words, int col, XFixed& xf) {
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+        const uint4* src = reinterpret_cast<const uint4*>(planes + p * words + col * 8);
+        const uint4 a = src[0], b = src[1];
+        xf.p[p][0] = a.x; xf.p[p][1] = a.y; xf.p[p][2] = a.z; xf.p[p][3] = a.w;
+        xf.p[p][4] = b.x; xf.p[p][5] = b.y; xf.p[p][6] = b.z; xf.p[p][7] = b.w;
+    }
+    xf.scale = bscale[col];
+    xf.xsum = bsum[col];
+}
+
+// One Q4_0 block against the thread's activations.  w = the 20 aligned bytes containing the
+// block; `sel` realigns the 16 quant bytes, `dsel` extracts the fp16 scale.  Element j < 16
+// is the low nibble of qs[j], element j + 16 the high nibble.
+// Returns d * sum_k x_k (q_k - 8).
 __device__ __forceinline__ float q4_0_block_dot(const uint32_t (&w)[5], uint32_t sel, uint32_t dsel,
-                                                const float2 (&xp)[16], float xcorr) {
+                                                const XFixed& xf) {
     const float d = __half2float(__ushort_as_half((unsigned short)prmt(w[0], 0u, dsel)));
-    float2 s0 = make_float2(0.0f, 0.0f), s1 = make_float2(0.0f, 0.0f);
+    int lo0 = 0, lo1 = 0, lo2 = 0, hi0 = 0, hi1 = 0, hi2 = 0;
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
         const uint32_t q = prmt(w[m], w[m + 1], sel);
-        const uint32_t lo = q & 0x0F0F0F0Fu;
-        const uint32_t hi = (q >> 4) & 0x0F0F0F0Fu;
-        s0 = __ffma2_rn(xp[2 * m], make_float2(HALF_F(lo, 0), HALF_F(lo, 1)), s0);
-        s1 = __ffma2_rn(xp[8 + 2 * m], make_float2(HALF_F(hi, 0), HALF_F(hi, 1)), s1);
-        s0 = __ffma2_rn(xp[2 * m + 1], make_float2(HALF_F(lo, 2), HALF_F(lo, 3)), s0);
-        s1 = __ffma2_rn(xp[9 + 2 * m], make_float2(HALF_F(hi, 2), HALF_F(hi, 3)), s1);
+        const uint32_t lo = q & 0x0F0F0F0Fu;  // elements 4m..4m+3
+        const uint32_t hi = q & 0xF0F0F0F0u;  // 16 x elements 16+4m..16+4m+3
+        lo0 = dp4a_uu(lo, xf.p[0][m], lo0);
+        lo1 = dp4a_uu(lo, xf.p[1][m], lo1);
+        lo2 = dp4a_us(lo, xf.p[2][m], lo2);
+        hi0 = dp4a_uu(hi, xf.p[0][4 + m], hi0);
+        hi1 = dp4a_uu(hi, xf.p[1][4 + m], hi1);
+        hi2 = dp4a_us(hi, xf.p[2][4 + m], hi2);
     }
-    const float sum = (s0.x + s0.y) + (s1.x + s1.y);
-    return d * fmaf(256.0f, sum, xcorr);
+    // 16 * sum X q per plane (exact int32), combined in fp32
+    const int t0 = lo0 * 16 + hi0, t1 = lo1 * 16 + hi1, t2 = lo2 * 16 + hi2;
+    const float s16 = fmaf((float)t2, 65536.0f, fmaf((float)t1, 256.0f, (float)t0));
+    // sum X (q - 8) = (s16 - 128 * xsum) / 16
+    return d * (xf.scale * 0.0625f) * fmaf(-128.0f, xf.xsum, s16);
 }
 
-// Same for Q8_0: 32 signed bytes; q ^ 0x80 = q + 128 is placed in the mantissa of 2^23,
-// then -(2^23 + 128) restores q exactly.
+// One Q8_0 block: 32 signed bytes, w = q * d.
 __device__ __forceinline__ float q8_0_block_dot(const uint32_t (&w)[9], uint32_t sel, uint32_t dsel,
-                                                const float2 (&xp)[16]) {
+                                                const XFixed& xf) {
     const float d = __half2float(__ushort_as_half((unsigned short)prmt(w[0], 0u, dsel)));
-    const float2 off = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-    float2 s0 = make_float2(0.0f, 0.0f), s1 = make_float2(0.0f, 0.0f);
+    int a0 = 0, a1 = 0, a2 = 0;
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
-        const uint32_t q = prmt(w[m], w[m + 1], sel) ^ 0x80808080u;
-        s0 = __ffma2_rn(xp[2 * m], __fadd2_rn(make_float2(MAGIC_F(q, 0), MAGIC_F(q, 1)), off), s0);
-        s1 = __ffma2_rn(xp[2 * m + 1], __fadd2_rn(make_float2(MAGIC_F(q, 2), MAGIC_F(q, 3)), off), s1);
+        const uint32_t q = prmt(w[m], w[m + 1], sel);  // elements 4m..4m+3
+        a0 = dp4a_su(q, xf.p[0][m], a0);
+        a1 = dp4a_su(q, xf.p[1][m], a1);
+        a2 = dp4a_ss(q, xf.p[2][m], a2);
     }
-    return d * ((s0.x + s0.y) + (s1.x + s1.y));
+    const float s = fmaf((float)a2, 65536.0f, fmaf((float)a1, 256.0f, (float)a0));
+    return d * xf.scale * s;
 }
 
 template <int QT, int NW>
 __device__ __forceinline__ float q_block_dot(const uint32_t (&w)[NW], uint32_t sel, uint32_t dsel,
-                                             const float2 (&xp)[16], float xcorr) {
-    if constexpr (QT == MGPU_Q4_0) return q4_0_block_dot(w, sel, dsel, xp, xcorr);
-    else return q8_0_block_dot(w, sel, dsel, xp);
-}
-
-// Load 32 activations starting at element `k0` as fp32 pairs.
-template <typename XT>
-__device__ __forceinline__ void load_x32(const XT* __restrict__ x, int k0, float2 (&xp)[16]) {
-    if constexpr (sizeof(XT) == 4) {
-        const float4* p = reinterpret_cast<const float4*>(x + k0);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            float4 v = __ldg(p + i);
-            xp[2 * i] = make_float2(v.x, v.y);
-            xp[2 * i + 1] = make_float2(v.z, v.w);
-        }
-    } else {
-        const uint4* p = reinterpret_cast<const uint4*>(x + k0);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            uint4 v = __ldg(p + i);
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                XT lo, hi;
-                uint16_t l16 = (uint16_t)(u[j] & 0xFFFF), h16 = (uint16_t)(u[j] >> 16);
-                memcpy(&lo, &l16, 2);
-                memcpy(&hi, &h16, 2);
-                xp[4 * i + j] = make_float2(to_f32<XT>(lo), to_f32<XT>(hi));
-            }
-        }
-    }
+                                             const XFixed& xf) {
+    if constexpr (QT == MGPU_Q4_0) return q4_0_block_dot(w, sel, dsel, xf);
+    else return q8_0_block_dot(w, sel, dsel, xf);
 }
 
 // Transposing butterfly: v[0..R) per lane in, the 32-lane sum of row `row` out, where lanes
@@ -154,6 +246,7 @@ struct GemvQArgs {
     int nb;             // blocks per row (K / 32); 32 <= nb <= 256, nb % 32 == 0
     uint32_t row_bytes; // nb * block bytes, a multiple of 16
     uint32_t stage_stride;
+    int chunks_per_flush;  // chunks whose row partials are buffered before one reduction
     int* status;
 };
 
@@ -164,7 +257,6 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[kGemvStages];
     __shared__ __align__(8) uint64_t empty_bar[kGemvStages];
-    __shared__ float wsum[2][8][RPT];
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -215,18 +307,22 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     // ---- consumers ----
     // x (and y) may belong to the preceding kernel of the stream: wait for it to complete.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int K = nb * 32;
+    uint32_t* planes = reinterpret_cast<uint32_t*>(smem + (size_t)kGemvStages * a.stage_stride);
+    float* bscale = reinterpret_cast<float*>(planes + 3 * (K / 4));
+    float* bsum = bscale + nb;
+    prepare_x<XT>(reinterpret_cast<const XT*>(a.x), K, planes, bscale, bsum, tid, kConsumerThreads);
+    named_barrier_sync(1, kConsumerThreads);
     const int col = tid % nb;  // block column owned by this thread for the whole launch
-    float2 xp[16];
-    load_x32<XT>(reinterpret_cast<const XT*>(a.x), col * 32, xp);
-    float xsum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) xsum += xp[i].x + xp[i].y;
-    const float xcorr = -136.0f * xsum;
+    XFixed xf;
+    load_xfixed(planes, bscale, bsum, K / 4, col, xf);
     const uint32_t par = (uint32_t)(tid * BB) & 3u;  // block starts at byte 0 or 2 of a word
     const uint32_t sel = par ? 0x7654u : 0x5432u;
     const uint32_t dsel = par ? 0x4432u : 0x4410u;
     const uint32_t toff = (uint32_t)(tid * BB) - par;
     const int wpr = nb >> 5;  // warps per row slot
+    const int slot = tid / nb;
+    float* part = bsum + nb;  // chunks_per_flush * TR * wpr floats
     YT* __restrict__ y = reinterpret_cast<YT*>(a.y);
 
     for (int c = 0; c < nchunks; ++c) {
@@ -241,21 +337,27 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
             uint32_t w[NW];
 #pragma unroll
             for (int q = 0; q < NW; ++q) w[q] = wp[q];
-            acc[i] = q_block_dot<QT, NW>(w, sel, dsel, xp, xcorr);
+            acc[i] = q_block_dot<QT, NW>(w, sel, dsel, xf);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[s]);
 
+        // Per-warp row partials go to shared memory; rows are reduced across the warps of
+        // their slot and written out once per flush (two barriers per flush, not per chunk).
         int ri;
         const float v = warp_reduce_rows<RPT>(acc, lane, ri);
-        if ((lane & ((32 / RPT) - 1)) == 0) wsum[c & 1][warp][ri] = v;
-        named_barrier_sync(1, kConsumerThreads);
-        if (tid < TR) {
-            const int slot = tid % RP, i = tid / RP;
-            float sum = 0.0f;
-            for (int w = slot * wpr; w < (slot + 1) * wpr; ++w) sum += wsum[c & 1][w][i];
-            const int row = r0 + c * TR + tid;
-            if (row < r1) y[row] = from_f32<YT>(sum);
+        const int cf = c % a.chunks_per_flush;
+        if ((lane & ((32 / RPT) - 1)) == 0) part[(cf * TR + slot + RP * ri) * wpr + (warp % wpr)] = v;
+        if (cf == a.chunks_per_flush - 1 || c == nchunks - 1) {
+            named_barrier_sync(1, kConsumerThreads);
+            const int row0 = r0 + (c - cf) * TR;
+            const int nrows = min((cf + 1) * TR, r1 - row0);
+            for (int r = tid; r < nrows; r += kConsumerThreads) {
+                float sum = 0.0f;
+                for (int w = 0; w < wpr; ++w) sum += part[r * wpr + w];
+                y[row0 + r] = from_f32<YT>(sum);
+            }
+            named_barrier_sync(1, kConsumerThreads);
         }
     }
 }
@@ -447,11 +549,22 @@ struct GemvQLaunch {
             const int RP = kConsumerThreads / nb;
             const int G = max(1, min(c.sm_count * kGemvCtasPerSm, (N + RP - 1) / RP));
             const int rows_per_cta = (N + G - 1) / G;
-            // Largest rows-per-thread (8,4,2,1) whose chunk fits the CTA's share and the ring.
-            int rpt = 8;
-            while (rpt > 1 && (RP * rpt > rows_per_cta ||
-                               (size_t)kGemvStages * RP * rpt * row_bytes > kGemvSmemBudget))
-                rpt >>= 1;
+            // Rows per thread (8, 4, 2, 1): the smallest that covers the CTA's share in one chunk,
+            // capped by the ring's share of the shared-memory budget.  Row partials of up to
+            // kPartFloats are buffered between flushes.
+            constexpr int kPartFloats = 4096;
+            const int wpr = nb / 32;
+            const size_t x_bytes = (size_t)3 * (K / 4) * 4 + (size_t)2 * nb * 4;
+            auto ring = [&](int r) { return (size_t)kGemvStages * (((size_t)RP * r * row_bytes + 1023) / 1024 * 1024); };
+            auto part_floats = [&](int r) {
+                const int tr = RP * r;
+                const int chunks = (rows_per_cta + tr - 1) / tr;
+                const int cpf = max(1, min(chunks, kPartFloats / (tr * wpr)));
+                return (size_t)cpf * tr * wpr;
+            };
+            int rpt = 1;
+            while (rpt < 8 && RP * rpt < rows_per_cta) rpt <<= 1;
+            while (rpt > 1 && ring(rpt) + x_bytes + 4 * part_floats(rpt) > kGemvSmemBudget) rpt >>= 1;
             GemvQArgs a;
             a.W = W;
             a.x = x;
@@ -460,8 +573,9 @@ struct GemvQLaunch {
             a.nb = nb;
             a.row_bytes = (uint32_t)row_bytes;
             a.stage_stride = (uint32_t)((RP * rpt * row_bytes + 1023) / 1024 * 1024);
+            a.chunks_per_flush = (int)(part_floats(rpt) / ((size_t)RP * rpt * wpr));
             a.status = c.status;
-            const size_t smem = (size_t)kGemvStages * a.stage_stride;
+            const size_t smem = (size_t)kGemvStages * a.stage_stride + x_bytes + 4 * part_floats(rpt);
             switch (rpt) {
                 case 8: return launch<8, XT, YT>(c, a, G, smem);
                 case 4: return launch<4, XT, YT>(c, a, G, smem);
@@ -472,8 +586,22 @@ struct GemvQLaunch {
         template <int RPT, typename XT2, typename YT2>
         static cudaError_t launch(const mgpu_k::LaunchCtx& c, const GemvQArgs& a, int G, size_t smem) {
             auto kern = gemv_q_stream<QT, RPT, XT2, YT2>;
-            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
+            // Every instantiation asks for the largest shared-memory carve-out, so that
+            // back-to-back GEMVs of different shapes never force an L1 / shared-memory
+            // reconfiguration between them (which would also stop their CTAs from
+            // overlapping under programmatic dependent launch).
+            static thread_local uint64_t configured = 0;  // one bit per device ordinal
+            int ordinal = 0;
+            cudaGetDevice(&ordinal);
+            if (!(configured & (1ull << (ordinal & 63)))) {
+                cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     (int)kGemvSmemBudget);
+                if (e != cudaSuccess) return e;
+                e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (int)cudaSharedmemCarveoutMaxShared);
+                if (e != cudaSuccess) return e;
+                configured |= 1ull << (ordinal & 63);
+            }
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(G);
             cfg.blockDim = dim3(kGemvThreads);
@@ -483,7 +611,11 @@ struct GemvQLaunch {
             attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
             attr[0].val.programmaticStreamSerializationAllowed = 1;
             cfg.attrs = attr;
+#ifdef MGPU_GEMV_NO_PDL
+            cfg.numAttrs = 0;
+#else
             cfg.numAttrs = 1;
+#endif
             return cudaLaunchKernelEx(&cfg, kern, a);
         }
     };
