@@ -151,6 +151,22 @@ mgpu_event* mgpu_dispatch_vision_proj(const mgpu_device* dev, mgpu_program progr
                                       mgpu_buf* proj_bias, mgpu_buf* output, int num_patches,
                                       int vision_dim, int llm_dim);
 
+/* No counterpart in the reference.  The same GEMV as mgpu_dispatch_gemv for a dense W stored
+ * [K][N] (f32 / f16 / bf16, the reference kernels' orientation), for callers that cannot let
+ * this library allocate device memory: engines that hand the whole GPU memory to their own
+ * pool at start-up (a cudaMalloc here would fail or fragment it), and decode loops that must
+ * not stall (mgpu_dispatch_gemv grows its scratch with cudaMalloc/cudaFree the first time it
+ * sees a larger shape, and cudaFree waits for the whole device).  The split-K scratch of this
+ * entry point is a fixed array of 1 MiB + 16 KiB that every GPU which loads this library holds
+ * until the process exits; N is limited to 262144 (larger N is rejected with
+ * MGPU_ERR_INVALID_ARG before anything is enqueued).  No cudaMalloc or cudaFree is called and
+ * no event is recorded (the return value is the status).  The first call on a device looks
+ * up the array's address on that device, which can load this library's device code there;
+ * make that first call before any stream capture.  All calls share the one array, so calls
+ * whose kernels overlap on the GPU (several streams, or several host threads on one device)
+ * race: serialise them on one stream. */
+int mgpu_dispatch_gemv_noalloc(const mgpu_device* dev, mgpu_buf* x, mgpu_buf* W_img, mgpu_buf* y, int N, int K);
+
 /* New (no reference counterpart: the reference has no quantised kernels, README.md:57).
  * y[1,N] = x[1,K] * dequant(W)^T with W packed GGUF blocks [N][K/32] of `type`. */
 mgpu_event* mgpu_gemv_q(const mgpu_device* dev, mgpu_buf* x, mgpu_buf* W, mgpu_buf* y, int N, int K,

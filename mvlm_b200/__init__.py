@@ -65,6 +65,7 @@ SIGNATURES = {
     "mgpu_dispatch_gemv": (_vp, [_vp, _vp, _vp, _vp, _vp, _i, _i]),
     "mgpu_dispatch_patch_embed": (_vp, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i]),
     "mgpu_dispatch_vision_proj": (_vp, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
+    "mgpu_dispatch_gemv_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i]),
     "mgpu_gemv_q": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i]),
     "mgpu_gemm_q": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "mgpu_gemm": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
@@ -372,6 +373,12 @@ def dispatch_vision_proj(dev: Device, program, visual_tokens: Buffer, proj_weigh
                          llm_dim: int) -> Event:
     return _ev(lib().mgpu_dispatch_vision_proj(dev.h, None, visual_tokens.h, proj_weight.h, _h(proj_bias), output.h,
                                                num_patches, vision_dim, llm_dim), "dispatch_vision_proj")
+
+
+def dispatch_gemv_noalloc(dev: Device, x: Buffer, W_img: Buffer, y: Buffer, N: int, K: int) -> None:
+    """mgpu_dispatch_gemv_noalloc: the [K][N] GEMV with its scratch in a fixed device array of
+    the library (no allocation; N <= 262144; calls that overlap on the GPU race)."""
+    _check(lib().mgpu_dispatch_gemv_noalloc(dev.h, x.h, W_img.h, y.h, N, K), "dispatch_gemv_noalloc")
 
 
 def gemv_q(dev: Device, x: Buffer, W: Buffer, y: Buffer, N: int, K: int, qtype: int) -> Event:

@@ -18,6 +18,8 @@
 //   across CTAs; fp32 partials go to scratch and the last CTA of each column tile sums them
 //   in split order, so the result is deterministic.
 // gemv_q_generic: any K that is a multiple of 32 (row starts need not be 16-byte aligned).
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -657,6 +659,14 @@ struct GemvKnLaunch {
     };
 };
 
+// Fixed scratch of gemv_kn_noalloc: split-K tickets (kNoAllocTickets x u32) followed by the
+// fp32 partials (kNoAllocPartials floats).  One copy per GPU that loads this library, kept
+// until the process exits; every call shares it.
+constexpr int kNoAllocTickets = 4096;            // column tiles of 256 -> N <= 1,048,576
+constexpr size_t kNoAllocPartials = 256 * 1024;  // splits * N <= 262,144 (1 MiB)
+constexpr size_t kNoAllocBytes = kNoAllocTickets * sizeof(unsigned int) + kNoAllocPartials * sizeof(float);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
 }  // namespace
 
 namespace mgpu_k {
@@ -680,6 +690,73 @@ cudaError_t gemv_nk(const LaunchCtx& c, int wtype, const void* W, int64_t ldw, i
         case MGPU_BF16: return dispatch_xy<GemvNkLaunch<__nv_bfloat16>::F>(xtype, ytype, c, W, ldw, x, y, N, K);
         default: return cudaErrorInvalidValue;
     }
+}
+
+size_t gemv_kn_noalloc_max_n() { return kNoAllocPartials; }
+
+cudaError_t gemv_kn_noalloc(const LaunchCtx& c, int wtype, const void* W, int64_t ldw, int xtype, const void* x,
+                            int ytype, void* y, int N, int K) {
+    if (N <= 0 || (size_t)N > kNoAllocPartials || (N + kKnCols - 1) / kKnCols > kNoAllocTickets)
+        return cudaErrorInvalidValue;
+    // The array's device address, looked up once per device with that device current.
+    static void* addr[64] = {};
+    static std::mutex mu;
+    int ordinal = 0;
+    cudaError_t e = cudaGetDevice(&ordinal);
+    if (e != cudaSuccess) return e;
+    if (ordinal < 0 || ordinal >= 64) return cudaErrorInvalidDevice;
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!addr[ordinal]) {
+            e = cudaGetSymbolAddress(&addr[ordinal], g_noalloc_scratch);
+            if (e != cudaSuccess) {
+                addr[ordinal] = nullptr;
+                return e;
+            }
+        }
+        base = addr[ordinal];
+    }
+    unsigned int* tickets = reinterpret_cast<unsigned int*>(base);
+    float* partials = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(base) +
+                                               kNoAllocTickets * sizeof(unsigned int));
+    int splits = 1;
+    gemv_kn_scratch_bytes(N, K, c.sm_count, &splits);
+    splits = max(1, min(splits, (int)(kNoAllocPartials / (size_t)N)));
+    const int col_tiles = (N + kKnCols - 1) / kKnCols;
+    // The tickets must start at zero; a previous call leaves them zero, but an aborted one
+    // might not, so clear them (an async memset: no allocation).
+    e = cudaMemsetAsync(tickets, 0, (size_t)col_tiles * sizeof(unsigned int), c.stream);
+    if (e != cudaSuccess) return e;
+    const int kchunk = (K + splits - 1) / splits;
+    dim3 grid(col_tiles, splits);
+#define MGPU_NA_LAUNCH(WT, XT, YT) \
+    gemv_kn_split<WT, XT, YT><<<grid, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x, (YT*)y, N, K, kchunk, \
+                                                          partials, tickets)
+#define MGPU_NA_Y(WT, XT)                                                 \
+    switch (ytype) {                                                      \
+        case MGPU_F32: MGPU_NA_LAUNCH(WT, XT, float); break;              \
+        case MGPU_F16: MGPU_NA_LAUNCH(WT, XT, __half); break;             \
+        case MGPU_BF16: MGPU_NA_LAUNCH(WT, XT, __nv_bfloat16); break;     \
+        default: return cudaErrorInvalidValue;                            \
+    }
+#define MGPU_NA_X(WT)                                    \
+    switch (xtype) {                                     \
+        case MGPU_F32: MGPU_NA_Y(WT, float) break;       \
+        case MGPU_F16: MGPU_NA_Y(WT, __half) break;      \
+        case MGPU_BF16: MGPU_NA_Y(WT, __nv_bfloat16) break; \
+        default: return cudaErrorInvalidValue;           \
+    }
+    switch (wtype) {
+        case MGPU_F32: MGPU_NA_X(float) break;
+        case MGPU_F16: MGPU_NA_X(__half) break;
+        case MGPU_BF16: MGPU_NA_X(__nv_bfloat16) break;
+        default: return cudaErrorInvalidValue;
+    }
+#undef MGPU_NA_X
+#undef MGPU_NA_Y
+#undef MGPU_NA_LAUNCH
+    return cudaGetLastError();
 }
 
 size_t gemv_kn_scratch_bytes(int N, int K, int sm_count, int* splits_out) {

@@ -26,6 +26,11 @@ cudaError_t gemv_nk(const LaunchCtx& c, int wtype, const void* W, int64_t ldw, i
 cudaError_t gemv_kn(const LaunchCtx& c, int wtype, const void* W, int64_t ldw, int xtype, const void* x,
                     int ytype, void* y, int N, int K, float* partials, unsigned int* counters);
 size_t gemv_kn_scratch_bytes(int N, int K, int sm_count, int* splits_out);
+// Same as gemv_kn, with its scratch in a fixed device array of this library (no allocation).
+// N <= gemv_kn_noalloc_max_n(); otherwise cudaErrorInvalidValue before any launch.
+cudaError_t gemv_kn_noalloc(const LaunchCtx& c, int wtype, const void* W, int64_t ldw, int xtype, const void* x,
+                            int ytype, void* y, int N, int K);
+size_t gemv_kn_noalloc_max_n();
 
 // ---------------------------------------------------------------- misc (misc.cu) ----
 cudaError_t dequant(const LaunchCtx& c, int qtype, const uint8_t* W, int otype, void* out, int64_t n);

@@ -612,6 +612,34 @@ mgpu_event* mgpu_dispatch_gemv(const mgpu_device* cd, mgpu_program, mgpu_buf* x,
     return event_end(d, ev);
 }
 
+int mgpu_dispatch_gemv_noalloc(const mgpu_device* cd, mgpu_buf* x, mgpu_buf* W, mgpu_buf* y, int N, int K) {
+    t_err = MGPU_OK;
+    t_msg[0] = 0;
+    auto fail = [](const char* fmt, auto... args) {
+        set_error(MGPU_ERR_INVALID_ARG, fmt, args...);
+        return (int)MGPU_ERR_INVALID_ARG;
+    };
+    if (!cd || !x || !W || !y) return fail("mgpu_dispatch_gemv_noalloc: null argument");
+    if (N <= 0 || K <= 0) return fail("mgpu_dispatch_gemv_noalloc: N=%d K=%d must be positive", N, K);
+    if ((size_t)N > mgpu_k::gemv_kn_noalloc_max_n())
+        return fail("mgpu_dispatch_gemv_noalloc: N=%d exceeds the fixed scratch limit N <= %zu", N,
+                    mgpu_k::gemv_kn_noalloc_max_n());
+    if (!is_float_type(W->type) || W->layout != MGPU_LAYOUT_KN)
+        return fail("mgpu_dispatch_gemv_noalloc: W must be dense f32/f16/bf16 stored [K][N]");
+    if (!is_float_type(x->type) || !is_float_type(y->type))
+        return fail("mgpu_dispatch_gemv_noalloc: x and y must be f32/f16/bf16");
+    const int64_t ld = ld_or(W, N);
+    if (ld < N || W->bytes < ((size_t)(K - 1) * ld + N) * elem_size(W->type))
+        return fail("mgpu_dispatch_gemv_noalloc: W too small for K=%d N=%d", K, N);
+    if (x->bytes < (size_t)K * elem_size(x->type)) return fail("mgpu_dispatch_gemv_noalloc: x holds fewer than K=%d values", K);
+    if (y->bytes < (size_t)N * elem_size(y->type)) return fail("mgpu_dispatch_gemv_noalloc: y holds fewer than N=%d values", N);
+    DeviceGuard g(cd->ordinal);
+    if (!cuda_ok(mgpu_k::gemv_kn_noalloc(ctx_of(cd), W->type, W->ptr, ld, x->type, x->ptr, y->type, y->ptr, N, K),
+                 "mgpu_dispatch_gemv_noalloc"))
+        return t_err;
+    return MGPU_OK;
+}
+
 mgpu_event* mgpu_gemv_q(const mgpu_device* d, mgpu_buf* x, mgpu_buf* W, mgpu_buf* y, int N, int K, int type) {
     API_ENTRY();
     REQUIRE(W && is_quant_type(type), "mgpu_gemv_q: type must be Q4_0 or Q8_0");
