@@ -12,8 +12,10 @@ from HBM.  The step is captured once as a CUDA graph through the library's captu
 value   = algorithmic bytes of a step (packed weights + x + y) / device time per step, GB/s.
 e2e     = the same metric through the public C ABI with host buffers: every step copies the
           activations host->device and the outputs device->host.
-roofline: the lm_head launch (the largest launch of the dominant kernel, gemv_q_stream),
-          timed by marker events captured inside the graph, against the measured HBM peak.
+roofline: the dominant kernel is gemv_q_stream: every one of the 97 launches of a step, back to
+          back; achieved = average algorithmic bytes per launch / average launch duration over
+          the timed region (CUDA events), against the measured HBM peak.  The lm_head launch
+          alone is also reported (marker events captured around it inside the graph).
 cpu_baseline: the CPU restatement of the reference's quantised path (dequantise + fp32 dot),
           OpenMP over all host cores, on a bounded sample of the same workload.
 prefill : secondary metric: tcgen05 GEMM TFLOP/s on the Phi-1.5 prefill shapes (M=761, Q8_0
@@ -298,10 +300,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                    "l2": "inputs larger than L2: 738 MB of packed weights per step vs 126 MB L2",
                    "parallelism": f"lm_head column-shard x{world} + NCCL all-gather; layers replicated"
                    if world > 1 else "single GPU", "seed": SEED, "prng": "SplitMix64 + Box-Muller (device)"},
-        "roofline": {"bound": "hbm", "kernel": "gemv_q_stream (lm_head launch)", "achieved": round(achieved, 1),
-                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "traffic": None, "bytes_per_launch": head_bytes, "launch_ms": round(head_ms, 5),
-                     "peak_source": peaks["source"]},
+        "roofline": {"bound": "hbm", "kernel": "gemv_q_stream", "launches_per_step": launches_per_step,
+                     "achieved": round(value, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(value / peaks["hbm_gbs"], 4), "traffic": None,
+                     "avg_launch_us": round(ms * 1e3 / launches_per_step, 3),
+                     "bytes_per_launch_avg": step_bytes // launches_per_step, "peak_source": peaks["source"],
+                     "basis": "every launch in the timed region is gemv_q_stream, back to back: average "
+                              "algorithmic bytes per launch / average launch duration (CUDA events)"},
+        "lm_head_launch": {"gbs": round(achieved, 1), "frac": round(achieved / peaks["hbm_gbs"], 4),
+                           "bytes": head_bytes, "ms": round(head_ms, 5),
+                           "basis": "marker events captured around the lm_head launch inside the graph"},
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,

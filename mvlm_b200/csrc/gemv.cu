@@ -30,7 +30,7 @@ namespace {
 constexpr int kConsumerThreads = 256;
 constexpr int kGemvThreads = kConsumerThreads + 32;
 constexpr int kGemvStages = 4;
-constexpr int kGemvCtasPerSm = 2;
+constexpr int kGemvCtasPerSm = 2;                 // at most; see the launcher
 constexpr uint32_t kGemvSmemBudget = 100 * 1024;  // per CTA: two CTAs share an SM
 
 template <int QT> struct QTraits;
@@ -549,7 +549,14 @@ struct GemvQLaunch {
                 return cudaGetLastError();
             }
             const int RP = kConsumerThreads / nb;
-            const int G = max(1, min(c.sm_count * kGemvCtasPerSm, (N + RP - 1) / RP));
+            // Layer-sized GEMVs take one CTA per SM: a launch then leaves room on every SM for
+            // one CTA of the next GEMV in the stream, which under programmatic dependent launch
+            // becomes resident early and streams its weights while this one finishes.  Large
+            // ones (more than kBigRows rows per SM, e.g. the lm_head) take two per SM: twice the
+            // warps and bytes in flight matter more there than the overlap.
+            constexpr int kBigRows = 64;
+            const int per_sm = N > c.sm_count * kBigRows ? kGemvCtasPerSm : 1;
+            const int G = max(1, min(c.sm_count * per_sm, (N + RP - 1) / RP));
             const int rows_per_cta = (N + G - 1) / G;
             // Rows per thread (8, 4, 2, 1): the smallest that covers the CTA's share in one chunk,
             // capped by the ring's share of the shared-memory budget.  Row partials of up to
