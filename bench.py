@@ -167,8 +167,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     peaks = measured_peaks()
 
     # ---------------- weights: generated and quantised on the device ----------------
-    head_rows = [HEAD[2] * r // world for r in range(world + 1)]
-    n_head = head_rows[rank + 1] - head_rows[rank]
+    from mvlm_b200.shard import column_shard, gather_columns
+    h0, h1 = column_shard(HEAD[2], world, rank)
+    n_head = h1 - h0
+    head_rows = [column_shard(HEAD[2], world, r)[0] for r in range(world)] + [HEAD[2]]
     max_el = max(max(K * N for _, K, N in LAYER_SHAPES), HEAD[1] * n_head)
     tmp = dev.empty(max_el, mg.F32)
 
@@ -218,14 +220,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     head0, head1 = enqueue_step()
     graph = dev.capture_end()
 
-    shard_sizes = [head_rows[i + 1] - head_rows[i] for i in range(world)]
-    even = len(set(shard_sizes)) == 1
-
     def gather_logits():
-        if even:
+        # one NCCL all-gather of the logit shards over NVLink (all_gather_into_tensor when the
+        # shards are equal, as for 51200 / {1,2,4,8})
+        if HEAD[2] % world == 0:
             dist.all_gather_into_tensor(y_full, y_shard_t)
         else:
-            dist.all_gather(list(y_full.split(shard_sizes)), y_shard_t)
+            y_full.copy_(gather_columns(y_shard_t, HEAD[2]))
 
     def step():
         graph.launch()
@@ -271,8 +272,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         ms, head_ms = float(t[0]), float(t[1])
 
     # ---------------- e2e through the C ABI with host buffers ----------------
-    e2e = run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, dist, y_full, y_shard_t,
-                  head_rows, torch, stream)
+    e2e = run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, dist, gather_logits, torch,
+                  stream)
 
     # ---------------- prefill GEMMs (secondary metric) ----------------
     prefill = run_prefill(dev, mg, torch, stream, peaks) if rank == 0 and not args.no_prefill else None
@@ -321,8 +322,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     return line
 
 
-def run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, dist, y_full, y_shard_t, head_rows,
-            torch, stream) -> dict:
+def run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, dist, gather_logits, torch,
+            stream) -> dict:
     """Public-API loop with pinned host buffers: per step every activation vector goes
     host->device and every output device->host; dispatches through mgpu_gemv_q."""
     L = mg.lib()
@@ -350,7 +351,7 @@ def run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, d
                 L.mgpu_buf_read_async(y.h, 0, hy + off, N * 4)
                 off += N * 4
             if world > 1:
-                dist.all_gather_into_tensor(y_full, y_shard_t)
+                gather_logits()
 
         steps = max(3, min(args.steps, 200))
         for _ in range(3):

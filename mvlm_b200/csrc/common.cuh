@@ -1,5 +1,5 @@
 // common.cuh - sm_100a device helpers shared by the mvlm_b200 kernels: bounded mbarrier
-// waits, bulk / tensor (TMA) copies without multicast, tcgen05 (TMEM + UMMA) wrappers and
+// waits, bulk / tensor (TMA) copies (CTA-local destinations only), tcgen05 (TMEM + UMMA) wrappers and
 // element conversions.  Every wait on a barrier is bounded by a %globaltimer deadline; on
 // expiry the kernel records MGPU_ERR_DEVICE_TIMEOUT in the per-device status word and
 // returns instead of spinning.
@@ -71,7 +71,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 
 // ------------------------------------------------------------------ copies ----------
 // 1-D bulk copy global -> shared, completion signalled on `bar` (complete_tx).  src, dst
-// 16-byte aligned; bytes a multiple of 16.  No multicast.
+// 16-byte aligned; bytes a multiple of 16.  The destination is this CTA's own shared memory.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -79,7 +79,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
-// 2-D tensor-map (TMA) tile load, no multicast.  x is the innermost coordinate.
+// 2-D tensor-map (TMA) tile load into this CTA's shared memory.  x is the innermost coordinate.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

@@ -19,7 +19,7 @@
 //               operand type and write them into the stage in the same 128B-swizzled
 //               K-major layout TMA would have produced, then fence.proxy.async + arrive.
 // B layouts: NK (K-major, e.g. GGUF F16 tensors) and KN (MN-major: the reference kernels'
-// B[K][N], read by tcgen05 with the B-transpose bit).  No cluster multicast anywhere.
+// B[K][N], read by tcgen05 with the B-transpose bit).  Every TMA load fills only the issuing CTA.
 #include <mutex>
 #include <type_traits>
 

@@ -1,0 +1,61 @@
+"""Host-side partitioning for running the matmul path on several GPUs of one node.
+
+One process per GPU (torchrun), ``torch.distributed`` for the plumbing (NCCL over NVLink on
+the GPUs; gloo works the same way on CPU tensors, which is how the logic is tested).
+
+- Column sharding (lm_head N=51200, fc1 N=8192): in the GGUF [N][K] layout an output column
+  is a weight row, so rank r owns the contiguous row range ``column_shard(N, world, r)`` of W
+  (a plain byte range of the packed blocks: no repacking) and produces those outputs; the
+  full vector is rebuilt with one all-gather.
+- Batch sharding (SigLIP images, decode sequences): rank r owns ``batch_shard(B, world, r)``;
+  the work is independent and needs no exchange.
+"""
+from __future__ import annotations
+
+
+def column_shard(n: int, world: int, rank: int) -> tuple[int, int]:
+    """[start, stop) of the n output columns (= GGUF weight rows) owned by `rank`.  The first
+    n % world ranks get one extra column, so shard sizes differ by at most one."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    base, extra = divmod(n, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def shard_sizes(n: int, world: int) -> list[int]:
+    return [b - a for a, b in (column_shard(n, world, r) for r in range(world))]
+
+
+def batch_shard(b: int, world: int, rank: int) -> tuple[int, int]:
+    """[start, stop) of the b independent items (images, sequences) owned by `rank`."""
+    return column_shard(b, world, rank)
+
+
+def weight_row_bytes_range(n: int, row_bytes: int, world: int, rank: int) -> tuple[int, int]:
+    """Byte range of rank's rows inside a packed [N][row_bytes] weight."""
+    a, b = column_shard(n, world, rank)
+    return a * row_bytes, b * row_bytes
+
+
+def gather_columns(local, n: int, group=None):
+    """All-gather the ranks' column shards (1-D tensors) into the full length-n vector, in
+    rank order.  Uses the single-buffer collective when the shards are equal."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    sizes = shard_sizes(n, world)
+    if local.numel() != sizes[dist.get_rank(group)]:
+        raise ValueError(f"local shard has {local.numel()} values, expected {sizes[dist.get_rank(group)]}")
+    width = max(sizes)
+    if len(set(sizes)) == 1:
+        out = torch.empty(n, dtype=local.dtype, device=local.device)
+        dist.all_gather(list(out.split(sizes)), local.contiguous(), group=group)
+        return out
+    # Unequal shards (n % world != 0): pad every shard to the widest, gather, then trim.
+    padded = torch.zeros(width, dtype=local.dtype, device=local.device)
+    padded[: local.numel()] = local
+    slots = torch.empty(world * width, dtype=local.dtype, device=local.device)
+    dist.all_gather(list(slots.split(width)), padded, group=group)
+    return torch.cat([slots[r * width: r * width + sizes[r]] for r in range(world)])
