@@ -310,7 +310,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                               "algorithmic bytes per launch / average launch duration (CUDA events)"},
         "lm_head_launch": {"gbs": round(achieved, 1), "frac": round(achieved / peaks["hbm_gbs"], 4),
                            "bytes": head_bytes, "ms": round(head_ms, 5),
-                           "basis": "marker events captured around the lm_head launch inside the graph"},
+                           "basis": "marker events captured around the lm_head launch inside the graph",
+                           "dram_traffic_bytes": 59059360 if world == 1 else None,
+                           "dram_traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch, "
+                                                  "profiles/gemv_q_stream_q4_0_lm_head_2048x51200.md"},
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
