@@ -381,17 +381,24 @@ def run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, d
 
 def run_prefill(dev, mg, torch, stream, peaks) -> dict:
     """tcgen05 GEMM on the Phi-1.5 prefill shapes: M=761, bf16 A, Q8_0 W (dequantised to bf16
-    tiles inside the kernel), fp32 accumulate, bf16 C.  Rotates 4 weight copies per shape."""
+    tiles inside the kernel), fp32 accumulate, bf16 C.  Rotates enough weight copies per shape
+    that each pass over them is about 2x the L2.
+    The kernels are timed as a captured graph of one launch per copy (at least 40), which is
+    what an engine replaying its prefill graph sees; `eager_tflops` is the same loop dispatched
+    call by call from Python, whose ~8 us of host time per call hides part of the kernel time."""
     out = {}
     tot_flop, tot_ms = 0.0, 0.0
     tmp_el = max(K * N for _, K, N in PREFILL_SHAPES)
     tmp = dev.empty(tmp_el, mg.F32)
     for M, K, N in PREFILL_SHAPES:
+        wbytes = N * (K // 32) * 34
+        ncopy = max(4, -(-256_000_000 // wbytes))
+        iters = max(40, ncopy)
         A = dev.empty(M * K, mg.BF16)
         dev.fill_normal(A, M * K, SEED + K, 1.0)
         Ws = []
-        for c in range(4):
-            w = dev.create_buffer(N * (K // 32) * 34, None, mg.Q8_0, mg.LAYOUT_NK, N, K)
+        for c in range(ncopy):
+            w = dev.create_buffer(wbytes, None, mg.Q8_0, mg.LAYOUT_NK, N, K)
             dev.fill_normal(tmp, N * K, SEED + N + 17 * c, 0.02)
             dev.quantize(tmp, w, N * K, mg.Q8_0)
             Ws.append(w)
@@ -399,22 +406,40 @@ def run_prefill(dev, mg, torch, stream, peaks) -> dict:
         for w in Ws:
             mg.gemm_q(dev, A, w, C, M, N, K, mg.Q8_0)
         torch.cuda.synchronize()
-        iters = 40
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(iters):
-            mg.gemm_q(dev, A, Ws[i % 4], C, M, N, K, mg.Q8_0)
+            mg.gemm_q(dev, A, Ws[i % ncopy], C, M, N, K, mg.Q8_0)
         e1.record(stream)
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / iters
+        ms_eager = e0.elapsed_time(e1) / iters
+        dev.capture_begin()
+        for i in range(iters):
+            mg.gemm_q(dev, A, Ws[i % ncopy], C, M, N, K, mg.Q8_0)
+        graph = dev.capture_end()
+        for _ in range(3):
+            graph.launch()
+        torch.cuda.synchronize()
+        reps = 5
+        e0.record(stream)
+        for _ in range(reps):
+            graph.launch()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del graph
+        ms = e0.elapsed_time(e1) / (reps * iters)
         flop = 2.0 * M * K * N
-        out[f"{K}x{N}"] = {"tflops": round(flop / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2)}
+        out[f"{K}x{N}"] = {"tflops": round(flop / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2),
+                           "eager_tflops": round(flop / (ms_eager * 1e-3) / 1e12, 1), "weight_copies": ncopy}
+        del Ws, A, C
         tot_flop += flop
         tot_ms += ms
     agg = tot_flop / (tot_ms * 1e-3) / 1e12
     return {"unit": "TFLOP/s", "M": 761, "weights": "Q8_0", "activations": "bf16", "shapes": out,
             "aggregate_tflops": round(agg, 1), "frac_of_peak": round(agg / peaks["bf16_tflops"], 4),
-            "peak": peaks["bf16_tflops"], "peak_source": peaks["source"]}
+            "peak": peaks["bf16_tflops"], "peak_source": peaks["source"],
+            "timing": "CUDA events around 5 replays of a captured graph of one launch per weight copy; "
+                      "copies rotated so each pass reads ~256 MB of packed weights (2x L2)"}
 
 
 # --------------------------------------------------------------------------------------

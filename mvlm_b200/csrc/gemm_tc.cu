@@ -20,6 +20,7 @@
 //               K-major layout TMA would have produced, then fence.proxy.async + arrive.
 // B layouts: NK (K-major, e.g. GGUF F16 tensors) and KN (MN-major: the reference kernels'
 // B[K][N], read by tcgen05 with the B-transpose bit).  Every TMA load fills only the issuing CTA.
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -44,14 +45,20 @@ __host__ __device__ constexpr int group_bytes(int m) { return is_q4_mode(m) ? 14
 constexpr int kDqWarps = 8;
 
 __host__ __device__ constexpr int gemm_threads(int bmode) { return 192 + (is_quant_mode(bmode) ? kDqWarps * 32 : 0); }
-__host__ __device__ constexpr int stage_bytes(int bn) { return kABytes + bn * BK * 2; }
+// MT = 128-row M sub-tiles per CTA tile.  With MT = 2 (TMA-staged quantised modes only) a CTA
+// computes a 256 x BN tile as two tcgen05 accumulators that share each decoded B stage, which
+// halves the decode work per FLOP (for M = 761 each weight is decoded 3 times instead of 6);
+// the host picks MT per shape, since 256-row tiles leave SMs idle when there are few of them.
+__host__ __device__ constexpr int stage_bytes(int bn, int mt = 1) { return mt * kABytes + bn * BK * 2; }
 // packed-group ring (two slots) of the TMA-staged quantised modes
 __host__ __device__ constexpr int packed_bytes(int bn, int bmode) { return is_packed_tma(bmode) ? 2 * bn * group_bytes(bmode) : 0; }
-__host__ __device__ constexpr int num_stages(int bn, int bmode = B_TMA_K) {
-    return is_packed_tma(bmode) ? 4 : kSmemBudget / stage_bytes(bn);
+constexpr int kSmemMaxDyn = 226 * 1024;  // dynamic shared memory available next to the static barriers
+__host__ __device__ constexpr int num_stages(int bn, int bmode = B_TMA_K, int mt = 1) {
+    return is_packed_tma(bmode) ? (kSmemMaxDyn - 1024 - packed_bytes(bn, bmode)) / stage_bytes(bn, mt)
+                                : kSmemBudget / stage_bytes(bn, mt);
 }
-__host__ __device__ constexpr int smem_bytes(int bn, int bmode) {
-    return num_stages(bn, bmode) * stage_bytes(bn) + packed_bytes(bn, bmode) + 1024;
+__host__ __device__ constexpr int smem_bytes(int bn, int bmode, int mt = 1) {
+    return num_stages(bn, bmode, mt) * stage_bytes(bn, mt) + packed_bytes(bn, bmode) + 1024;
 }
 
 struct GemmArgs {
@@ -183,12 +190,15 @@ __device__ __forceinline__ void decode_store(const RawBlock<NW>& rb, uint4* cons
     }
 }
 
-template <int BN, int BMODE, typename T>
+template <int BN, int BMODE, typename T, int MT>
 __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
-    constexpr int S = num_stages(BN, BMODE);
-    constexpr int SB = stage_bytes(BN);
-    constexpr uint32_t kTmemCols = 2 * BN;
+    static_assert(MT == 1 || (MT == 2 && BN == 128), "256-row tiles use 128-column B tiles");
+    constexpr int S = num_stages(BN, BMODE, MT);
+    constexpr int SB = stage_bytes(BN, MT);
+    constexpr int TBM = BM * MT;                 // rows of a CTA tile
+    constexpr int AB = MT * kABytes;             // A bytes per stage
+    constexpr uint32_t kTmemCols = 2 * MT * BN;  // double-buffered accumulators
     constexpr bool kQuant = is_quant_mode(BMODE);
     constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
     constexpr uint32_t kIdesc = idesc_f16(kBf16, false, BMODE == B_TMA_MN, BM, BN);
@@ -248,10 +258,12 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                     const uint32_t s = it % S, ph = (it / S) & 1u;
                     if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
                     uint8_t* a_dst = smem + s * SB;
-                    uint8_t* b_dst = a_dst + kABytes;
-                    const uint32_t tx = kABytes + (kQuant ? 0u : (uint32_t)(BN * BK * 2));
+                    uint8_t* b_dst = a_dst + AB;
+                    const uint32_t tx = AB + (kQuant ? 0u : (uint32_t)(BN * BK * 2));
                     mbar_arrive_expect_tx(&full_bar[s], tx);
-                    tma_load_2d(a_dst, &tmA, kb * BK, m_blk * BM, &full_bar[s]);
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt)
+                        tma_load_2d(a_dst + mt * kABytes, &tmA, kb * BK, m_blk * TBM + mt * BM, &full_bar[s]);
                     if constexpr (BMODE == B_TMA_K) {
                         tma_load_2d(b_dst, &tmB, kb * BK, n_blk * BN, &full_bar[s]);
                     } else if constexpr (BMODE == B_TMA_MN) {
@@ -271,22 +283,25 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                 const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
                 if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, g.status)) { abort_flag = 1; break; }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * BN;
+                const uint32_t d_tmem = tmem_base + acc * (MT * BN);
                 for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
                     const uint32_t s = it % S, ph = (it / S) & 1u;
                     if (!mbar_wait(&full_bar[s], ph, g.status)) { abort_flag = 1; break; }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + s * SB);
-                    const uint32_t b_addr = a_addr + kABytes;
+                    const uint32_t b_addr = a_addr + AB;
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
-                        const uint64_t adesc = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
                         uint64_t bdesc;
                         if constexpr (BMODE == B_TMA_MN)
                             bdesc = smem_desc(b_addr + k * 2048, 8192, 1024, kSwizzle128B);
                         else
                             bdesc = smem_desc(b_addr + k * 32, 16, 1024, kSwizzle128B);
-                        umma_f16(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            const uint64_t adesc = smem_desc(a_addr + mt * kABytes + k * 32, 16, 1024, kSwizzle128B);
+                            umma_f16(d_tmem + mt * BN, adesc, bdesc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+                        }
                     }
                     issued = true;
                     umma_commit(&empty_bar[s]);
@@ -310,11 +325,13 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
             if (abort_flag || !mbar_wait(&tfull_bar[acc], acc_ph, g.status)) { abort_flag = 1; break; }
             tc_fence_after();
-            const int row = m_blk * BM + q * 32 + lane;
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 32; ++cc) {
+            for (int cm = 0; cm < MT * (BN / 32); ++cm) {
+            const int mt = cm / (BN / 32), cc = cm % (BN / 32);
+            const int row = m_blk * TBM + mt * BM + q * 32 + lane;
+            {
                 float v[32];
-                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cc * 32, v);
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * (MT * BN) + mt * BN + cc * 32, v);
                 const int n0 = n_blk * BN + cc * 32;
                 if (g.bias) {
 #pragma unroll
@@ -344,6 +361,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                             if (n0 + i < g.N) store_out(g.C, g.c_type, base + i, v[i]);
                     }
                 }
+            }
             }
             tc_fence_before();
             __syncwarp();
@@ -395,7 +413,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                 const uint32_t it = gi * 4 + 2 * h + jj;
                 const uint32_t s = it % S, ph = (it / S) & 1u;
                 if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
-                uint8_t* row_base = smem + s * SB + kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+                uint8_t* row_base = smem + s * SB + AB + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     constexpr int dummy = 0;
@@ -448,7 +466,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         auto decode_stage = [&](RawBlock<NW>(&src)[UPT], uint32_t it) -> bool {
             const uint32_t s = it % S, ph = (it / S) & 1u;
             if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) return false;
-            uint8_t* b_dst = smem + s * SB + kABytes;
+            uint8_t* b_dst = smem + s * SB + AB;
 #pragma unroll
             for (int v = 0; v < UPT; ++v) {
                 const int u = dt + v * kDqWarps * 32;
@@ -536,12 +554,21 @@ bool make_map_plain(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int BMODE, typename T>
+template <int BN, int BMODE, typename T, int MT = 1>
 cudaError_t launch_gemm(const mgpu_k::LaunchCtx& c, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g) {
-    auto kern = gemm_tc_kernel<BN, BMODE, T>;
-    const int smem = smem_bytes(BN, BMODE);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    auto kern = gemm_tc_kernel<BN, BMODE, T, MT>;
+    const int smem = smem_bytes(BN, BMODE, MT);
+    // The shared-memory opt-in is a per-device function attribute: set it once per device.
+    static std::atomic<uint64_t> configured{0};
+    int ordinal = 0;
+    cudaError_t e = cudaGetDevice(&ordinal);
     if (e != cudaSuccess) return e;
+    const uint64_t bit = ordinal < 64 ? (1ull << ordinal) : 0ull;
+    if (!bit || !(configured.load(std::memory_order_acquire) & bit)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        configured.fetch_or(bit, std::memory_order_acq_rel);
+    }
     const int tiles = g.tiles_m * g.tiles_n;
     const int grid = tiles < c.sm_count ? tiles : c.sm_count;
     kern<<<grid, gemm_threads(BMODE), smem, c.stream>>>(ma, mb, g);
@@ -549,7 +576,7 @@ cudaError_t launch_gemm(const mgpu_k::LaunchCtx& c, const CUtensorMap& ma, const
 }
 
 template <int BN, typename T>
-cudaError_t launch_mode(const mgpu_k::LaunchCtx& c, int bmode, const CUtensorMap& ma, const CUtensorMap& mb,
+cudaError_t launch_mode(const mgpu_k::LaunchCtx& c, int bmode, int mt, const CUtensorMap& ma, const CUtensorMap& mb,
                         const GemmArgs& g) {
     switch (bmode) {
         case B_TMA_K: return launch_gemm<BN, B_TMA_K, T>(c, ma, mb, g);
@@ -557,10 +584,12 @@ cudaError_t launch_mode(const mgpu_k::LaunchCtx& c, int bmode, const CUtensorMap
         case B_Q8: return launch_gemm<BN, B_Q8, T>(c, ma, mb, g);
         case B_Q4: return launch_gemm<BN, B_Q4, T>(c, ma, mb, g);
         case B_Q8_TMA:
-            if constexpr (BN == 128) return launch_gemm<BN, B_Q8_TMA, T>(c, ma, mb, g);
+            if constexpr (BN == 128)
+                return mt == 2 ? launch_gemm<BN, B_Q8_TMA, T, 2>(c, ma, mb, g) : launch_gemm<BN, B_Q8_TMA, T, 1>(c, ma, mb, g);
             return cudaErrorInvalidValue;
         default:
-            if constexpr (BN == 128) return launch_gemm<BN, B_Q4_TMA, T>(c, ma, mb, g);
+            if constexpr (BN == 128)
+                return mt == 2 ? launch_gemm<BN, B_Q4_TMA, T, 2>(c, ma, mb, g) : launch_gemm<BN, B_Q4_TMA, T, 1>(c, ma, mb, g);
             return cudaErrorInvalidValue;
     }
 }
@@ -605,14 +634,18 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
     else if (B.type == MGPU_Q4_0) bmode = packed_ok ? B_Q4_TMA : B_Q4;
     else bmode = (B.layout == MGPU_LAYOUT_NK) ? B_TMA_K : B_TMA_MN;
 
-    // Pick BN by the estimated makespan over the SMs (tile time ~ BN + fixed overhead).
-    const int tiles_m = (M + BM - 1) / BM;
-    auto makespan = [&](int bn) {
-        const long tiles = (long)tiles_m * ((N + bn - 1) / bn);
-        const long waves = (tiles + c.sm_count - 1) / c.sm_count;
-        return waves * (bn + 32);
+    // Pick the tile by the estimated makespan over the SMs.  Dense: BN in {128, 256}, tile time
+    // ~ BN + a fixed overhead.  Packed quantised: BN = 128 and 128 or 256 rows; a 256-row tile
+    // decodes its B stages once for twice the MMAs and takes about 1.4x as long as a 128-row
+    // one (measured on M = 761 prefill shapes).
+    auto waves = [&](int bm, int bn) {
+        const long tiles = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
+        return (tiles + c.sm_count - 1) / c.sm_count;
     };
-    const int BN = is_packed_tma(bmode) ? 128 : (makespan(128) < makespan(256) ? 128 : 256);
+    int BN = 128, mt = 1;
+    if (is_packed_tma(bmode)) mt = waves(2 * BM, 128) * 14 < waves(BM, 128) * 10 ? 2 : 1;
+    else BN = waves(BM, 128) * (128 + 32) < waves(BM, 256) * (256 + 32) ? 128 : 256;
+    const int tiles_m = (M + BM * mt - 1) / (BM * mt);
 
     GemmArgs g;
     g.M = M;
@@ -650,8 +683,8 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
     }
     const bool bf16 = A.type == MGPU_BF16;
     if (BN == 256)
-        return bf16 ? launch_mode<256, __nv_bfloat16>(c, bmode, ma, mb, g) : launch_mode<256, __half>(c, bmode, ma, mb, g);
-    return bf16 ? launch_mode<128, __nv_bfloat16>(c, bmode, ma, mb, g) : launch_mode<128, __half>(c, bmode, ma, mb, g);
+        return bf16 ? launch_mode<256, __nv_bfloat16>(c, bmode, mt, ma, mb, g) : launch_mode<256, __half>(c, bmode, mt, ma, mb, g);
+    return bf16 ? launch_mode<128, __nv_bfloat16>(c, bmode, mt, ma, mb, g) : launch_mode<128, __half>(c, bmode, mt, ma, mb, g);
 }
 
 }  // namespace mgpu_k

@@ -52,7 +52,7 @@ def test_prefill_quantised_phi(dev, qt, K, N):
 
 @pytest.mark.parametrize("qt", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("M,N,K", [(8, 2048, 2048), (32, 6144, 2048), (128, 2048, 8192), (5, 100, 96),
-                                   (130, 300, 160)])
+                                   (130, 300, 160), (600, 5000, 512)])
 def test_quantised_ragged_and_batched(dev, qt, M, N, K):
     A = O.bf16(O.normal(M * K, M + N, 1.0))
     W = O.quantize(O.normal(N * K, K, 0.02), qt)
