@@ -2,7 +2,7 @@
 //
 // gemv_q_stream: y = dequant(W) . x for GGUF Q4_0 / Q8_0 weights kept packed in their
 //   [N][K/32] block layout.  Each CTA owns an even share of the rows.  One producer thread
-//   streams the CTA's contiguous byte range from HBM into a 4-stage shared-memory ring with
+//   streams the CTA's contiguous byte range from HBM into a 2..8-stage shared-memory ring with
 //   cp.async.bulk (the 1-D TMA engine, 16-byte granular, no registers held in flight); 8
 //   consumer warps decode the 18 / 34-byte blocks out of shared memory.  Each consumer thread
 //   owns one 32-element block column for the whole launch; its 32 activations are turned
@@ -29,7 +29,7 @@ namespace {
 
 constexpr int kConsumerThreads = 256;
 constexpr int kGemvThreads = kConsumerThreads + 32;
-constexpr int kGemvStages = 4;
+constexpr int kGemvMaxStages = 8;  // ring depth is chosen per shape, up to this
 constexpr int kGemvCtasPerSm = 2;                 // at most; see the launcher
 constexpr uint32_t kGemvSmemBudget = 100 * 1024;  // per CTA: two CTAs share an SM
 
@@ -248,6 +248,7 @@ struct GemvQArgs {
     int nb;             // blocks per row (K / 32); 32 <= nb <= 256, nb % 32 == 0
     uint32_t row_bytes; // nb * block bytes, a multiple of 16
     uint32_t stage_stride;
+    int stages;            // ring depth, 2..kGemvMaxStages
     int chunks_per_flush;  // chunks whose row partials are buffered before one reduction
     int* status;
 };
@@ -257,8 +258,8 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     constexpr int BB = QTraits<QT>::kBlockBytes;
     constexpr int NW = QTraits<QT>::kWords;
     extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full_bar[kGemvStages];
-    __shared__ __align__(8) uint64_t empty_bar[kGemvStages];
+    __shared__ __align__(8) uint64_t full_bar[kGemvMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kGemvMaxStages];
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -271,7 +272,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     const int nchunks = (r1 - r0 + TR - 1) / TR;
 
     if (tid == 0) {
-        for (int s = 0; s < kGemvStages; ++s) {
+        for (int s = 0; s < a.stages; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], kConsumerThreads / 32);
         }
@@ -287,20 +288,23 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
         // Weights are never written by the preceding kernel, so streaming starts before
         // griddepcontrol.wait and overlaps the previous kernel's tail.
         if (lane == 0) {
-            int c = 0;
+            int c = 0, s = 0;
+            uint32_t ph = 0;
             for (; c < nchunks; ++c) {
-                const int s = c % kGemvStages;
-                const uint32_t ph = (uint32_t)(c / kGemvStages) & 1u;
                 if (!mbar_wait(&empty_bar[s], ph ^ 1u, a.status)) break;
                 const int row = r0 + c * TR;
                 const uint32_t bytes = (uint32_t)min(TR, r1 - row) * a.row_bytes;
                 mbar_arrive_expect_tx(&full_bar[s], bytes);
                 bulk_g2s(smem + (size_t)s * a.stage_stride, a.W + (size_t)row * a.row_bytes, bytes, &full_bar[s]);
+                if (++s == a.stages) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
             if (c < nchunks) {
                 // Timed out: let the copies already issued land before the CTA exits.
-                for (int k = max(0, c - kGemvStages); k < c; ++k)
-                    mbar_wait(&full_bar[k % kGemvStages], (uint32_t)(k / kGemvStages) & 1u, nullptr);
+                for (int k = max(0, c - a.stages); k < c; ++k)
+                    mbar_wait(&full_bar[k % a.stages], (uint32_t)(k / a.stages) & 1u, nullptr);
             }
         }
         return;
@@ -310,7 +314,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     // x (and y) may belong to the preceding kernel of the stream: wait for it to complete.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int K = nb * 32;
-    uint32_t* planes = reinterpret_cast<uint32_t*>(smem + (size_t)kGemvStages * a.stage_stride);
+    uint32_t* planes = reinterpret_cast<uint32_t*>(smem + (size_t)a.stages * a.stage_stride);
     float* bscale = reinterpret_cast<float*>(planes + 3 * (K / 4));
     float* bsum = bscale + nb;
     prepare_x<XT>(reinterpret_cast<const XT*>(a.x), K, planes, bscale, bsum, tid, kConsumerThreads);
@@ -327,9 +331,9 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     float* part = bsum + nb;  // chunks_per_flush * TR * wpr floats
     YT* __restrict__ y = reinterpret_cast<YT*>(a.y);
 
+    int s = 0;
+    uint32_t ph = 0;
     for (int c = 0; c < nchunks; ++c) {
-        const int s = c % kGemvStages;
-        const uint32_t ph = (uint32_t)(c / kGemvStages) & 1u;
         if (!mbar_wait(&full_bar[s], ph, a.status)) return;
         const uint8_t* st = smem + (size_t)s * a.stage_stride + toff;
         float acc[RPT];
@@ -343,6 +347,10 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[s]);
+        if (++s == a.stages) {
+            s = 0;
+            ph ^= 1u;
+        }
 
         // Per-warp row partials go to shared memory; rows are reduced across the warps of
         // their slot and written out once per flush (two barriers per flush, not per chunk).
@@ -558,22 +566,53 @@ struct GemvQLaunch {
             const int per_sm = N > c.sm_count * kBigRows ? kGemvCtasPerSm : 1;
             const int G = max(1, min(c.sm_count * per_sm, (N + RP - 1) / RP));
             const int rows_per_cta = (N + G - 1) / G;
-            // Rows per thread (8, 4, 2, 1): the smallest that covers the CTA's share in one chunk,
-            // capped by the ring's share of the shared-memory budget.  Row partials of up to
-            // kPartFloats are buffered between flushes.
+            // Rows per thread (8, 4, 2, 1) and ring depth (2..8 stages).  Layer-sized GEMVs: a
+            // ring that holds all of the CTA's rows, so the weights stream in before
+            // griddepcontrol.wait returns; among those, the widest chunk (more independent rows
+            // per thread) that computes at most 25 % padding rows.  GEMVs too large to prefetch
+            // whole (the lm_head) stream through a 4-stage ring of the widest chunk that fits.
+            // Row partials of up to kPartFloats are buffered between flushes.
             constexpr int kPartFloats = 4096;
             const int wpr = nb / 32;
             const size_t x_bytes = (size_t)3 * (K / 4) * 4 + (size_t)2 * nb * 4;
-            auto ring = [&](int r) { return (size_t)kGemvStages * (((size_t)RP * r * row_bytes + 1023) / 1024 * 1024); };
+            auto stride = [&](int r) { return ((size_t)RP * r * row_bytes + 1023) / 1024 * 1024; };
+            auto chunks_of = [&](int r) { return (rows_per_cta + RP * r - 1) / (RP * r); };
             auto part_floats = [&](int r) {
-                const int tr = RP * r;
-                const int chunks = (rows_per_cta + tr - 1) / tr;
-                const int cpf = max(1, min(chunks, kPartFloats / (tr * wpr)));
-                return (size_t)cpf * tr * wpr;
+                const int cpf = max(1, min(chunks_of(r), kPartFloats / (RP * r * wpr)));
+                return (size_t)cpf * RP * r * wpr;
             };
-            int rpt = 1;
-            while (rpt < 8 && RP * rpt < rows_per_cta) rpt <<= 1;
-            while (rpt > 1 && ring(rpt) + x_bytes + 4 * part_floats(rpt) > kGemvSmemBudget) rpt >>= 1;
+            auto depth = [&](int r, int cap) {
+                const size_t fixed = x_bytes + 4 * part_floats(r);
+                if (fixed + 2 * stride(r) > kGemvSmemBudget) return 0;
+                return max(2, min(cap, min(chunks_of(r), (int)((kGemvSmemBudget - fixed) / stride(r)))));
+            };
+            int rpt = 0, stages = 0;
+            for (int r = 8; r >= 1 && !rpt; r >>= 1) {
+                const int d = depth(r, kGemvMaxStages);
+                const int waste = chunks_of(r) * RP * r - rows_per_cta;
+                if (d && d >= chunks_of(r) && 4 * waste <= rows_per_cta) {
+                    rpt = r;
+                    stages = d;
+                }
+            }
+            for (int r = 8; r >= 1 && !rpt; r >>= 1) {
+                const int d = depth(r, 4);
+                if (d >= min(4, chunks_of(r))) {
+                    rpt = r;
+                    stages = d;
+                }
+            }
+            for (int r = 8; r >= 1 && !rpt; r >>= 1) {
+                const int d = depth(r, 4);
+                if (d) {
+                    rpt = r;
+                    stages = d;
+                }
+            }
+            if (!rpt) {
+                rpt = 1;
+                stages = 2;
+            }
             GemvQArgs a;
             a.W = W;
             a.x = x;
@@ -581,10 +620,11 @@ struct GemvQLaunch {
             a.N = N;
             a.nb = nb;
             a.row_bytes = (uint32_t)row_bytes;
-            a.stage_stride = (uint32_t)((RP * rpt * row_bytes + 1023) / 1024 * 1024);
+            a.stage_stride = (uint32_t)stride(rpt);
+            a.stages = stages;
             a.chunks_per_flush = (int)(part_floats(rpt) / ((size_t)RP * rpt * wpr));
             a.status = c.status;
-            const size_t smem = (size_t)kGemvStages * a.stage_stride + x_bytes + 4 * part_floats(rpt);
+            const size_t smem = (size_t)a.stages * a.stage_stride + x_bytes + 4 * part_floats(rpt);
             switch (rpt) {
                 case 8: return launch<8, XT, YT>(c, a, G, smem);
                 case 4: return launch<4, XT, YT>(c, a, G, smem);
