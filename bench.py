@@ -277,6 +277,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     # ---------------- prefill GEMMs (secondary metric) ----------------
     prefill = run_prefill(dev, mg, torch, stream, peaks) if rank == 0 and not args.no_prefill else None
+    # ---------------- the other BASELINE configs (secondary, one GPU) ----------------
+    secondary = None
+    if rank == 0 and world == 1 and not args.no_secondary:
+        secondary = {"fp32_gemv": run_fp32_gemv(dev, mg, torch, stream, peaks),
+                     "batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head),
+                     "siglip": run_siglip(dev, mg, torch, stream, peaks)}
 
     graph = None
     if world > 1:
@@ -320,6 +326,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     }
     if prefill:
         line["prefill"] = prefill
+    if secondary:
+        line.update(secondary)
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(args.cpu_budget)
     return line
@@ -442,6 +450,127 @@ def run_prefill(dev, mg, torch, stream, peaks) -> dict:
                       "copies rotated so each pass reads ~256 MB of packed weights (2x L2)"}
 
 
+def time_graph(dev, torch, stream, enqueue, reps: int, flush=None) -> float:
+    """Capture enqueue() once as a graph through the library's capture API, replay it twice
+    untimed, then return the mean device time (ms) of `reps` replays, each bracketed by its
+    own CUDA events; `flush` (an L2-sized write) runs before each replay, outside the events."""
+    enqueue()  # eager pass: validates arguments and sizes the workspace outside the capture
+    dev.finish()
+    dev.capture_begin()
+    enqueue()
+    graph = dev.capture_end()
+    for _ in range(2):
+        graph.launch()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for e0, e1 in evs:
+        if flush is not None:
+            flush()
+        e0.record(stream)
+        graph.launch()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    del graph
+    return sum(e0.elapsed_time(e1) for e0, e1 in evs) / reps
+
+
+def run_fp32_gemv(dev, mg, torch, stream, peaks) -> dict:
+    """fp32 GEMV M=1, K=2048, N=8192, x and W [K][N] row-major ~U(-1,1)
+    (the reference orientation), through dispatch_gemv.  Four weight copies (268 MB, > 2x L2)
+    rotate, one launch each per replay."""
+    K, N, copies = 2048, 8192, 4
+    Ws = []
+    for c in range(copies):
+        w = dev.create_buffer(K * N * 4, None, mg.F32, mg.LAYOUT_KN, K, N)
+        dev.fill_uniform(w, K * N, SEED + 300 + c)
+        Ws.append(w)
+    x = dev.empty(K, mg.F32)
+    dev.fill_uniform(x, K, SEED + 301)
+    y = dev.empty(N, mg.F32)
+
+    def enqueue():
+        for w in Ws:
+            mg.dispatch_gemv(dev, None, x, w, y, N, K)
+
+    ms = time_graph(dev, torch, stream, enqueue, 20) / copies
+    nbytes = 4 * K * N + 4 * K + 4 * N
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"shape": f"{K}x{N}", "gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 4), "us": round(ms * 1e3, 2),
+            "bytes": nbytes, "basis": "4 weight copies of 67 MB rotated; algorithmic bytes 4KN+4K+4N per launch"}
+
+
+SIGLIP_LAYER = [(1152, 3456), (1152, 1152), (1152, 4304), (4304, 1152)]  # (K, N) per image token
+SIGLIP_PROJ = [(2304, 8192), (8192, 2048)]
+
+
+def run_siglip(dev, mg, torch, stream, peaks, batches=(1, 8, 64)) -> dict:
+    """SigLIP encoder GEMMs at M = 729 * B with fp16 A ~N(0,1) and fp16
+    weights ~N(0,0.02) in GGUF [N][K] order: one encoder layer (qkv, out, fc1, fc2) plus the
+    projection MLP (2304->8192->2048), fp32 accumulate, fp16 C.  Each replay of the captured
+    sequence follows a 256 MB write that evicts L2."""
+    flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    shapes = SIGLIP_LAYER + SIGLIP_PROJ
+    tmp = dev.empty(max(K * N for K, N in shapes), mg.F32)
+    Ws = []
+    for i, (K, N) in enumerate(shapes):
+        w = dev.create_buffer(N * K * 2, None, mg.F16, mg.LAYOUT_NK, N, K)
+        dev.fill_normal(tmp, N * K, SEED + 400 + i, 0.02)
+        dev.convert(tmp, w, N * K)
+        Ws.append(w)
+    del tmp
+    out = {}
+    for B in batches:
+        M = 729 * B
+        A = dev.empty(M * max(K for K, _ in shapes), mg.F16)
+        dev.fill_normal(A, M * max(K for K, _ in shapes), SEED + 500 + B, 1.0)
+        C = dev.empty(M * max(N for _, N in shapes), mg.F16)
+
+        def enqueue():
+            for (K, N), w in zip(shapes, Ws):
+                mg.gemm(dev, A, w, C, M, N, K)
+
+        ms = time_graph(dev, torch, stream, enqueue, 5 if B >= 64 else 20, flush=lambda: flush_buf.zero_())
+        flop = sum(2.0 * M * K * N for K, N in shapes)
+        tf = flop / (ms * 1e-3) / 1e12
+        out[f"B{B}"] = {"M": M, "tflops": round(tf, 1), "frac": round(tf / peaks["bf16_tflops"], 4),
+                        "ms": round(ms, 4), "gflop": round(flop / 1e9, 1)}
+        del A, C
+    return {"unit": "TFLOP/s", "dtype": "f16", "gemms": "layer qkv/out/fc1/fc2 + projection 2304x8192, 8192x2048",
+            "peak": peaks["bf16_tflops"], "peak_source": peaks["source"], "batches": out}
+
+
+def run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head, seqs=(8, 32, 128)) -> dict:
+    """S concurrent decode sequences, i.e. GEMMs with M = S over the 24
+    layers' Q4_0 weights (the same 738 MB as the GEMV sweep, > 5x L2) plus the lm_head; bf16
+    activations ~N(0,1), bf16 outputs.  One replay = one decode step of all S sequences."""
+    out = {}
+    wbytes = sum(w.nbytes for mats in layers for (_, _, _, w, _, _) in mats) + Wh.nbytes
+    maxk = max(K for mats in layers for (_, K, _, _, _, _) in mats)
+    maxn = max(max(N for mats in layers for (_, _, N, _, _, _) in mats), n_head)
+    for S in seqs:
+        A = dev.empty(S * maxk, mg.BF16)
+        dev.fill_normal(A, S * maxk, SEED + 600 + S, 1.0)
+        C = dev.empty(S * maxn, mg.BF16)
+
+        def enqueue():
+            for mats in layers:
+                for _, K, N, W, _, _ in mats:
+                    mg.gemm_q(dev, A, W, C, S, N, K, mg.Q4_0)
+            mg.gemm_q(dev, A, Wh, C, S, n_head, K_h, mg.Q4_0)
+
+        ms = time_graph(dev, torch, stream, enqueue, 10)
+        act = sum(2 * S * (K + N) for mats in layers for (_, K, N, _, _, _) in mats) + 2 * S * (K_h + n_head)
+        flop = sum(2.0 * S * K * N for mats in layers for (_, K, N, _, _, _) in mats) + 2.0 * S * K_h * n_head
+        gbs = (wbytes + act) / (ms * 1e-3) / 1e9
+        tf = flop / (ms * 1e-3) / 1e12
+        out[f"S{S}"] = {"ms_per_step": round(ms, 4), "gbs": round(gbs, 1), "hbm_frac": round(gbs / peaks["hbm_gbs"], 4),
+                        "tflops": round(tf, 1), "tensor_frac": round(tf / peaks["bf16_tflops"], 4),
+                        "launches": 4 * len(layers) + 1}
+        del A, C
+    return {"weights": "Q4_0", "activations": "bf16", "layers": len(layers), "steps": out,
+            "basis": "roofline = min(HBM x AI, tensor peak); weights stream from HBM every step"}
+
+
 # --------------------------------------------------------------------------------------
 # reference arm: the reference's quantised path as its CPU restatement (the reference has no
 # Q4_0 kernel of its own and no runnable OpenCL here), on the host cores
@@ -471,6 +600,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the fp32 GEMV, batched-decode and SigLIP sections")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

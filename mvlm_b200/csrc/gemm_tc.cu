@@ -72,6 +72,12 @@ struct GemmArgs {
     int64_t bq_row_bytes;
     const uint8_t* bq_end;
     int* status;
+    // split-K: `splits` CTAs share a tile, each over kb_per_split k-blocks (a multiple of 4,
+    // i.e. whole 256-k groups); fp32 partials [split][M][N], and the tile's ticket counts
+    // arrivals so that the last one sums the partials in split order.
+    int splits, kb_per_split;
+    unsigned int* tickets;
+    float* partials;
 };
 
 template <typename T>
@@ -214,9 +220,11 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
     __shared__ __align__(8) uint64_t pk_empty[2];
     __shared__ uint32_t tmem_base_slot;
     __shared__ volatile int abort_flag;
+    __shared__ volatile int split_last;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int total_tiles = g.tiles_m * g.tiles_n;
+    const int total_units = total_tiles * g.splits;  // unit = (split, tile): split-major
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -252,9 +260,10 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         // ---------------------------------------------------------------- TMA producer
         if (lane == 0) {
             uint32_t it = 0;
-            for (int tile = blockIdx.x; tile < total_tiles && !abort_flag; tile += gridDim.x) {
+            for (int unit = blockIdx.x; unit < total_units && !abort_flag; unit += gridDim.x) {
+                const int tile = unit % total_tiles, kb0 = (unit / total_tiles) * g.kb_per_split;
                 const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
-                for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
+                for (int kb = kb0; kb < kb0 + g.kb_per_split; ++kb, ++it) {
                     const uint32_t s = it % S, ph = (it / S) & 1u;
                     if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
                     uint8_t* a_dst = smem + s * SB;
@@ -279,12 +288,13 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         if (lane == 0) {
             uint32_t it = 0, tcount = 0;
             bool issued = false;
-            for (int tile = blockIdx.x; tile < total_tiles && !abort_flag; tile += gridDim.x, ++tcount) {
+            for (int unit = blockIdx.x; unit < total_units && !abort_flag; unit += gridDim.x, ++tcount) {
+                const int kb0 = (unit / total_tiles) * g.kb_per_split;
                 const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
                 if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, g.status)) { abort_flag = 1; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * (MT * BN);
-                for (int kb = 0; kb < g.num_kb; ++kb, ++it) {
+                for (int kb = kb0; kb < kb0 + g.kb_per_split; ++kb, ++it) {
                     const uint32_t s = it % S, ph = (it / S) & 1u;
                     if (!mbar_wait(&full_bar[s], ph, g.status)) { abort_flag = 1; break; }
                     tc_fence_after();
@@ -300,7 +310,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
 #pragma unroll
                         for (int mt = 0; mt < MT; ++mt) {
                             const uint64_t adesc = smem_desc(a_addr + mt * kABytes + k * 32, 16, 1024, kSwizzle128B);
-                            umma_f16(d_tmem + mt * BN, adesc, bdesc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+                            umma_f16(d_tmem + mt * BN, adesc, bdesc, kIdesc, (kb != kb0 || k != 0) ? 1u : 0u);
                         }
                     }
                     issued = true;
@@ -320,7 +330,8 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         uint32_t tcount = 0;
         const bool vec_ok = (g.ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0);
-        for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tcount) {
+        for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x, ++tcount) {
+            const int tile = unit % total_tiles, split = unit / total_tiles;
             const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
             const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
             if (abort_flag || !mbar_wait(&tfull_bar[acc], acc_ph, g.status)) { abort_flag = 1; break; }
@@ -333,6 +344,22 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                 float v[32];
                 tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * (MT * BN) + mt * BN + cc * 32, v);
                 const int n0 = n_blk * BN + cc * 32;
+                if (g.splits > 1) {
+                    // split-K: this CTA's fp32 partial of the tile
+                    if (row < g.M && n0 < g.N) {
+                        float* pr = g.partials + ((size_t)split * g.M + row) * g.N + n0;
+                        if ((g.N & 3) == 0 && n0 + 32 <= g.N) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                reinterpret_cast<float4*>(pr)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (n0 + i < g.N) pr[i] = v[i];
+                        }
+                    }
+                    continue;
+                }
                 if (g.bias) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
@@ -366,6 +393,52 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+            if (g.splits > 1) {
+                // The last of the tile's splits to arrive sums the partials in split order
+                // (deterministic) and writes C; it leaves the ticket at zero for the next call.
+                __threadfence();
+                named_barrier_sync(2, 128);
+                if (warp == 2 && lane == 0) {
+                    const unsigned int t = atomicAdd(&g.tickets[tile], 1u);
+                    const int last = t == (unsigned int)(g.splits - 1);
+                    if (last) g.tickets[tile] = 0u;
+                    split_last = last;
+                }
+                named_barrier_sync(2, 128);
+                if (split_last) {
+                    // all 128 epilogue threads over the tile's rows x columns, 4 columns each
+                    __threadfence();
+                    const int et = (warp - 2) * 32 + lane;
+                    const int row0 = m_blk * TBM, n_base = n_blk * BN;
+                    const int rows = min(TBM, g.M - row0), cols = min(BN, g.N - n_base);
+                    const int c4 = (cols + 3) / 4;
+                    const bool vec = (g.N & 3) == 0;
+                    for (int idx = et; idx < rows * c4; idx += 128) {
+                        const int row = row0 + idx / c4, n = n_base + (idx % c4) * 4;
+                        float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        for (int sp = 0; sp < g.splits; ++sp) {
+                            const float* src = g.partials + ((size_t)sp * g.M + row) * g.N + n;
+                            if (vec) {
+                                const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src));
+                                sum[0] += v4.x;
+                                sum[1] += v4.y;
+                                sum[2] += v4.z;
+                                sum[3] += v4.w;
+                            } else {
+                                for (int i = 0; i < 4; ++i)
+                                    if (n + i < n_base + cols) sum[i] += __ldcg(src + i);
+                            }
+                        }
+                        for (int i = 0; i < 4; ++i) {
+                            if (n + i >= n_base + cols) break;
+                            float o = sum[i];
+                            if (g.bias) o += bias_at(g.bias, g.bias_type, n + i);
+                            store_out(g.C, g.c_type, (size_t)row * g.ldc + n + i, o);
+                        }
+                    }
+                }
+                named_barrier_sync(2, 128);
+            }
         }
     } else if constexpr (is_packed_tma(BMODE)) {
         // ---------------------------------------------------------------- dequantisers (TMA-staged)
@@ -381,12 +454,13 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         const int dt = tid - 192;
         const int r = dt & (BN - 1), h = dt >> 7;
         uint8_t* pk = smem + S * SB;
-        const int groups = g.K / 256;
-        const int my_tiles = total_tiles > (int)blockIdx.x ? (total_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-        const uint32_t n_groups = (uint32_t)my_tiles * (uint32_t)groups;
+        const int groups = g.kb_per_split / 4;  // 256-k groups per unit
+        const int my_units = total_units > (int)blockIdx.x ? (total_units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const uint32_t n_groups = (uint32_t)my_units * (uint32_t)groups;
         auto issue_group = [&](uint32_t gi) {
-            const int tile = (int)blockIdx.x + (int)(gi / groups) * (int)gridDim.x;
-            const int grp = (int)(gi % groups);
+            const int unit = (int)blockIdx.x + (int)(gi / groups) * (int)gridDim.x;
+            const int tile = unit % total_tiles;
+            const int grp = (unit / total_tiles) * groups + (int)(gi % groups);
             const uint32_t slot = gi & 1u;
             if (!mbar_wait(&pk_empty[slot], ((gi >> 1) & 1u) ^ 1u, g.status)) return false;
             mbar_arrive_expect_tx(&pk_full[slot], (uint32_t)(BN * GB));
@@ -437,7 +511,8 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         }
     } else if constexpr (kQuant) {
         // ---------------------------------------------------------------- dequantisers
-        // Stage `it` of this CTA is k-block (it % num_kb) of its (it / num_kb)-th tile.  The
+        // Stage `it` of this CTA is k-block (it % kb_per_split) of its (it / kb_per_split)-th
+        // unit (a tile, or one split of it).  The
         // packed blocks of stage it+3 are loaded into registers before stage it is decoded,
         // so three stages of global-memory latency are in flight per thread.
         constexpr int BB = is_q4_mode(BMODE) ? 18 : 34;
@@ -446,13 +521,14 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         constexpr int NPRE = 3;
         const int dt = tid - 192;
         const int nbk = (g.K + 31) / 32;  // blocks per row
-        const int my_tiles = total_tiles > (int)blockIdx.x ? (total_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-        const uint32_t n_stages = (uint32_t)my_tiles * (uint32_t)g.num_kb;
+        const int my_units = total_units > (int)blockIdx.x ? (total_units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const uint32_t n_stages = (uint32_t)my_units * (uint32_t)g.kb_per_split;
         RawBlock<NW> raw[NPRE][UPT];
         auto load_stage = [&](RawBlock<NW>(&dst)[UPT], uint32_t it) {
             const bool live = it < n_stages;
-            const int tile = (int)blockIdx.x + (int)(it / g.num_kb) * (int)gridDim.x;
-            const int kb = (int)(it % g.num_kb);
+            const int unit = (int)blockIdx.x + (int)(it / g.kb_per_split) * (int)gridDim.x;
+            const int tile = unit % total_tiles;
+            const int kb = (unit / total_tiles) * g.kb_per_split + (int)(it % g.kb_per_split);
             const int n_blk = live ? tile / g.tiles_m : 0;
 #pragma unroll
             for (int v = 0; v < UPT; ++v) {
@@ -569,8 +645,8 @@ cudaError_t launch_gemm(const mgpu_k::LaunchCtx& c, const CUtensorMap& ma, const
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit, std::memory_order_acq_rel);
     }
-    const int tiles = g.tiles_m * g.tiles_n;
-    const int grid = tiles < c.sm_count ? tiles : c.sm_count;
+    const int units = g.tiles_m * g.tiles_n * g.splits;
+    const int grid = units < c.sm_count ? units : c.sm_count;
     kern<<<grid, gemm_threads(BMODE), smem, c.stream>>>(ma, mb, g);
     return cudaGetLastError();
 }
@@ -621,18 +697,17 @@ const char* gemm_check(const GemmOperand& A, const GemmOperand& B, const GemmOpe
     return nullptr;
 }
 
-cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
-                 const void* bias, int bias_type, int M, int N, int K) {
-    if (gemm_check(A, B, C, M, N, K)) return cudaErrorInvalidValue;
-    int bmode;
+GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, int M, int N, int K) {
+    (void)A;
+    GemmPlan p;
     const bool quant = B.type == MGPU_Q8_0 || B.type == MGPU_Q4_0;
     // Packed rows can be staged by TMA in 256-k groups when every group starts on a 16-byte
     // boundary: K % 256 == 0, row pitch % 16 == 0 and a 16-byte aligned base.
     const bool packed_ok = quant && K % 256 == 0 && B.ld % 16 == 0 && (reinterpret_cast<uintptr_t>(B.ptr) & 15) == 0 &&
                            B.ld == (int64_t)(K / 32) * (B.type == MGPU_Q4_0 ? 18 : 34);
-    if (B.type == MGPU_Q8_0) bmode = packed_ok ? B_Q8_TMA : B_Q8;
-    else if (B.type == MGPU_Q4_0) bmode = packed_ok ? B_Q4_TMA : B_Q4;
-    else bmode = (B.layout == MGPU_LAYOUT_NK) ? B_TMA_K : B_TMA_MN;
+    if (B.type == MGPU_Q8_0) p.bmode = packed_ok ? B_Q8_TMA : B_Q8;
+    else if (B.type == MGPU_Q4_0) p.bmode = packed_ok ? B_Q4_TMA : B_Q4;
+    else p.bmode = (B.layout == MGPU_LAYOUT_NK) ? B_TMA_K : B_TMA_MN;
 
     // Pick the tile by the estimated makespan over the SMs.  Dense: BN in {128, 256}, tile time
     // ~ BN + a fixed overhead.  Packed quantised: BN = 128 and 128 or 256 rows; a 256-row tile
@@ -642,10 +717,48 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
         const long tiles = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
         return (tiles + c.sm_count - 1) / c.sm_count;
     };
-    int BN = 128, mt = 1;
-    if (is_packed_tma(bmode)) mt = waves(2 * BM, 128) * 14 < waves(BM, 128) * 10 ? 2 : 1;
-    else BN = waves(BM, 128) * (128 + 32) < waves(BM, 256) * (256 + 32) ? 128 : 256;
-    const int tiles_m = (M + BM * mt - 1) / (BM * mt);
+    p.BN = 128;
+    p.mt = 1;
+    if (is_packed_tma(p.bmode)) p.mt = waves(2 * BM, 128) * 14 < waves(BM, 128) * 10 ? 2 : 1;
+    else p.BN = waves(BM, 128) * (128 + 32) < waves(BM, 256) * (256 + 32) ? 128 : 256;
+    p.tiles_m = (M + BM * p.mt - 1) / (BM * p.mt);
+    p.tiles_n = (N + p.BN - 1) / p.BN;
+    p.num_kb = (K + BK - 1) / BK;
+    // Split K for skinny M (M <= 16, e.g. a decode batch of up to 16 sequences) when the tiles
+    // fill at most half of the SMs: the largest split count that divides the 256-k groups
+    // and keeps splits x tiles within the SMs; each split is at least one group.  (At
+    // M = 32 and 128 the fp32 partials cost as much as the idle SMs, measured on the Phi-1.5
+    // decode shapes.)
+    p.splits = 1;
+    const int tiles = p.tiles_m * p.tiles_n;
+    if (M <= 16 && K % 256 == 0 && tiles * 2 <= c.sm_count) {
+        const int groups = p.num_kb / 4;
+        for (int sp = min(groups, c.sm_count / tiles); sp >= 2; --sp)
+            if (groups % sp == 0) {
+                p.splits = sp;
+                break;
+            }
+    }
+    p.kb_per_split = p.num_kb / p.splits;
+    return p;
+}
+
+size_t gemm_split_bytes(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, int M, int N, int K) {
+    const GemmPlan p = plan_gemm(c, A, B, M, N, K);
+    return p.splits > 1 ? (size_t)p.splits * M * N * sizeof(float) : 0;
+}
+
+cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
+                 const void* bias, int bias_type, int M, int N, int K, const GemmSplitScratch* split) {
+    if (gemm_check(A, B, C, M, N, K)) return cudaErrorInvalidValue;
+    GemmPlan p = plan_gemm(c, A, B, M, N, K);
+    if (p.splits > 1 && (!split || !split->tickets || !split->partials ||
+                         (size_t)p.splits * M * N > split->max_partials ||
+                         (size_t)p.tiles_m * p.tiles_n > split->max_tickets)) {
+        p.splits = 1;
+        p.kb_per_split = p.num_kb;
+    }
+    const int bmode = p.bmode, BN = p.BN, mt = p.mt, tiles_m = p.tiles_m;
 
     GemmArgs g;
     g.M = M;
@@ -663,6 +776,10 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
     g.bq_row_bytes = 0;
     g.bq_end = nullptr;
     g.status = c.status;
+    g.splits = p.splits;
+    g.kb_per_split = p.kb_per_split;
+    g.tickets = p.splits > 1 ? split->tickets : nullptr;
+    g.partials = p.splits > 1 ? split->partials : nullptr;
 
     CUtensorMap ma, mb;
     memset(&mb, 0, sizeof(mb));

@@ -13,6 +13,11 @@
 //   launch: the producer starts streaming weights while the previous kernel drains, and the
 //   consumers execute griddepcontrol.wait before reading x (which the previous kernel may
 //   write).
+// gemv_q_mma: the same product with the warp-level integer MMA (mma.sync m16n8k32, u8/s8
+//   weights x s8 activation digits, exact s32 sums): two GGUF blocks of 16 rows per MMA pair,
+//   rows staged at a padded pitch so fragment loads are conflict-free.  Fewer instructions per
+//   block, but in a chain of dependent launches of mixed shapes it measures slower than the
+//   dp4a kernel, so the launcher uses it for the K whose block count does not divide 256.
 // gemv_nk: dense [N][K] rows (GGUF F32/F16/BF16 tensors): warp per row group, 16-byte loads.
 // gemv_kn: dense [K][N] (the reference kernels' orientation): columns across lanes, K split
 //   across CTAs; fp32 partials go to scratch and the last CTA of each column tile sums them
@@ -32,6 +37,9 @@ constexpr int kGemvThreads = kConsumerThreads + 32;
 constexpr int kGemvMaxStages = 8;  // ring depth is chosen per shape, up to this
 constexpr int kGemvCtasPerSm = 2;                 // at most; see the launcher
 constexpr uint32_t kGemvSmemBudget = 100 * 1024;  // per CTA: two CTAs share an SM
+// The MMA kernel's budget: two such CTAs plus their 1 KB reservations stay within an SM's
+// 228 KB, and a 16-row chunk of K = 8192 Q4_0 rows (74 KB) fits beside its activations.
+constexpr uint32_t kGemvMmaSmemBudget = 110 * 1024;
 
 template <int QT> struct QTraits;
 template <> struct QTraits<MGPU_Q4_0> {
@@ -86,15 +94,16 @@ struct XFixed {
 //   planes[p * (K/4) + w]  (w = word index = element / 4), bscale[b], bsum[b] per block b.
 // Consumer threads then read their own block's 24 words.  Costs one round trip to L2 plus a
 // handful of instructions per thread, instead of 32 loads and conversions per thread.
-template <typename XT>
-__device__ __forceinline__ void prepare_x(const XT* __restrict__ x, int K, uint32_t* planes, float* bscale,
-                                          float* bsum, int tid, int nthreads) {
-    // words = K / 4 is a multiple of 256 (K % 1024 == 0) and at most 2048 (K <= 8192), so each
-    // thread converts at most 8 words; all loads are issued before any is used, so the
-    // whole activation vector costs one round trip.
-    constexpr int kMaxIter = 8;
+// words = K / 4 is a multiple of 256 (K % 1024 == 0) and at most 2048 (K <= 8192), so each
+// thread converts ITERS = K / 1024 words; the count is a compile-time constant so that all
+// loads are issued before any is used and the activation vector costs one round trip.
+// (K of 3, 5, 6 or 7 x 1024 takes the runtime-bounded form: ITERS = 8, EXACT = false.)
+template <typename XT, int ITERS, bool EXACT>
+__device__ __forceinline__ void prepare_x_n(const XT* __restrict__ x, int K, uint32_t* planes, float* bscale,
+                                            float* bsum, int tid, int nthreads) {
+    constexpr int kMaxIter = ITERS;
     const int words = K / 4;
-    const int iters = words / nthreads;
+    const int iters = EXACT ? ITERS : words / nthreads;
     float v[kMaxIter][4];
 #pragma unroll
     for (int it = 0; it < kMaxIter; ++it) {
@@ -148,6 +157,18 @@ __device__ __forceinline__ void prepare_x(const XT* __restrict__ x, int K, uint3
                 bsum[w >> 3] = (float)sum;
             }
         }
+    }
+}
+
+template <typename XT>
+__device__ __forceinline__ void prepare_x(const XT* __restrict__ x, int K, uint32_t* planes, float* bscale,
+                                          float* bsum, int tid, int nthreads) {
+    switch (K >> 10) {
+        case 1: prepare_x_n<XT, 1, true>(x, K, planes, bscale, bsum, tid, nthreads); break;
+        case 2: prepare_x_n<XT, 2, true>(x, K, planes, bscale, bsum, tid, nthreads); break;
+        case 4: prepare_x_n<XT, 4, true>(x, K, planes, bscale, bsum, tid, nthreads); break;
+        case 8: prepare_x_n<XT, 8, true>(x, K, planes, bscale, bsum, tid, nthreads); break;
+        default: prepare_x_n<XT, 8, false>(x, K, planes, bscale, bsum, tid, nthreads); break;
     }
 }
 
@@ -372,6 +393,344 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     }
 }
 
+// ---- integer tensor-core inner product (mma.sync m16n8k32) ---------------------------
+// gemv_q_mma computes the same sums as gemv_q_stream with the warp-level integer MMA:
+//   A (16 x 32, u8 for Q4_0 nibbles / s8 for Q8_0 quants) = weights of 16 rows,
+//   B (32 x 8, s8) = activation digit planes, D (16 x 8, s32) = exact integer sums.
+// Activations are 23-bit fixed point per 32-element block (x = X * 2^(e-22), as above) written
+// as three balanced base-256 digits X = p0 + 256 p1 + 65536 p2 with every p in [-128, 127],
+// so all of B is signed bytes.  One MMA pair covers two blocks (b = 2p, 2p+1) of 16 rows: in
+// the "lo" MMA the k positions 0..15 are elements 0..15 of block 2p and 16..31 elements 0..15
+// of block 2p+1; the "hi" MMA does elements 16..31.  B column n < 4 holds plane n of block 2p
+// on k < 16 (zeros on k >= 16), column n >= 4 plane n-4 of block 2p+1 on k >= 16; plane 3 is
+// zero.  Lane (g, t) of D then holds, for rows g and g+8, the plane sums of block
+// 2p + (t >> 1): t even planes 0 and 1, t odd plane 2.  With the nibbles of a Q4_0 quant
+// word split into lo (q & 0x0F0F0F0F) and hi ((q >> 4) & 0x0F0F0F0F), the A fragments come
+// straight from the packed bytes.  The -8 of Q4_0 enters once per block as -8 sum X,
+// added by the plane-2 lanes: sum X (q - 8) = sum X q - 8 sum X.
+// Rows are staged with a pitch of row_bytes + 16, which puts the 8 rows a fragment load
+// touches on distinct banks.
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, bool u8a) {
+    if (u8a)
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Per-block activation record in shared memory (128 bytes): planes 0, 1, 2 and a zero plane,
+// 32 bytes each, with the 8 words of a plane stored in the order 0,4,1,5,2,6,3,7 so that lane
+// t's (word t, word t+4) pair is one 8-byte load.  Per-block auxiliaries (16 bytes, fp32):
+// {2^(e-22), 0, 2^(e-22) * 65536, -8 sum X / 65536 (Q4_0; 0 for Q8_0)}, read by lane t at
+// offset 8 * (t & 1): a lane's plane scale and the offset it adds before scaling.
+constexpr int kXRecBytes = 128;
+constexpr int kXAuxBytes = 16;
+
+// ITERS = K / 1024 words per thread (256 threads), a compile-time count so that all of the
+// thread's loads are issued before the first is used (one L2 round trip, not ITERS).
+// (K of 3, 5, 6 or 7 x 1024 takes the runtime-bounded form: ITERS = 8, EXACT = false.)
+template <typename XT, bool Q4, int ITERS, bool EXACT>
+__device__ __forceinline__ void prepare_x_digits_n(const XT* __restrict__ x, int K, uint8_t* xrec, uint8_t* xaux,
+                                                   int tid, int nthreads) {
+    constexpr int kMaxIter = ITERS;
+    const int iters = EXACT ? ITERS : (K / 4) / nthreads;
+    float v[kMaxIter][4];
+#pragma unroll
+    for (int it = 0; it < kMaxIter; ++it) {
+        if (it < iters) {
+            const int w = it * nthreads + tid;
+            if constexpr (sizeof(XT) == 4) {
+                const float4 f = __ldg(reinterpret_cast<const float4*>(x) + w);
+                v[it][0] = f.x; v[it][1] = f.y; v[it][2] = f.z; v[it][3] = f.w;
+            } else {
+                const uint2 u = __ldg(reinterpret_cast<const uint2*>(x) + w);
+                const uint32_t uu[2] = {u.x, u.y};
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    XT lo, hi;
+                    uint16_t l16 = (uint16_t)(uu[j] & 0xFFFF), h16 = (uint16_t)(uu[j] >> 16);
+                    memcpy(&lo, &l16, 2);
+                    memcpy(&hi, &h16, 2);
+                    v[it][2 * j] = to_f32<XT>(lo);
+                    v[it][2 * j + 1] = to_f32<XT>(hi);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int it = 0; it < kMaxIter; ++it) {
+        if (it < iters) {
+            const int w = it * nthreads + tid;
+            const int blk = w >> 3, wi = w & 7;
+            float amax = fmaxf(fmaxf(fabsf(v[it][0]), fabsf(v[it][1])), fmaxf(fabsf(v[it][2]), fabsf(v[it][3])));
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            int e = 0;
+            frexpf(amax, &e);  // the block's |x| < 2^e
+            const float up = __int_as_float((127 + 22 - e) << 23);  // 2^(22-e); |e| < 100 for finite x
+            // X + 0x808080 = u0 + 256 u1 + 65536 u2 with u in [0, 255] (|X| <= 2^22), and
+            // p_i = u_i - 128 = the byte u_i ^ 0x80 read as signed: the balanced digits.
+            uint32_t u[4];
+            int xs = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int X = __float2int_rn(v[it][j] * up);  // |X| <= 2^22
+                xs += X;
+                u[j] = (uint32_t)(X + 0x808080);
+            }
+            const uint32_t lo01 = prmt(u[0], u[1], 0x6240u), lo23 = prmt(u[2], u[3], 0x6240u);  // bytes 0, 2
+            const uint32_t hi01 = prmt(u[0], u[1], 0x7351u), hi23 = prmt(u[2], u[3], 0x7351u);  // bytes 1, 3
+            const uint32_t w0 = prmt(lo01, lo23, 0x5410u) ^ 0x80808080u;  // byte 0 of each X
+            const uint32_t w1 = prmt(hi01, hi23, 0x5410u) ^ 0x80808080u;  // byte 1
+            const uint32_t w2 = prmt(lo01, lo23, 0x7632u) ^ 0x80808080u;  // byte 2
+            uint8_t* rec = xrec + (size_t)blk * kXRecBytes;
+            const int slot = wi < 4 ? 2 * wi : 2 * (wi - 4) + 1;
+            reinterpret_cast<uint32_t*>(rec)[slot] = w0;
+            reinterpret_cast<uint32_t*>(rec + 32)[slot] = w1;
+            reinterpret_cast<uint32_t*>(rec + 64)[slot] = w2;
+            reinterpret_cast<uint32_t*>(rec + 96)[slot] = 0u;
+            if constexpr (Q4) {
+#pragma unroll
+                for (int off = 1; off < 8; off <<= 1) xs += __shfl_xor_sync(0xffffffffu, xs, off);
+            }
+            if (wi == 0) {
+                const float sc = __int_as_float((127 + e - 22) << 23);  // 2^(e-22)
+                uint32_t* aux = reinterpret_cast<uint32_t*>(xaux + (size_t)blk * kXAuxBytes);
+                aux[0] = __float_as_uint(sc);
+                aux[1] = 0u;
+                aux[2] = __float_as_uint(sc * 65536.0f);
+                // the Q4_0 offset, -8 sum X, applied once per block by the plane-2 lanes (in
+                // units of their 65536 scale)
+                aux[3] = __float_as_uint(Q4 ? (float)(-8 * (long long)xs) * (1.0f / 65536.0f) : 0.0f);
+            }
+        }
+    }
+}
+
+template <typename XT, bool Q4>
+__device__ __forceinline__ void prepare_x_digits(const XT* __restrict__ x, int K, uint8_t* xrec, uint8_t* xaux,
+                                                 int tid, int nthreads) {
+    switch (K >> 10) {
+        case 1: prepare_x_digits_n<XT, Q4, 1, true>(x, K, xrec, xaux, tid, nthreads); break;
+        case 2: prepare_x_digits_n<XT, Q4, 2, true>(x, K, xrec, xaux, tid, nthreads); break;
+        case 4: prepare_x_digits_n<XT, Q4, 4, true>(x, K, xrec, xaux, tid, nthreads); break;
+        case 8: prepare_x_digits_n<XT, Q4, 8, true>(x, K, xrec, xaux, tid, nthreads); break;
+        default: prepare_x_digits_n<XT, Q4, 8, false>(x, K, xrec, xaux, tid, nthreads); break;
+    }
+}
+
+struct GemvMmaArgs {
+    const uint8_t* W;
+    const void* x;
+    void* y;
+    int N;
+    int nb;                // blocks per row (K / 32); nb % 32 == 0, nb <= 256
+    uint32_t row_bytes;    // nb * block bytes, a multiple of 32
+    uint32_t pitch;        // row_bytes + 16: shared-memory row pitch
+    uint32_t stage_stride;
+    int stages;            // ring depth, 2..kGemvMaxStages
+    int chunks_per_flush;  // chunks whose row partials are buffered before one reduction
+    int* status;
+};
+
+constexpr int kMmaWarps = kConsumerThreads / 32;  // 8: each takes 1/8 of K
+
+// RG = 16-row groups per chunk.  Warp w of the consumers owns block pairs
+// [w * nb / 16, (w + 1) * nb / 16) of every row; its row partials meet in shared memory.
+template <int QT, int RG, typename XT, typename YT>
+__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_mma(GemvMmaArgs a) {
+    constexpr bool kQ4 = QT == MGPU_Q4_0;
+    constexpr int BB = QTraits<QT>::kBlockBytes;
+    constexpr int TR = 16 * RG;  // rows per chunk
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full_bar[kGemvMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kGemvMaxStages];
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nb = a.nb;
+    const int G = gridDim.x;
+    const int r0 = (int)((long long)a.N * blockIdx.x / G);
+    const int r1 = (int)((long long)a.N * (blockIdx.x + 1) / G);
+    const int nchunks = (r1 - r0 + TR - 1) / TR;
+
+    if (tid == 0) {
+        for (int s = 0; s < a.stages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], kMmaWarps);
+        }
+        fence_mbar_init();
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == kMmaWarps) {
+        // ---- producer warp: one bulk copy per row (into the padded pitch), 32 lanes issue ----
+        int c = 0, s = 0;
+        uint32_t ph = 0;
+        for (; c < nchunks; ++c) {
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&empty_bar[s], ph ^ 1u, a.status);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            const int row = r0 + c * TR;
+            const int n = min(TR, r1 - row);
+            if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], (uint32_t)n * a.row_bytes);
+            __syncwarp();
+            uint8_t* dst = smem + (size_t)s * a.stage_stride;
+            for (int i = lane; i < n; i += 32)
+                bulk_g2s(dst + (size_t)i * a.pitch, a.W + (size_t)(row + i) * a.row_bytes, a.row_bytes, &full_bar[s]);
+            if (++s == a.stages) {
+                s = 0;
+                ph ^= 1u;
+            }
+        }
+        if (c < nchunks && lane == 0) {
+            // Timed out: let the copies already issued land before the CTA exits.
+            for (int k = max(0, c - a.stages); k < c; ++k)
+                mbar_wait(&full_bar[k % a.stages], (uint32_t)(k / a.stages) & 1u, nullptr);
+        }
+        return;
+    }
+
+    // ---- consumers ----
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int K = nb * 32;
+    uint8_t* xrec = smem + (size_t)a.stages * a.stage_stride;
+    uint8_t* xaux = xrec + (size_t)nb * kXRecBytes;
+    float* part = reinterpret_cast<float*>(xaux + (size_t)nb * kXAuxBytes);
+    prepare_x_digits<XT, kQ4>(reinterpret_cast<const XT*>(a.x), K, xrec, xaux, tid, kConsumerThreads);
+    named_barrier_sync(1, kConsumerThreads);
+
+    const int g = lane >> 2, t = lane & 3;
+    const int ppw = nb >> 4;  // block pairs per warp
+    const int p_begin = warp * ppw;
+    // lane constants: which B register carries the data, and the lane's block within a pair
+    const uint32_t bsel_lo = (g < 4) ? 0xFFFFFFFFu : 0u;
+    const int bhalf = t >> 1;
+    const uint8_t* xb_lane = xrec + (g >> 2) * kXRecBytes + (g & 3) * 32 + 8 * t;
+    const uint8_t* xa_lane = xaux + bhalf * kXAuxBytes + (t & 1) * 8;
+    YT* __restrict__ y = reinterpret_cast<YT*>(a.y);
+
+    int s = 0;
+    uint32_t ph = 0;
+    for (int c = 0; c < nchunks; ++c) {
+        if (!mbar_wait(&full_bar[s], ph, a.status)) return;
+        const uint8_t* st = smem + (size_t)s * a.stage_stride;
+        float acc[RG][2];
+#pragma unroll
+        for (int r = 0; r < RG; ++r) acc[r][0] = acc[r][1] = 0.0f;
+        // two block pairs per iteration (ppw is even: nb % 32 == 0), so that two independent
+        // MMA chains are in flight per warp
+#pragma unroll 1
+        for (int pp = 0; pp < ppw; pp += 2) {
+            uint32_t b0[2], b1[2], h0[2], h1[2];
+            float xsl[2];
+            float corr[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int pr = p_begin + pp + u;
+                const uint2 bw = *reinterpret_cast<const uint2*>(xb_lane + (size_t)(2 * pr) * kXRecBytes);
+                const uint2 ax = *reinterpret_cast<const uint2*>(xa_lane + (size_t)(2 * pr) * kXAuxBytes);
+                xsl[u] = __uint_as_float(ax.x);
+                corr[u] = __uint_as_float(ax.y);
+                b0[u] = bw.x & bsel_lo;
+                b1[u] = bw.x & ~bsel_lo;
+                h0[u] = bw.y & bsel_lo;
+                h1[u] = bw.y & ~bsel_lo;
+            }
+#pragma unroll
+            for (int r = 0; r < RG; ++r) {
+                const uint8_t* rg = st + (size_t)(r * 16 + g) * a.pitch;
+                const uint8_t* rg8 = rg + (size_t)8 * a.pitch;
+                int dl[2][4], dh[2][4];
+                float dg[2], dg8[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int pr = p_begin + pp + u;
+                    uint32_t alo[4], ahi[4];
+                    if constexpr (kQ4) {
+                        // block 2pr at byte 36 pr (quants at +2: realign), block 2pr+1 at
+                        // 36 pr + 18 (quants at +20: aligned)
+                        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(rg + 36 * pr + 4 * t);
+                        const uint32_t* q8 = reinterpret_cast<const uint32_t*>(rg8 + 36 * pr + 4 * t);
+                        const uint32_t u0 = prmt(q0[0], q0[1], 0x5432u), u1 = q0[5];
+                        const uint32_t v0 = prmt(q8[0], q8[1], 0x5432u), v1 = q8[5];
+                        alo[0] = u0 & 0x0F0F0F0Fu; ahi[0] = (u0 >> 4) & 0x0F0F0F0Fu;
+                        alo[1] = v0 & 0x0F0F0F0Fu; ahi[1] = (v0 >> 4) & 0x0F0F0F0Fu;
+                        alo[2] = u1 & 0x0F0F0F0Fu; ahi[2] = (u1 >> 4) & 0x0F0F0F0Fu;
+                        alo[3] = v1 & 0x0F0F0F0Fu; ahi[3] = (v1 >> 4) & 0x0F0F0F0Fu;
+                    } else {
+                        // block 2pr at byte 68 pr (quants at +2 and +18: realign), block 2pr+1
+                        // at 68 pr + 34 (quants at +36 and +52: aligned)
+                        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(rg + 68 * pr + 4 * t);
+                        const uint32_t* q8 = reinterpret_cast<const uint32_t*>(rg8 + 68 * pr + 4 * t);
+                        alo[0] = prmt(q0[0], q0[1], 0x5432u);
+                        ahi[0] = prmt(q0[4], q0[5], 0x5432u);
+                        alo[1] = prmt(q8[0], q8[1], 0x5432u);
+                        ahi[1] = prmt(q8[4], q8[5], 0x5432u);
+                        alo[2] = q0[9];
+                        ahi[2] = q0[13];
+                        alo[3] = q8[9];
+                        ahi[3] = q8[13];
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) dl[u][i] = dh[u][i] = 0;
+                    mma_s8(dl[u], alo, b0[u], b1[u], kQ4);
+                    mma_s8(dh[u], ahi, h0[u], h1[u], kQ4);
+                    // this lane's block: 2pr + (t >> 1); its fp16 scale for rows g and g+8
+                    const int boff = (2 * pr + bhalf) * BB;
+                    dg[u] = __half2float(*reinterpret_cast<const __half*>(rg + boff)) * xsl[u];
+                    dg8[u] = __half2float(*reinterpret_cast<const __half*>(rg8 + boff)) * xsl[u];
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int vg = (dl[u][0] + dh[u][0]) + 256 * (dl[u][1] + dh[u][1]);
+                    const int vg8 = (dl[u][2] + dh[u][2]) + 256 * (dl[u][3] + dh[u][3]);
+                    acc[r][0] = fmaf(dg[u], (float)vg + corr[u], acc[r][0]);
+                    acc[r][1] = fmaf(dg8[u], (float)vg8 + corr[u], acc[r][1]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[s]);
+        if (++s == a.stages) {
+            s = 0;
+            ph ^= 1u;
+        }
+        // sum the four lanes of a row, then the 8 warps through shared memory
+        const int cf = c % a.chunks_per_flush;
+#pragma unroll
+        for (int r = 0; r < RG; ++r) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float v = acc[r][h];
+                v += __shfl_xor_sync(0xffffffffu, v, 1);
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                if (t == 0) part[(cf * TR + r * 16 + g + 8 * h) * kMmaWarps + warp] = v;
+            }
+        }
+        if (cf == a.chunks_per_flush - 1 || c == nchunks - 1) {
+            named_barrier_sync(1, kConsumerThreads);
+            const int row0 = r0 + (c - cf) * TR;
+            const int nrows = min((cf + 1) * TR, r1 - row0);
+            for (int r = tid; r < nrows; r += kConsumerThreads) {
+                const float4* pv = reinterpret_cast<const float4*>(part + r * kMmaWarps);
+                const float4 u = pv[0], w = pv[1];
+                y[row0 + r] = from_f32<YT>(((u.x + u.y) + (u.z + u.w)) + ((w.x + w.y) + (w.z + w.w)));
+            }
+            named_barrier_sync(1, kConsumerThreads);
+        }
+    }
+}
+
 // Fallback for rows that are not 16-byte aligned or K outside [1024, 8192]: one warp per
 // row, byte loads.
 template <int QT, typename XT, typename YT>
@@ -556,6 +915,21 @@ struct GemvQLaunch {
                 gemv_q_generic<QT, XT, YT><<<blocks, 256, 0, c.stream>>>(W, (const XT*)x, (YT*)y, N, nb, row_bytes);
                 return cudaGetLastError();
             }
+            // The dp4a kernel gives each thread one block column of a row slot, so it needs
+            // nb to divide 256 (K = 1024, 2048, 4096, 8192).  Other K go to the MMA kernel
+            // when it can stage them.  (Timed inside a chain of dependent GEMVs of different
+            // shapes, the dp4a kernel is the faster of the two on every Phi-1.5 shape, so it
+            // takes all K it supports.)
+            const bool dp4a_ok = (kConsumerThreads % nb) == 0;
+            if (!dp4a_ok) {
+                const cudaError_t e = run_mma(c, W, x, y, N, K, true);
+                if (e != cudaErrorNotSupported) return e;
+            }
+            if (!dp4a_ok) {
+                const int blocks = (N * 32 + 255) / 256;
+                gemv_q_generic<QT, XT, YT><<<blocks, 256, 0, c.stream>>>(W, (const XT*)x, (YT*)y, N, nb, row_bytes);
+                return cudaGetLastError();
+            }
             const int RP = kConsumerThreads / nb;
             // Layer-sized GEMVs take one CTA per SM: a launch then leaves room on every SM for
             // one CTA of the next GEMV in the stream, which under programmatic dependent launch
@@ -631,6 +1005,115 @@ struct GemvQLaunch {
                 case 2: return launch<2, XT, YT>(c, a, G, smem);
                 default: return launch<1, XT, YT>(c, a, G, smem);
             }
+        }
+        // Integer tensor-core path (gemv_q_mma).  Returns cudaErrorNotSupported, launching
+        // nothing, when a 16-row chunk with its padded pitch does not fit the shared-memory
+        // budget (Q8_0 rows of K = 8192) or, unless `any_shape`, when the shape is not one it
+        // is the faster kernel for; the caller then takes the dp4a kernel.
+        static cudaError_t run_mma(const mgpu_k::LaunchCtx& c, const uint8_t* W, const void* x, void* y, int N,
+                                   int K, bool any_shape) {
+            constexpr int BB = QTraits<QT>::kBlockBytes;
+            const int nb = K / 32;
+            const size_t row_bytes = (size_t)nb * BB;
+            const size_t pitch = row_bytes + 16;
+            constexpr int kBigRows = 64;
+            const int per_sm = N > c.sm_count * kBigRows ? kGemvCtasPerSm : 1;
+            const int G = max(1, min(c.sm_count * per_sm, (N + 15) / 16));
+            const int rows_per_cta = (N + G - 1) / G;
+            constexpr int kPartFloats = 4096;
+            const size_t x_bytes = (size_t)nb * (kXRecBytes + kXAuxBytes);
+            auto stride = [&](int rg) { return ((size_t)16 * rg * pitch + 1023) / 1024 * 1024; };
+            auto chunks_of = [&](int rg) { return (rows_per_cta + 16 * rg - 1) / (16 * rg); };
+            auto part_floats = [&](int rg) {
+                const int cpf = max(1, min(chunks_of(rg), kPartFloats / (16 * rg * kMmaWarps)));
+                return (size_t)cpf * 16 * rg * kMmaWarps;
+            };
+            // ring depth for chunks of rg row groups, at most `cap`; a CTA whose rows form one
+            // chunk may use a single stage
+            auto depth = [&](int rg, int cap) {
+                const size_t fixed = x_bytes + 4 * part_floats(rg);
+                const int dmin = chunks_of(rg) == 1 ? 1 : 2;
+                if (fixed + dmin * stride(rg) > kGemvMmaSmemBudget) return 0;
+                return max(dmin, min(cap, min(chunks_of(rg), (int)((kGemvMmaSmemBudget - fixed) / stride(rg)))));
+            };
+            // Same policy as the dp4a kernel: prefetch the CTA's whole share when a ring can
+            // hold it (widest chunk with at most 25 % padding rows), else stream through a
+            // 4-stage ring of the widest chunk that fits.
+            int rg = 0, stages = 0;
+            for (int r = 4; r >= 1 && !rg; r >>= 1) {
+                const int d = depth(r, kGemvMaxStages);
+                const int waste = chunks_of(r) * 16 * r - rows_per_cta;
+                if (d && d >= chunks_of(r) && 4 * waste <= max(rows_per_cta, 16)) {
+                    rg = r;
+                    stages = d;
+                }
+            }
+            for (int r = 4; r >= 1 && !rg; r >>= 1) {
+                const int d = depth(r, 4);
+                if (d >= min(4, chunks_of(r))) {
+                    rg = r;
+                    stages = d;
+                }
+            }
+            for (int r = 4; r >= 1 && !rg; r >>= 1) {
+                const int d = depth(r, 4);
+                if (d) {
+                    rg = r;
+                    stages = d;
+                }
+            }
+            if (!rg) return cudaErrorNotSupported;
+            const bool prefetched = stages >= chunks_of(rg);
+            if (!any_shape && !(prefetched && rows_per_cta >= 24)) return cudaErrorNotSupported;
+            GemvMmaArgs a;
+            a.W = W;
+            a.x = x;
+            a.y = y;
+            a.N = N;
+            a.nb = nb;
+            a.row_bytes = (uint32_t)row_bytes;
+            a.pitch = (uint32_t)pitch;
+            a.stage_stride = (uint32_t)stride(rg);
+            a.stages = stages;
+            a.chunks_per_flush = (int)(part_floats(rg) / ((size_t)16 * rg * kMmaWarps));
+            a.status = c.status;
+            const size_t smem = (size_t)stages * a.stage_stride + x_bytes + 4 * part_floats(rg);
+            switch (rg) {
+                case 4: return launch_mma<4>(c, a, G, smem);
+                case 2: return launch_mma<2>(c, a, G, smem);
+                default: return launch_mma<1>(c, a, G, smem);
+            }
+        }
+        template <int RG>
+        static cudaError_t launch_mma(const mgpu_k::LaunchCtx& c, const GemvMmaArgs& a, int G, size_t smem) {
+            auto kern = gemv_q_mma<QT, RG, XT, YT>;
+            static thread_local uint64_t configured = 0;  // one bit per device ordinal
+            int ordinal = 0;
+            cudaGetDevice(&ordinal);
+            if (!(configured & (1ull << (ordinal & 63)))) {
+                cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     (int)kGemvMmaSmemBudget);
+                if (e != cudaSuccess) return e;
+                e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (int)cudaSharedmemCarveoutMaxShared);
+                if (e != cudaSuccess) return e;
+                configured |= 1ull << (ordinal & 63);
+            }
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(G);
+            cfg.blockDim = dim3(kGemvThreads);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = c.stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+#ifdef MGPU_GEMV_NO_PDL
+            cfg.numAttrs = 0;
+#else
+            cfg.numAttrs = 1;
+#endif
+            return cudaLaunchKernelEx(&cfg, kern, a);
         }
         template <int RPT, typename XT2, typename YT2>
         static cudaError_t launch(const mgpu_k::LaunchCtx& c, const GemvQArgs& a, int G, size_t smem) {

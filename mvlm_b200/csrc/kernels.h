@@ -51,9 +51,25 @@ struct GemmOperand {
     int layout;   // MGPU_LAYOUT_KN / MGPU_LAYOUT_NK (B only)
     int64_t ld;   // row pitch in elements (dense) or bytes (quantised rows)
 };
-// C[M,N] = A[M,K] * op(B) (+ bias[N]); A row-major [M][lda].
+// How gemm() runs a shape: B mode, tile, and split-K.
+struct GemmPlan {
+    int bmode, BN, mt, tiles_m, tiles_n, num_kb, splits, kb_per_split;
+};
+GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, int M, int N, int K);
+// Split-K scratch: one ticket per output tile (zero between calls; the kernel leaves it so)
+// and fp32 partials for splits x M x N.
+struct GemmSplitScratch {
+    unsigned int* tickets;
+    size_t max_tickets;
+    float* partials;
+    size_t max_partials;  // floats
+};
+// Bytes of fp32 partials gemm() uses for this shape (0: it does not split K).
+size_t gemm_split_bytes(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, int M, int N, int K);
+// C[M,N] = A[M,K] * op(B) (+ bias[N]); A row-major [M][lda].  `split` may be null (no
+// split-K, whatever the plan says).
 cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
-                 const void* bias, int bias_type, int M, int N, int K);
+                 const void* bias, int bias_type, int M, int N, int K, const GemmSplitScratch* split);
 // Why a GEMM request cannot run (nullptr when it can).
 const char* gemm_check(const GemmOperand& A, const GemmOperand& B, const GemmOperand& C, int M, int N, int K);
 

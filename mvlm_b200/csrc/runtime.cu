@@ -104,10 +104,14 @@ bool is_float_type(int t) { return t == MGPU_F32 || t == MGPU_F16 || t == MGPU_B
 bool is_quant_type(int t) { return t == MGPU_Q4_0 || t == MGPU_Q8_0; }
 size_t quant_row_bytes(int t, int64_t k) { return (size_t)((k + 31) / 32) * (t == MGPU_Q4_0 ? 18 : 34); }
 
-// Scratch arena layout: [0, kScratchOffset) holds the split-K tickets of gemv_kn, which
-// must stay zero between launches (the kernel resets them); everything after it is free
-// for per-call use (split-K partials, im2col patches, staged operands), in stream order.
-constexpr size_t kScratchOffset = 64 * 1024;
+// Scratch arena layout: [0, 64 KB) holds the split-K tickets of gemv_kn and [64 KB, 128 KB)
+// those of the split-K GEMM; both must stay zero between launches (the kernels reset them).
+// Everything from kScratchOffset on is free for per-call use (split-K partials, im2col
+// patches, staged operands), in stream order.
+constexpr size_t kGemvTicketBytes = 64 * 1024;
+constexpr size_t kGemmTicketOffset = 64 * 1024;
+constexpr size_t kGemmTicketBytes = 64 * 1024;
+constexpr size_t kScratchOffset = 128 * 1024;
 
 mgpu_k::LaunchCtx ctx_of(const mgpu_device* d) {
     mgpu_k::LaunchCtx c;
@@ -129,12 +133,19 @@ bool ensure_workspace(mgpu_device* d, size_t bytes) {
     }
     size_t want = std::max(bytes, d->workspace_bytes * 2);
     want = (want + 4095) & ~(size_t)4095;
-    if (!cuda_ok(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize")) return false;
+    // The new arena is zeroed and then takes the old one's contents, so that a caller that
+    // has already staged data in the arena (e.g. im2col patches before their GEMM) keeps it.
+    void* fresh = nullptr;
+    if (!cuda_ok(cudaMalloc(&fresh, want), "cudaMalloc(workspace)")) return false;
+    if (!cuda_ok(cudaMemsetAsync(fresh, 0, want, d->stream), "cudaMemsetAsync(workspace)") ||
+        (d->workspace && !cuda_ok(cudaMemcpyAsync(fresh, d->workspace, d->workspace_bytes, cudaMemcpyDeviceToDevice,
+                                                  d->stream), "cudaMemcpyAsync(workspace)")) ||
+        !cuda_ok(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize")) {
+        cudaFree(fresh);
+        return false;
+    }
     if (d->workspace) cudaFree(d->workspace);
-    d->workspace = nullptr;
-    d->workspace_bytes = 0;
-    if (!cuda_ok(cudaMalloc(&d->workspace, want), "cudaMalloc(workspace)")) return false;
-    if (!cuda_ok(cudaMemsetAsync(d->workspace, 0, want, d->stream), "cudaMemsetAsync(workspace)")) return false;
+    d->workspace = fresh;
     d->workspace_bytes = want;
     return true;
 }
@@ -222,13 +233,16 @@ bool gemm_checked(mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M
     auto misaligned = [](const void* p, int64_t ld) { return ((uintptr_t)p & 15) || (ld * 2) % 16; };
     const bool stage_a = misaligned(a.ptr, a.ld);
     const bool stage_b = !is_quant_type(B->type) && misaligned(b.ptr, b.ld);
+    const int64_t a_ld = (K + 7) / 8 * 8;
+    const int64_t b_rows = B->layout == MGPU_LAYOUT_NK ? N : K, b_cols = B->layout == MGPU_LAYOUT_NK ? K : N;
+    const int64_t b_ld = (b_cols + 7) / 8 * 8;
+    const size_t a_bytes = stage_a ? (((size_t)M * a_ld * 2 + 255) & ~(size_t)255) : 0;
+    const size_t b_bytes = stage_b ? (((size_t)b_rows * b_ld * 2 + 255) & ~(size_t)255) : 0;
+    // split-K partials (skinny M) go after the staged operands
+    const size_t split_bytes = mgpu_k::gemm_split_bytes(ctx_of(dev), a, b, M, N, K);
+    if (stage_a || stage_b || split_bytes)
+        if (!ensure_workspace(dev, scratch_base + a_bytes + b_bytes + split_bytes)) return false;
     if (stage_a || stage_b) {
-        const int64_t a_ld = (K + 7) / 8 * 8;
-        const int64_t b_rows = B->layout == MGPU_LAYOUT_NK ? N : K, b_cols = B->layout == MGPU_LAYOUT_NK ? K : N;
-        const int64_t b_ld = (b_cols + 7) / 8 * 8;
-        const size_t a_bytes = stage_a ? (((size_t)M * a_ld * 2 + 255) & ~(size_t)255) : 0;
-        const size_t b_bytes = stage_b ? (size_t)b_rows * b_ld * 2 : 0;
-        if (!ensure_workspace(dev, scratch_base + a_bytes + b_bytes)) return false;
         char* ws = (char*)dev->workspace + scratch_base;
         if (stage_a) {
             if (!cuda_ok(cudaMemcpy2DAsync(ws, a_ld * 2, a.ptr, a.ld * 2, (size_t)K * 2, M, cudaMemcpyDeviceToDevice,
@@ -253,7 +267,15 @@ bool gemm_checked(mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M
         GREQ(is_float_type(bias->type) && bias->bytes >= (size_t)N * elem_size(bias->type),
              "%s: bias must hold N float values", who);
 #undef GREQ
-    cudaError_t e = mgpu_k::gemm(ctx_of(dev), a, b, c, bias ? bias->ptr : nullptr, bias ? bias->type : 0, M, N, K);
+    mgpu_k::GemmSplitScratch split{};
+    if (split_bytes) {
+        split.tickets = (unsigned int*)((char*)dev->workspace + kGemmTicketOffset);
+        split.max_tickets = kGemmTicketBytes / sizeof(unsigned int);
+        split.partials = (float*)((char*)dev->workspace + scratch_base + a_bytes + b_bytes);
+        split.max_partials = split_bytes / sizeof(float);
+    }
+    cudaError_t e = mgpu_k::gemm(ctx_of(dev), a, b, c, bias ? bias->ptr : nullptr, bias ? bias->type : 0, M, N, K,
+                                 split_bytes ? &split : nullptr);
     return cuda_ok(e, who);
 }
 
@@ -598,7 +620,7 @@ mgpu_event* mgpu_dispatch_gemv(const mgpu_device* cd, mgpu_program, mgpu_buf* x,
         const int64_t ld = ld_or(W, N);
         REQUIRE(ld >= N && W->bytes >= ((size_t)(K - 1) * ld + N) * elem_size(W->type), "dispatch_gemv: W too small");
         const size_t need = mgpu_k::gemv_kn_scratch_bytes(N, K, d->sm_count, nullptr);
-        REQUIRE((size_t)((N + 255) / 256) * 4 <= kScratchOffset, "dispatch_gemv: N=%d too large for KN layout", N);
+        REQUIRE((size_t)((N + 255) / 256) * 4 <= kGemvTicketBytes, "dispatch_gemv: N=%d too large for KN layout", N);
         if (!ensure_workspace(d, kScratchOffset + need)) return nullptr;
         unsigned int* counters = (unsigned int*)d->workspace;
         float* partials = (float*)((char*)d->workspace + kScratchOffset);

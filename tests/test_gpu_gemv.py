@@ -47,7 +47,7 @@ def test_gemv_q_io_types(dev, qt, xt, yt):
 
 
 @pytest.mark.parametrize("K,N", [(32, 1), (96, 7), (1152, 33), (4096, 5), (16384, 64), (1024, 1), (2048, 3),
-                                 (8192, 300)])
+                                 (8192, 300), (3072, 500), (5120, 129), (7168, 40), (6144, 4000)])
 @pytest.mark.parametrize("qt", [O.Q4_0, O.Q8_0])
 def test_gemv_q_ragged(dev, qt, K, N):
     x = O.uniform(K, K + N)
