@@ -744,13 +744,21 @@ GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& 
 }
 
 size_t gemm_split_bytes(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, int M, int N, int K) {
+    if (skinny_ok(A, B, M, N, K)) return 0;
     const GemmPlan p = plan_gemm(c, A, B, M, N, K);
     return p.splits > 1 ? (size_t)p.splits * M * N * sizeof(float) : 0;
+}
+
+bool make_tensor_map_u16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,
+                         int box_rows) {
+    return make_map_plain(m, ptr, rows, cols, ld, box_cols, box_rows);
 }
 
 cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
                  const void* bias, int bias_type, int M, int N, int K, const GemmSplitScratch* split) {
     if (gemm_check(A, B, C, M, N, K)) return cudaErrorInvalidValue;
+    // A few sequences against Q4_0 weights (batched decode): the streaming skinny kernel.
+    if (skinny_ok(A, B, M, N, K)) return gemm_q4_skinny(c, A, B, C, bias, bias_type, M, N, K);
     GemmPlan p = plan_gemm(c, A, B, M, N, K);
     if (p.splits > 1 && (!split || !split->tickets || !split->partials ||
                          (size_t)p.splits * M * N > split->max_partials ||

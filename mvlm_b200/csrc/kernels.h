@@ -1,5 +1,6 @@
 // kernels.h - host-side launchers of the sm_100a kernels (internal to libmgpu).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -70,6 +71,14 @@ size_t gemm_split_bytes(const LaunchCtx& c, const GemmOperand& A, const GemmOper
 // split-K, whatever the plan says).
 cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
                  const void* bias, int bias_type, int M, int N, int K, const GemmSplitScratch* split);
+// Skinny GEMM for batched decode (skinny.cu): Q4_0 W [N][K/32] rows, bf16/fp16 A, M <= 32.
+bool skinny_ok(const GemmOperand& A, const GemmOperand& B, int M, int N, int K);
+cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
+                           const void* bias, int bias_type, int M, int N, int K);
+// A 2-D TMA map over 16-bit units without swizzle: `rows` x `cols`, row pitch `ld` units, box
+// {box_cols, box_rows} (gemm_tc.cu).
+bool make_tensor_map_u16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,
+                         int box_rows);
 // Why a GEMM request cannot run (nullptr when it can).
 const char* gemm_check(const GemmOperand& A, const GemmOperand& B, const GemmOperand& C, int M, int N, int K);
 

@@ -130,3 +130,23 @@ def test_gemm_rejects_bad_arguments(dev):
     with pytest.raises(mg.MgpuError):
         mg.dispatch_gemm_naive(dev, None, A, Bb, C, 8, 8, 8)  # mixed fp16 / bf16 operands
     dev.finish()
+
+
+@pytest.mark.parametrize("at", [mg.BF16, mg.F16])
+@pytest.mark.parametrize("M,N,K", [(1, 100, 256), (3, 2048, 2048), (8, 6144, 2048), (13, 1000, 512),
+                                   (40, 2048, 8192), (128, 4096, 2048), (32, 51200, 2048)])
+def test_skinny_q4_batched_decode(dev, at, M, N, K):
+    # batched decode: M sequences against GGUF Q4_0 weights (the streaming skinny kernel)
+    A = O.normal(M * K, 3 * M + K, 1.0)
+    A16 = O.bf16(A) if at == mg.BF16 else O.f16(A)
+    A32 = O.bf16_to_f32(A16) if at == mg.BF16 else O.f16_to_f32(A16)
+    W = O.quantize(O.normal(N * K, N + 11, 0.02), O.Q4_0)
+    bias = O.normal(N, N + 5, 0.1)
+    ref = O.gemm_q(A32, W, M, N, K, O.Q4_0, threads=True).reshape(M, N) + bias[None, :]
+    for ct in (mg.F32, mg.BF16, mg.F16):
+        dC = dev.empty(M * N, ct)
+        mg.gemm_q(dev, dev.array(A16, at), dev.array(W, O.Q4_0, mg.LAYOUT_NK), dC, M, N, K, O.Q4_0,
+                  bias=dev.array(bias, mg.F32)).wait()
+        C = dC.read(mg.NP_DTYPE[ct])
+        C = O.bf16_to_f32(C) if ct == mg.BF16 else O.f16_to_f32(C) if ct == mg.F16 else C
+        assert_close(C, ref.reshape(-1), TOL_16, f"skinny {M}x{N}x{K} a{at} c{ct}")
