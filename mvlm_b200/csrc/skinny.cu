@@ -13,8 +13,10 @@
 //     cost ~50 ns of issue each, which serialised the ring.  Weights are never written by the
 //     preceding kernel, so the first slices stream before griddepcontrol.wait; activations
 //     after it.
-//   * Eight consumer warps: warp w takes 16-row group (w % RG) and blocks of the slice
-//     (RG of the 8, so the 8/RG warps of a row group split K).  Every warp consumes every
+//   * A stage holds 1, 2 or 4 such 256-k sub-slices, so that each warp has several independent
+//     blocks to decode per stage (one block per stage left a warp with a single serial chain).
+//   * Eight consumer warps: warp w takes 16-row group (w % RG) and a contiguous run of the
+//     stage's blocks (the 8/RG warps of a row group split K).  Every warp consumes every
 //     stage, in order, so a warp's parity wait on a slot is never more than one phase ahead.  A lane turns its two quant
 //     bytes per row and block into bf16 / fp16 pairs: nibble | 0x4300 (bf16 128 + q) or
 //     | 0x6400 (fp16 1024 + q), minus 136 / 1032 gives q - 8 exactly, times the block's d.
@@ -50,8 +52,9 @@ struct SkinnyArgs {
     int bias_type;
     int S, N, K;
     int stages;
-    uint32_t stage_bytes;  // one stage: TR x 144 weight bytes, then 2 x 8 NT x 272 activation bytes
-    uint32_t x_offset;     // offset of the activation rows inside a stage
+    uint32_t sub_bytes;    // one sub-slice: TR x 144 weight bytes, then 2 x 8 NT x 272 activation bytes
+    uint32_t stage_bytes;  // subs x sub_bytes, rounded up to 1 KB
+    uint32_t x_offset;     // offset of the activation rows inside a sub-slice
     int* status;
 };
 
@@ -120,13 +123,14 @@ __device__ __forceinline__ void store_value(void* C, int type, size_t idx, float
     else reinterpret_cast<__nv_bfloat16*>(C)[idx] = __float2bfloat16_rn(v);
 }
 
-// NT = 8-sequence tiles per CTA (S per CTA <= 8 NT); RG = 16-row groups per chunk.
-template <int NT, int RG, typename T>
+// NT = 8-sequence tiles per CTA (S per CTA <= 8 NT); RG = 16-row groups per chunk; SUBS =
+// 256-k sub-slices per stage.
+template <int NT, int RG, int SUBS, typename T>
 __global__ void __launch_bounds__(kSkThreads, 1)
     gemm_q4_skinny(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, SkinnyArgs a) {
     constexpr int TR = 16 * RG;         // rows per chunk
     constexpr int WPG = 8 / RG;         // warps per row group (split K)
-    constexpr int BPW = 8 / WPG;        // blocks of a slice per warp
+    constexpr int BPW = RG * SUBS;      // blocks of a stage per warp
     constexpr int SP = 8 * NT;          // sequences per CTA
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -144,7 +148,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     const int seq0 = blockIdx.y * SP;
     const int ns = min(SP, a.S - seq0);  // sequences of this CTA
     const int nchunks = (r1 - r0 + TR - 1) / TR;
-    const int nslices = a.K / kSkSlice;
+    const int nslices = a.K / (kSkSlice * SUBS);  // stages per chunk
     const int total = nchunks * nslices;
     float* red = reinterpret_cast<float*>(smem + (size_t)a.stages * a.stage_bytes);  // [WPG][TR][SP]
 
@@ -165,17 +169,21 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         if (lane == 0) {
             prefetch_tensormap(&tmW);
             prefetch_tensormap(&tmX);
-            const uint32_t bytes = (uint32_t)TR * kSkWRowBytes + 2u * SP * kSkXPitch;
+            const uint32_t bytes = (uint32_t)SUBS * a.sub_bytes;
             auto w_load = [&](int it, int s) {
                 const int c = it / nslices, ks = it % nslices;
-                tma_load_2d(smem + (size_t)s * a.stage_bytes, &tmW, ks * (kSkWRowBytes / 2), r0 + c * TR,
-                            &full_bar[s]);
+                for (int u = 0; u < SUBS; ++u)
+                    tma_load_2d(smem + (size_t)s * a.stage_bytes + (size_t)u * a.sub_bytes, &tmW,
+                                (ks * SUBS + u) * (kSkWRowBytes / 2), r0 + c * TR, &full_bar[s]);
             };
             auto x_load = [&](int it, int s) {
                 const int ks = it % nslices;
-                uint8_t* xdst = smem + (size_t)s * a.stage_bytes + a.x_offset;
-                tma_load_2d(xdst, &tmX, ks * kSkSlice, seq0, &full_bar[s]);
-                tma_load_2d(xdst + SP * kSkXPitch, &tmX, ks * kSkSlice + 128, seq0, &full_bar[s]);
+                for (int u = 0; u < SUBS; ++u) {
+                    uint8_t* xdst = smem + (size_t)s * a.stage_bytes + (size_t)u * a.sub_bytes + a.x_offset;
+                    const int k0 = (ks * SUBS + u) * kSkSlice;
+                    tma_load_2d(xdst, &tmX, k0, seq0, &full_bar[s]);
+                    tma_load_2d(xdst + SP * kSkXPitch, &tmX, k0 + 128, seq0, &full_bar[s]);
+                }
             };
             // weights of the first stages before the dependency wait, activations after it
             const int pre = min(a.stages, total);
@@ -218,13 +226,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
         for (int ks = 0; ks < nslices; ++ks) {
             if (!mbar_wait(&full_bar[s], ph, a.status)) return;
-            const uint8_t* wst = smem + (size_t)s * a.stage_bytes;
-            const uint8_t* xst = wst + a.x_offset;
-            const uint8_t* rowg = wst + (size_t)(rg * 16 + g) * kSkWRowBytes;
-            const uint8_t* rowg8 = rowg + 8 * kSkWRowBytes;
+            const uint8_t* stg = smem + (size_t)s * a.stage_bytes;
 #pragma unroll
             for (int bi = 0; bi < BPW; ++bi) {
-                const int b = kw * BPW + bi;  // block within the slice
+                const int bb = kw * BPW + bi;  // block within the stage
+                const uint8_t* wst = stg + (size_t)(bb >> 3) * a.sub_bytes;  // its sub-slice
+                const uint8_t* xst = wst + a.x_offset;
+                const int b = bb & 7;                                         // block within the sub-slice
+                const uint8_t* rowg = wst + (size_t)(rg * 16 + g) * kSkWRowBytes;
+                const uint8_t* rowg8 = rowg + 8 * kSkWRowBytes;
                 // quant bytes 2t, 2t+1 (elements 2t, 2t+1 and 16+2t, 17+2t) and 8+2t, 9+2t
                 const uint8_t* qg = rowg + b * 18 + 2;
                 const uint8_t* qg8 = rowg8 + b * 18 + 2;
@@ -295,10 +305,10 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     }
 }
 
-template <int NT, int RG, typename T>
+template <int NT, int RG, int SUBS, typename T>
 cudaError_t launch_skinny(const mgpu_k::LaunchCtx& c, const CUtensorMap& tm, const CUtensorMap& tx,
                           const SkinnyArgs& a, dim3 grid, size_t smem) {
-    auto kern = gemm_q4_skinny<NT, RG, T>;
+    auto kern = gemm_q4_skinny<NT, RG, SUBS, T>;
     static thread_local uint64_t configured = 0;  // one bit per device ordinal
     int ordinal = 0;
     cudaGetDevice(&ordinal);
@@ -324,13 +334,15 @@ cudaError_t launch_skinny(const mgpu_k::LaunchCtx& c, const CUtensorMap& tm, con
 }
 
 template <int NT, typename T>
-cudaError_t dispatch_rg(const mgpu_k::LaunchCtx& c, int rg, const CUtensorMap& tm, const CUtensorMap& tx,
+cudaError_t dispatch_rg(const mgpu_k::LaunchCtx& c, int rg, int subs, const CUtensorMap& tm, const CUtensorMap& tx,
                         const SkinnyArgs& a, dim3 grid, size_t smem) {
-    switch (rg) {
-        case 4: return launch_skinny<NT, 4, T>(c, tm, tx, a, grid, smem);
-        case 2: return launch_skinny<NT, 2, T>(c, tm, tx, a, grid, smem);
-        default: return launch_skinny<NT, 1, T>(c, tm, tx, a, grid, smem);
-    }
+    // (row groups, sub-slices): at most 4 blocks per warp per stage
+    if (rg == 4) return launch_skinny<NT, 4, 1, T>(c, tm, tx, a, grid, smem);
+    if (rg == 2) return subs == 2 ? launch_skinny<NT, 2, 2, T>(c, tm, tx, a, grid, smem)
+                                  : launch_skinny<NT, 2, 1, T>(c, tm, tx, a, grid, smem);
+    return subs == 4 ? launch_skinny<NT, 1, 4, T>(c, tm, tx, a, grid, smem)
+         : subs == 2 ? launch_skinny<NT, 1, 2, T>(c, tm, tx, a, grid, smem)
+                     : launch_skinny<NT, 1, 1, T>(c, tm, tx, a, grid, smem);
 }
 
 }  // namespace
@@ -358,8 +370,14 @@ cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmO
     while (RG < 4 && 16 * RG < rows_per_cta) RG <<= 1;
     const int TR = 16 * RG;
     const uint32_t x_offset = (uint32_t)((TR * kSkWRowBytes + 127) / 128 * 128);
-    const uint32_t stage_bytes = (uint32_t)((x_offset + 2 * SP * kSkXPitch + 1023) / 1024 * 1024);
+    const uint32_t sub_bytes = x_offset + 2 * SP * kSkXPitch;  // a multiple of 128
     const size_t red_bytes = (size_t)(8 / RG) * TR * SP * sizeof(float);
+    // sub-slices per stage: up to 4 blocks per warp, dividing K / 256, with at least 2 stages
+    int subs = 4 / RG;
+    auto stage_of = [&](int u) { return ((size_t)u * sub_bytes + 1023) / 1024 * 1024; };
+    while (subs > 1 && ((K / kSkSlice) % subs != 0 || 2 * stage_of(subs) + red_bytes + 1024 > kSkSmemBudget))
+        subs >>= 1;
+    const uint32_t stage_bytes = (uint32_t)stage_of(subs);
     const int stages = (int)std::min<size_t>(kSkMaxStages, (kSkSmemBudget - 1024 - red_bytes) / stage_bytes);
     if (stages < 2) return cudaErrorInvalidValue;
     const size_t smem = 1024 + (size_t)stages * stage_bytes + red_bytes;
@@ -383,15 +401,16 @@ cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmO
     a.N = N;
     a.K = K;
     a.stages = stages;
+    a.sub_bytes = sub_bytes;
     a.stage_bytes = stage_bytes;
     a.x_offset = x_offset;
     a.status = c.status;
     const dim3 grid(G, (M + SP - 1) / SP);
     const bool bf16 = A.type == MGPU_BF16;
     switch (NT) {
-        case 1: return bf16 ? dispatch_rg<1, __nv_bfloat16>(c, RG, tm, tx, a, grid, smem) : dispatch_rg<1, __half>(c, RG, tm, tx, a, grid, smem);
-        case 2: return bf16 ? dispatch_rg<2, __nv_bfloat16>(c, RG, tm, tx, a, grid, smem) : dispatch_rg<2, __half>(c, RG, tm, tx, a, grid, smem);
-        default: return bf16 ? dispatch_rg<4, __nv_bfloat16>(c, RG, tm, tx, a, grid, smem) : dispatch_rg<4, __half>(c, RG, tm, tx, a, grid, smem);
+        case 1: return bf16 ? dispatch_rg<1, __nv_bfloat16>(c, RG, subs, tm, tx, a, grid, smem) : dispatch_rg<1, __half>(c, RG, subs, tm, tx, a, grid, smem);
+        case 2: return bf16 ? dispatch_rg<2, __nv_bfloat16>(c, RG, subs, tm, tx, a, grid, smem) : dispatch_rg<2, __half>(c, RG, subs, tm, tx, a, grid, smem);
+        default: return bf16 ? dispatch_rg<4, __nv_bfloat16>(c, RG, subs, tm, tx, a, grid, smem) : dispatch_rg<4, __half>(c, RG, subs, tm, tx, a, grid, smem);
     }
 }
 
