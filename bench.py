@@ -117,6 +117,9 @@ class ClockSampler:
 # --------------------------------------------------------------------------------------
 def cpu_baseline(budget_s: float = 12.0) -> dict:
     import oracle as O
+    # all the host threads this process may run on (torchrun sets OMP_NUM_THREADS=1 per rank;
+    # only rank 0 runs this)
+    O.set_threads(len(os.sched_getaffinity(0)))
     shapes = [(K, N) for _, K, N in LAYER_SHAPES] + [(HEAD[1], HEAD[2])]
     mats = []
     for i, (K, N) in enumerate(shapes):

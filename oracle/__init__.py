@@ -70,6 +70,7 @@ def lib():
         L.ora_row_bytes.argtypes = [i32, i64]
         L.ora_row_bytes.restype = sz
         L.ora_max_threads.restype = i32
+        L.ora_set_threads.argtypes = [i32]
     return _lib
 
 
@@ -229,3 +230,8 @@ def im2col(img, C, H, W, ph, pw):
 
 def max_threads() -> int:
     return lib().ora_max_threads()
+
+
+def set_threads(n: int) -> None:
+    """Use n host threads in the multithreaded variants."""
+    lib().ora_set_threads(int(n))

@@ -312,6 +312,15 @@ void ora_im2col(const float* img, float* patches, int C, int H, int W, int ph, i
 /* ------------------------------------------------------------------------------------ */
 /* Multithreaded variants (timed CPU baseline).  Same per-output arithmetic.             */
 /* ------------------------------------------------------------------------------------ */
+/* Use n host threads in the multithreaded variants (a launcher may have set OMP_NUM_THREADS=1). */
+void ora_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 int ora_max_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -77,6 +77,7 @@ void ora_gemv_f32_kn_mt(const float* x, const float* W, float* y, int N, int K);
 void ora_gemm_naive_f32_mt(const float* A, const float* B, float* C, int M, int N, int K);
 void ora_gemm_nk_mt(const float* A, const void* W, int wtype, float* C, int M, int N, int K);
 int ora_max_threads(void);
+void ora_set_threads(int n);
 
 #ifdef __cplusplus
 }
