@@ -242,6 +242,10 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         }
         abort_flag = 0;
         fence_mbar_init();
+        // Programmatic dependent launch: the next kernel of the stream may start its prologue
+        // (and stage its own weights) on SMs this grid leaves free; it reads our output only
+        // after its griddepcontrol.wait.
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     }
     if (warp == 0 && lane == 0) {
         prefetch_tensormap(&tmA);
@@ -259,6 +263,12 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
         if (lane == 0) {
+            // A (and bias / C) may belong to the preceding kernel of the stream: wait for it.
+            // Everything that reads A or writes C is ordered after this (the MMAs consume the
+            // stages loaded here, the epilogue their accumulators).  Quantised B is staged by
+            // the dequant warps without waiting: weights are never written by the previous
+            // kernel.
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             uint32_t it = 0;
             for (int unit = blockIdx.x; unit < total_units && !abort_flag; unit += gridDim.x) {
                 const int tile = unit % total_tiles, kb0 = (unit / total_tiles) * g.kb_per_split;
@@ -647,8 +657,17 @@ cudaError_t launch_gemm(const mgpu_k::LaunchCtx& c, const CUtensorMap& ma, const
     }
     const int units = g.tiles_m * g.tiles_n * g.splits;
     const int grid = units < c.sm_count ? units : c.sm_count;
-    kern<<<grid, gemm_threads(BMODE), smem, c.stream>>>(ma, mb, g);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(gemm_threads(BMODE));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, ma, mb, g);
 }
 
 template <int BN, typename T>
