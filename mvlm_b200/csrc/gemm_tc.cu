@@ -268,16 +268,44 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             // stages loaded here, the epilogue their accumulators).  Quantised B is staged by
             // the dequant warps without waiting: weights are never written by the previous
             // kernel.
-            asm volatile("griddepcontrol.wait;" ::: "memory");
+            // Dense B of this CTA's first stages is staged before the wait too.
             uint32_t it = 0;
+            int pre = 0;
+            if constexpr (!kQuant) {
+                if ((int)blockIdx.x < total_units) {
+                    const int tile = (int)blockIdx.x % total_tiles, kb0 = ((int)blockIdx.x / total_tiles) * g.kb_per_split;
+                    const int n_blk = tile / g.tiles_m;
+                    pre = min(S, g.kb_per_split);
+                    for (int p = 0; p < pre; ++p) {
+                        // fresh ring: every slot is free
+                        uint8_t* b_dst = smem + p * SB + AB;
+                        mbar_arrive_expect_tx(&full_bar[p], (uint32_t)(AB + BN * BK * 2));
+                        if constexpr (BMODE == B_TMA_K) {
+                            tma_load_2d(b_dst, &tmB, (kb0 + p) * BK, n_blk * BN, &full_bar[p]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < BN / 64; ++j)
+                                tma_load_2d(b_dst + j * 8192, &tmB, n_blk * BN + j * 64, (kb0 + p) * BK, &full_bar[p]);
+                        }
+                    }
+                }
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int unit = blockIdx.x; unit < total_units && !abort_flag; unit += gridDim.x) {
                 const int tile = unit % total_tiles, kb0 = (unit / total_tiles) * g.kb_per_split;
                 const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
                 for (int kb = kb0; kb < kb0 + g.kb_per_split; ++kb, ++it) {
                     const uint32_t s = it % S, ph = (it / S) & 1u;
-                    if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
                     uint8_t* a_dst = smem + s * SB;
                     uint8_t* b_dst = a_dst + AB;
+                    if ((int)it < pre) {
+                        // B already in flight: A only
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt)
+                            tma_load_2d(a_dst + mt * kABytes, &tmA, kb * BK, m_blk * TBM + mt * BM, &full_bar[s]);
+                        continue;
+                    }
+                    if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
                     const uint32_t tx = AB + (kQuant ? 0u : (uint32_t)(BN * BK * 2));
                     mbar_arrive_expect_tx(&full_bar[s], tx);
 #pragma unroll
