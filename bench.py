@@ -275,8 +275,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         ms, head_ms = float(t[0]), float(t[1])
 
     # ---------------- e2e through the C ABI with host buffers ----------------
+    y_full_buf = dev.wrap(y_full.data_ptr(), HEAD[2] * 4, mg.F32) if world > 1 else None
     e2e = run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, dist, gather_logits, torch,
-                  stream)
+                  stream, y_full_buf)
 
     # ---------------- prefill GEMMs (secondary metric) ----------------
     prefill = run_prefill(dev, mg, torch, stream, peaks) if rank == 0 and not args.no_prefill else None
@@ -337,37 +338,59 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
 
 def run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, dist, gather_logits, torch,
-            stream) -> dict:
-    """Public-API loop with pinned host buffers: per step every activation vector goes
-    host->device and every output device->host; dispatches through mgpu_gemv_q."""
+            stream, y_full_buf=None) -> dict:
+    """The step through the public C ABI, from pinned host memory to pinned host memory, the way
+    an engine drives it: the step's 97 activation vectors live in one device arena (views from
+    mgpu_buf_view), so one mgpu_buf_write_async moves them all; the 97 mgpu_gemv_q dispatches
+    are captured once with mgpu_capture_begin/end and replayed with mgpu_graph_launch; one
+    mgpu_buf_read_async returns every layer output.  The logits: on one GPU they are in the same
+    arena; on N GPUs each rank's shard is all-gathered (NCCL over NVLink) and the full logits
+    are read back with a second mgpu_buf_read_async.  Device time of the whole loop, copies
+    included, by CUDA events on the stream."""
     L = mg.lib()
-    xs = [(x, K) for mats in layers for (_, K, _, _, x, _) in mats] + [(xh, K_h)]
-    ys = [(y, N) for mats in layers for (_, _, N, _, _, y) in mats] + [(yh, n_head)]
-    h2d = sum(K * 4 for _, K in xs)
-    d2h = sum(N * 4 for _, N in ys)
+    shapes = [(K, N, W) for mats in layers for (_, K, N, W, _, _) in mats] + [(K_h, n_head, Wh)]
+    h2d = sum(K * 4 for K, _, _ in shapes)
+    y_shapes = shapes if world == 1 else shapes[:-1]  # N>1: the logit shard goes to yh, then all-gathered
+    y_bytes = sum(N * 4 for _, N, _ in y_shapes)
+    logit_bytes = 0 if world == 1 else HEAD[2] * 4
+    d2h = y_bytes + logit_bytes
+    x_arena = dev.create_buffer(h2d, None, mg.F32)
+    y_arena = dev.create_buffer(y_bytes, None, mg.F32)
+    xv, yv = [], []
+    xo = yo = 0
+    for K, N, _ in shapes:
+        xv.append(x_arena.view(xo, K * 4))
+        xo += K * 4
+    for _, N, _ in y_shapes:
+        yv.append(y_arena.view(yo, N * 4))
+        yo += N * 4
+    if world > 1:
+        yv.append(yh)
     hx = L.mgpu_host_alloc(h2d)
     hy = L.mgpu_host_alloc(d2h)
     try:
         host_x = np.ctypeslib.as_array((np.ctypeslib.ctypes.c_float * (h2d // 4)).from_address(hx))
         host_x[:] = np.random.default_rng(SEED).standard_normal(h2d // 4).astype(np.float32)
 
+        def enqueue():
+            for (K, N, W), x, y in zip(shapes, xv, yv):
+                mg.gemv_q(dev, x, W, y, N, K, mg.Q4_0)
+
+        enqueue()  # eager pass: validates arguments outside the capture
+        dev.finish()
+        dev.capture_begin()
+        enqueue()
+        graph = dev.capture_end()
+
         def one():
-            off = 0
-            for x, K in xs:
-                L.mgpu_buf_write_async(x.h, 0, hx + off, K * 4)
-                off += K * 4
-            for mats in layers:
-                for name, K, N, W, x, y in mats:
-                    L.mgpu_gemv_q(dev.h, x.h, W.h, y.h, N, K, mg.Q4_0)
-            L.mgpu_gemv_q(dev.h, xh.h, Wh.h, yh.h, n_head, K_h, mg.Q4_0)
-            off = 0
-            for y, N in ys:
-                L.mgpu_buf_read_async(y.h, 0, hy + off, N * 4)
-                off += N * 4
+            mg._check(L.mgpu_buf_write_async(x_arena.h, 0, hx, h2d), "buf_write_async")
+            graph.launch()
+            mg._check(L.mgpu_buf_read_async(y_arena.h, 0, hy, y_bytes), "buf_read_async")
             if world > 1:
                 gather_logits()
+                mg._check(L.mgpu_buf_read_async(y_full_buf.h, 0, hy + y_bytes, logit_bytes), "buf_read_async")
 
-        steps = max(3, min(args.steps, 200))
+        steps = max(3, min(args.steps, 2000))
         for _ in range(3):
             one()
         torch.cuda.synchronize()
@@ -377,6 +400,7 @@ def run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, d
             one()
         e1.record(stream)
         torch.cuda.synchronize()
+        del graph
         ms = e0.elapsed_time(e1) / steps
         if world > 1:
             t = torch.tensor([ms], dtype=torch.float64, device="cuda")
@@ -384,7 +408,9 @@ def run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, d
             ms = float(t[0])
         return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 5), "steps": steps,
-                "api": "mgpu_buf_write_async + mgpu_gemv_q x97 + mgpu_buf_read_async (pinned host)"}
+                "api": "mgpu_buf_write_async (all 97 inputs, one pinned buffer) + mgpu_graph_launch of the "
+                       "captured 97 mgpu_gemv_q + mgpu_buf_read_async (all outputs"
+                       + ("" if world == 1 else "; logits after an NCCL all-gather") + ")"}
     finally:
         L.mgpu_host_free(hx)
         L.mgpu_host_free(hy)
