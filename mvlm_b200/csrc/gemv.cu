@@ -820,7 +820,7 @@ __global__ void __launch_bounds__(256) gemv_nk_dense(const WT* __restrict__ W, i
 // consecutive columns of kchunk/8 rows.  Partials of split s go to partials[s][N]; the last
 // CTA of a column tile (atomic ticket) sums splits 0..S-1 in order and resets the ticket.
 constexpr int kKnCols = 256;
-template <typename WT, typename XT, typename YT>
+template <typename WT, typename XT, typename YT, bool UNROLL>
 __global__ void __launch_bounds__(256) gemv_kn_split(const WT* __restrict__ W, int64_t ldw,
                                                      const XT* __restrict__ x, YT* __restrict__ y, int N,
                                                      int K, int kchunk, float* __restrict__ partials,
@@ -838,7 +838,31 @@ __global__ void __launch_bounds__(256) gemv_kn_split(const WT* __restrict__ W, i
     for (int i = 0; i < CPT; ++i) acc[i] = 0.0f;
     const bool full_vec = (n0 + CPT <= N) && ((ldw * sizeof(WT)) % 16 == 0) &&
                           ((reinterpret_cast<uintptr_t>(W) & 15) == 0);
-    for (int k = k_begin + warp; k < k_end; k += 8) {
+    int k = k_begin + warp;
+    if (UNROLL && full_vec) {
+        // four rows per step, all loads issued before any is used: four times the bytes in
+        // flight per warp (measured faster for fp32 rows of N >= 4096, slower for N = 2048 and
+        // for 16-bit rows; the launcher decides)
+        constexpr int R = 4;
+        constexpr int V = (int)(CPT * sizeof(WT) / 16);
+        for (; k + 8 * (R - 1) < k_end; k += 8 * R) {
+            WT wv[R][CPT];
+            float xv[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const WT* wr = W + (size_t)(k + 8 * r) * ldw + n0;
+#pragma unroll
+                for (int v = 0; v < V; ++v)
+                    reinterpret_cast<uint4*>(wv[r])[v] = __ldg(reinterpret_cast<const uint4*>(wr) + v);
+                xv[r] = to_f32<XT>(x[k + 8 * r]);
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int i = 0; i < CPT; ++i) acc[i] = fmaf(xv[r], to_f32<WT>(wv[r][i]), acc[i]);
+        }
+    }
+    for (; k < k_end; k += 8) {
         const float xv = to_f32<XT>(x[k]);
         const WT* wr = W + (size_t)k * ldw + n0;
         if (full_vec) {
@@ -1182,8 +1206,12 @@ struct GemvKnLaunch {
             mgpu_k::gemv_kn_scratch_bytes(N, K, c.sm_count, &splits);
             const int kchunk = (K + splits - 1) / splits;
             dim3 grid((N + kKnCols - 1) / kKnCols, splits);
-            gemv_kn_split<WT, XT, YT><<<grid, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x, (YT*)y, N, K,
-                                                                 kchunk, partials, counters);
+            if (sizeof(WT) == 4 && N >= 4096)
+                gemv_kn_split<WT, XT, YT, true><<<grid, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x, (YT*)y,
+                                                                           N, K, kchunk, partials, counters);
+            else
+                gemv_kn_split<WT, XT, YT, false><<<grid, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x, (YT*)y,
+                                                                            N, K, kchunk, partials, counters);
             return cudaGetLastError();
         }
     };
@@ -1261,8 +1289,12 @@ cudaError_t gemv_kn_noalloc(const LaunchCtx& c, int wtype, const void* W, int64_
     const int kchunk = (K + splits - 1) / splits;
     dim3 grid(col_tiles, splits);
 #define MGPU_NA_LAUNCH(WT, XT, YT) \
-    gemv_kn_split<WT, XT, YT><<<grid, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x, (YT*)y, N, K, kchunk, \
-                                                          partials, tickets)
+    if (sizeof(WT) == 4 && N >= 4096)                                                                            \
+        gemv_kn_split<WT, XT, YT, true><<<grid, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x, (YT*)y, N, K,     \
+                                                                    kchunk, partials, tickets);                       \
+    else                                                                                                            \
+        gemv_kn_split<WT, XT, YT, false><<<grid, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x, (YT*)y, N, K,    \
+                                                                     kchunk, partials, tickets)
 #define MGPU_NA_Y(WT, XT)                                                 \
     switch (ytype) {                                                      \
         case MGPU_F32: MGPU_NA_LAUNCH(WT, XT, float); break;              \
