@@ -283,10 +283,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     prefill = run_prefill(dev, mg, torch, stream, peaks) if rank == 0 and not args.no_prefill else None
     # ---------------- the other BASELINE configs (secondary, one GPU) ----------------
     secondary = None
-    if rank == 0 and world == 1 and not args.no_secondary:
-        secondary = {"fp32_gemv": run_fp32_gemv(dev, mg, torch, stream, peaks),
-                     "batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head),
-                     "siglip": run_siglip(dev, mg, torch, stream, peaks)}
+    if not args.no_secondary:
+        if world == 1:
+            secondary = {"fp32_gemv": run_fp32_gemv(dev, mg, torch, stream, peaks),
+                         "batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head),
+                         "siglip": run_siglip(dev, mg, torch, stream, peaks)}
+        else:
+            # every rank takes part (collectives); rank 0 reports
+            secondary = {"batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head,
+                                                              world=world, dist=dist),
+                         "siglip": run_siglip(dev, mg, torch, stream, peaks, batches=(8, 64), world=world, dist=dist)}
 
     graph = None
     if world > 1:
@@ -532,11 +538,13 @@ SIGLIP_LAYER = [(1152, 3456), (1152, 1152), (1152, 4304), (4304, 1152)]  # (K, N
 SIGLIP_PROJ = [(2304, 8192), (8192, 2048)]
 
 
-def run_siglip(dev, mg, torch, stream, peaks, batches=(1, 8, 64)) -> dict:
+def run_siglip(dev, mg, torch, stream, peaks, batches=(1, 8, 64), world=1, dist=None) -> dict:
     """SigLIP encoder GEMMs at M = 729 * B with fp16 A ~N(0,1) and fp16
     weights ~N(0,0.02) in GGUF [N][K] order: one encoder layer (qkv, out, fc1, fc2) plus the
     projection MLP (2304->8192->2048), fp32 accumulate, fp16 C.  Each replay of the captured
-    sequence follows a 256 MB write that evicts L2."""
+    sequence follows a 256 MB write that evicts L2.  On N GPUs the images are batch-sharded
+    (B/N per GPU, weights replicated, no exchange); the time is the maximum over ranks and the
+    TFLOP/s are the whole batch's."""
     flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
     shapes = SIGLIP_LAYER + SIGLIP_PROJ
     tmp = dev.empty(max(K * N for K, N in shapes), mg.F32)
@@ -549,7 +557,9 @@ def run_siglip(dev, mg, torch, stream, peaks, batches=(1, 8, 64)) -> dict:
     del tmp
     out = {}
     for B in batches:
-        M = 729 * B
+        if B % world:
+            continue
+        M = 729 * (B // world)
         A = dev.empty(M * max(K for K, _ in shapes), mg.F16)
         dev.fill_normal(A, M * max(K for K, _ in shapes), SEED + 500 + B, 1.0)
         C = dev.empty(M * max(N for _, N in shapes), mg.F16)
@@ -559,44 +569,106 @@ def run_siglip(dev, mg, torch, stream, peaks, batches=(1, 8, 64)) -> dict:
                 mg.gemm(dev, A, w, C, M, N, K)
 
         ms = time_graph(dev, torch, stream, enqueue, 5 if B >= 64 else 20, flush=lambda: flush_buf.zero_())
-        flop = sum(2.0 * M * K * N for K, N in shapes)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t[0])
+        flop = sum(2.0 * M * K * N for K, N in shapes) * world
         tf = flop / (ms * 1e-3) / 1e12
-        out[f"B{B}"] = {"M": M, "tflops": round(tf, 1), "frac": round(tf / peaks["bf16_tflops"], 4),
+        out[f"B{B}"] = {"M_per_gpu": M, "tflops": round(tf, 1), "frac": round(tf / (peaks["bf16_tflops"] * world), 4),
                         "ms": round(ms, 4), "gflop": round(flop / 1e9, 1)}
         del A, C
     return {"unit": "TFLOP/s", "dtype": "f16", "gemms": "layer qkv/out/fc1/fc2 + projection 2304x8192, 8192x2048",
-            "peak": peaks["bf16_tflops"], "peak_source": peaks["source"], "batches": out}
+            "peak": peaks["bf16_tflops"], "peak_source": peaks["source"], "batches": out,
+            "parallelism": "single GPU" if world == 1 else f"batch-shard x{world} (B/{world} images per GPU)"}
 
 
-def run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head, seqs=(8, 32, 128)) -> dict:
+def run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head, seqs=(8, 32, 128), world=1,
+                       dist=None) -> dict:
     """S concurrent decode sequences, i.e. GEMMs with M = S over the 24
     layers' Q4_0 weights (the same 738 MB as the GEMV sweep, > 5x L2) plus the lm_head; bf16
-    activations ~N(0,1), bf16 outputs.  One replay = one decode step of all S sequences."""
+    activations ~N(0,1), bf16 outputs.  One replay = one decode step of all S sequences.
+    On N GPUs the sequences are sharded for the layers (S/N per GPU, weights replicated); the
+    hidden states are all-gathered and each GPU applies its column shard of the lm_head (Wh,
+    51200/N rows) to all S, then the logit shards are all-gathered (NCCL).  The time is the
+    maximum over ranks."""
     out = {}
-    wbytes = sum(w.nbytes for mats in layers for (_, _, _, w, _, _) in mats) + Wh.nbytes
+    layer_bytes = sum(w.nbytes for mats in layers for (_, _, _, w, _, _) in mats)
     maxk = max(K for mats in layers for (_, K, _, _, _, _) in mats)
-    maxn = max(max(N for mats in layers for (_, _, N, _, _, _) in mats), n_head)
+    maxn = max(N for mats in layers for (_, _, N, _, _, _) in mats)
     for S in seqs:
-        A = dev.empty(S * maxk, mg.BF16)
-        dev.fill_normal(A, S * maxk, SEED + 600 + S, 1.0)
-        C = dev.empty(S * maxn, mg.BF16)
+        if S % world:
+            continue
+        Sl = S // world
+        A = dev.empty(Sl * maxk, mg.BF16)
+        dev.fill_normal(A, Sl * maxk, SEED + 600 + S, 1.0)
+        C = dev.empty(Sl * maxn, mg.BF16)
+        hid_t = torch.empty(S * K_h, dtype=torch.bfloat16, device="cuda")
+        hid = dev.wrap(hid_t.data_ptr(), S * K_h * 2, mg.BF16)
+        hid_local = hid_t[:Sl * K_h] if world == 1 else torch.empty(Sl * K_h, dtype=torch.bfloat16, device="cuda")
+        logit_t = torch.empty(S * n_head, dtype=torch.bfloat16, device="cuda")
+        logits = dev.wrap(logit_t.data_ptr(), S * n_head * 2, mg.BF16)
+        gathered = torch.empty(world * S * n_head, dtype=torch.bfloat16, device="cuda") if world > 1 else None
 
-        def enqueue():
+        def layers_enqueue():
             for mats in layers:
                 for _, K, N, W, _, _ in mats:
-                    mg.gemm_q(dev, A, W, C, S, N, K, mg.Q4_0)
-            mg.gemm_q(dev, A, Wh, C, S, n_head, K_h, mg.Q4_0)
+                    mg.gemm_q(dev, A, W, C, Sl, N, K, mg.Q4_0)
 
-        ms = time_graph(dev, torch, stream, enqueue, 10)
-        act = sum(2 * S * (K + N) for mats in layers for (_, K, N, _, _, _) in mats) + 2 * S * (K_h + n_head)
-        flop = sum(2.0 * S * K * N for mats in layers for (_, K, N, _, _, _) in mats) + 2.0 * S * K_h * n_head
+        def head_enqueue():
+            mg.gemm_q(dev, hid, Wh, logits, S, n_head, K_h, mg.Q4_0)
+
+        if world == 1:
+            def enqueue():
+                layers_enqueue()
+                head_enqueue()
+
+            ms = time_graph(dev, torch, stream, enqueue, 10)
+        else:
+            # layers as one captured graph, the exchanges and the head between replays
+            layers_enqueue()
+            head_enqueue()
+            dev.finish()
+            dev.capture_begin()
+            layers_enqueue()
+            g_layers = dev.capture_end()
+
+            def step():
+                g_layers.launch()
+                dist.all_gather_into_tensor(hid_t, hid_local)
+                head_enqueue()
+                dist.all_gather_into_tensor(gathered, logit_t)
+
+            for _ in range(2):
+                step()
+            torch.cuda.synchronize()
+            dist.barrier()
+            reps = 10
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                step()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            del g_layers
+            ms = e0.elapsed_time(e1) / reps
+            t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t[0])
+        act = sum(2 * S * (K + N) for mats in layers for (_, K, N, _, _, _) in mats) + 2 * S * (K_h + n_head * world)
+        flop = sum(2.0 * S * K * N for mats in layers for (_, K, N, _, _, _) in mats) + 2.0 * S * K_h * n_head * world
+        # bytes every GPU streams per step: all layer weights (replicated) and its lm_head shard
+        wbytes = (layer_bytes + Wh.nbytes) * world
         gbs = (wbytes + act) / (ms * 1e-3) / 1e9
         tf = flop / (ms * 1e-3) / 1e12
-        out[f"S{S}"] = {"ms_per_step": round(ms, 4), "gbs": round(gbs, 1), "hbm_frac": round(gbs / peaks["hbm_gbs"], 4),
-                        "tflops": round(tf, 1), "tensor_frac": round(tf / peaks["bf16_tflops"], 4),
+        out[f"S{S}"] = {"ms_per_step": round(ms, 4), "gbs": round(gbs, 1),
+                        "hbm_frac": round(gbs / (peaks["hbm_gbs"] * world), 4),
+                        "tflops": round(tf, 1), "tensor_frac": round(tf / (peaks["bf16_tflops"] * world), 4),
                         "launches": 4 * len(layers) + 1}
         del A, C
     return {"weights": "Q4_0", "activations": "bf16", "layers": len(layers), "steps": out,
+            "parallelism": "single GPU" if world == 1 else
+            f"sequences x{world} for the layers, lm_head column-shard x{world}, NCCL all-gathers",
             "basis": "roofline = min(HBM x AI, tensor peak); weights stream from HBM every step"}
 
 
