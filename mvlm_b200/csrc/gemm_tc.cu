@@ -20,6 +20,14 @@
 //               K-major layout TMA would have produced, then fence.proxy.async + arrive.
 // B layouts: NK (K-major, e.g. GGUF F16 tensors) and KN (MN-major: the reference kernels'
 // B[K][N], read by tcgen05 with the B-transpose bit).  Every TMA load fills only the issuing CTA.
+//
+// CTA pairs (CG = 2): a (2,1,1) cluster computes a 256 x BN tile with tcgen05 cta_group::2.
+// Each CTA stages its own 128 rows of A and BN / 2 rows of B (TMA or its own dequantisers);
+// the even CTA's MMA warp issues M = 256 MMAs that read both CTAs' stages and accumulate into
+// both CTAs' TMEM.  Stage and accumulator barriers live in the even CTA (the odd CTA's TMA
+// loads count their bytes there, its dequantisers and epilogue arrive there); the MMA commits
+// arrive on the same barrier offsets of both CTAs, releasing each CTA's stages and
+// accumulators.  This halves the B operand bytes each tensor core reads per MMA.
 #include <atomic>
 #include <mutex>
 #include <type_traits>
@@ -49,16 +57,23 @@ __host__ __device__ constexpr int gemm_threads(int bmode) { return 192 + (is_qua
 // computes a 256 x BN tile as two tcgen05 accumulators that share each decoded B stage, which
 // halves the decode work per FLOP (for M = 761 each weight is decoded 3 times instead of 6);
 // the host picks MT per shape, since 256-row tiles leave SMs idle when there are few of them.
-__host__ __device__ constexpr int stage_bytes(int bn, int mt = 1) { return mt * kABytes + bn * BK * 2; }
+// CG = CTAs per tile: with CG = 2 a (2,1,1) cluster computes a 256 x BN tile with tcgen05
+// cta_group::2 MMAs (M = 256), each CTA staging 128 rows of A and BN / 2 rows of B.  Each
+// tensor core then reads half as many B bytes per MMA as with one CTA per tile, and the
+// MMA's shared-memory operand reads are what bound the one-CTA kernel (measured: a 128 x 128
+// x 16 MMA step takes ~70 ns there, with decode, A loads and everything else removed).
+__host__ __device__ constexpr int stage_bytes(int bn, int mt = 1, int cg = 1) { return mt * kABytes + (bn / cg) * BK * 2; }
 // packed-group ring (two slots) of the TMA-staged quantised modes
-__host__ __device__ constexpr int packed_bytes(int bn, int bmode) { return is_packed_tma(bmode) ? 2 * bn * group_bytes(bmode) : 0; }
-constexpr int kSmemMaxDyn = 226 * 1024;  // dynamic shared memory available next to the static barriers
-__host__ __device__ constexpr int num_stages(int bn, int bmode = B_TMA_K, int mt = 1) {
-    return is_packed_tma(bmode) ? (kSmemMaxDyn - 1024 - packed_bytes(bn, bmode)) / stage_bytes(bn, mt)
-                                : kSmemBudget / stage_bytes(bn, mt);
+__host__ __device__ constexpr int packed_bytes(int bn, int bmode, int cg = 1) {
+    return is_packed_tma(bmode) ? 2 * (bn / cg) * group_bytes(bmode) : 0;
 }
-__host__ __device__ constexpr int smem_bytes(int bn, int bmode, int mt = 1) {
-    return num_stages(bn, bmode, mt) * stage_bytes(bn, mt) + packed_bytes(bn, bmode) + 1024;
+constexpr int kSmemMaxDyn = 226 * 1024;  // dynamic shared memory available next to the static barriers
+__host__ __device__ constexpr int num_stages(int bn, int bmode = B_TMA_K, int mt = 1, int cg = 1) {
+    return is_packed_tma(bmode) ? (kSmemMaxDyn - 1024 - packed_bytes(bn, bmode, cg)) / stage_bytes(bn, mt, cg)
+                                : kSmemBudget / stage_bytes(bn, mt, cg);
+}
+__host__ __device__ constexpr int smem_bytes(int bn, int bmode, int mt = 1, int cg = 1) {
+    return num_stages(bn, bmode, mt, cg) * stage_bytes(bn, mt, cg) + packed_bytes(bn, bmode, cg) + 1024;
 }
 
 struct GemmArgs {
@@ -196,18 +211,22 @@ __device__ __forceinline__ void decode_store(const RawBlock<NW>& rb, uint4* cons
     }
 }
 
-template <int BN, int BMODE, typename T, int MT>
+template <int BN, int BMODE, typename T, int MT, int CG>
 __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
-    static_assert(MT == 1 || (MT == 2 && BN == 128), "256-row tiles use 128-column B tiles");
-    constexpr int S = num_stages(BN, BMODE, MT);
-    constexpr int SB = stage_bytes(BN, MT);
-    constexpr int TBM = BM * MT;                 // rows of a CTA tile
-    constexpr int AB = MT * kABytes;             // A bytes per stage
+    static_assert(MT == 1 || (MT == 2 && BN == 128 && CG == 1), "256-row tiles use 128-column B tiles");
+    static_assert(CG == 1 || (CG == 2 && (BMODE == B_TMA_K || BMODE == B_TMA_MN || is_packed_tma(BMODE))),
+                  "CTA pairs stage A and B by TMA");
+    constexpr int BNC = BN / CG;                 // B rows (output columns) staged by this CTA
+    constexpr int S = num_stages(BN, BMODE, MT, CG);
+    constexpr int SB = stage_bytes(BN, MT, CG);
+    constexpr int TBM = BM * MT * CG;            // rows of a tile
+    constexpr int AB = MT * kABytes;             // A bytes per stage in this CTA
     constexpr uint32_t kTmemCols = 2 * MT * BN;  // double-buffered accumulators
     constexpr bool kQuant = is_quant_mode(BMODE);
+    constexpr bool kPair = CG == 2;
     constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
-    constexpr uint32_t kIdesc = idesc_f16(kBf16, false, BMODE == B_TMA_MN, BM, BN);
+    constexpr uint32_t kIdesc = idesc_f16(kBf16, false, BMODE == B_TMA_MN, BM * CG, BN);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -225,15 +244,20 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int total_tiles = g.tiles_m * g.tiles_n;
     const int total_units = total_tiles * g.splits;  // unit = (split, tile): split-major
+    // CTA pairs walk the units together: cluster index and count stand in for the block's.
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+    const int cta0 = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int ncta = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full_bar[s], 1 + (is_packed_tma(BMODE) ? kDqWarps / 2 : kQuant ? kDqWarps : 0));
+            // the pair's stage is full when both CTAs' dequantisers have arrived (on the even CTA)
+            mbar_init(&full_bar[s], 1 + CG * (is_packed_tma(BMODE) ? BNC / 32 : kQuant ? kDqWarps : 0));
             mbar_init(&empty_bar[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull_bar[a], 1);
-            mbar_init(&tempty_bar[a], 4);
+            mbar_init(&tempty_bar[a], 4 * CG);
         }
         mbar_init(&drain_bar, 1);
         for (int p = 0; p < 2; ++p) {
@@ -252,13 +276,24 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         if (!kQuant || is_packed_tma(BMODE)) prefetch_tensormap(&tmB);
     }
     if (warp == 1) {
-        tmem_alloc(&tmem_base_slot, kTmemCols);
-        tmem_relinquish();
+        if constexpr (kPair) {
+            tmem_alloc_pair(&tmem_base_slot, kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(&tmem_base_slot, kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    // the peer arrives on (and its TMA completes bytes on) this CTA's barriers: both CTAs'
+    // barriers are initialised before either goes on
+    if constexpr (kPair) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = tmem_base_slot;
+    // the even CTA's barriers, in the cluster window (pair mode)
+    const uint32_t full0_cl = kPair ? cluster_addr(&full_bar[0], 0) : 0u;
+    const uint32_t tempty0_cl = kPair ? cluster_addr(&tempty_bar[0], 0) : 0u;
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
@@ -269,29 +304,46 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             // the dequant warps without waiting: weights are never written by the previous
             // kernel.
             // Dense B of this CTA's first stages is staged before the wait too.
+            // In pair mode every load of either CTA counts its bytes on the even CTA's barrier,
+            // and only the even CTA announces them (for both CTAs).
+            auto expect = [&](uint32_t s) {
+                if (!kPair || rank == 0)
+                    mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(CG * (AB + (kQuant ? 0 : BNC * BK * 2))));
+            };
+            auto load = [&](uint8_t* dst, int x, int y, uint32_t s, const CUtensorMap* map) {
+                if constexpr (kPair) tma_load_2d_pair(dst, map, x, y, full0_cl + 8u * s);
+                else tma_load_2d(dst, map, x, y, &full_bar[s]);
+            };
+            auto load_a = [&](uint8_t* a_dst, int kb, int m_blk, uint32_t s) {
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+                    load(a_dst + mt * kABytes, kb * BK, m_blk * TBM + ((int)rank * MT + mt) * BM, s, &tmA);
+            };
+            auto load_b = [&](uint8_t* b_dst, int kb, int n_blk, uint32_t s) {
+                const int n0 = n_blk * BN + (int)rank * BNC;
+                if constexpr (BMODE == B_TMA_K) {
+                    load(b_dst, kb * BK, n0, s, &tmB);
+                } else if constexpr (BMODE == B_TMA_MN) {
+#pragma unroll
+                    for (int j = 0; j < BNC / 64; ++j) load(b_dst + j * 8192, n0 + j * 64, kb * BK, s, &tmB);
+                }
+            };
             uint32_t it = 0;
             int pre = 0;
             if constexpr (!kQuant) {
-                if ((int)blockIdx.x < total_units) {
-                    const int tile = (int)blockIdx.x % total_tiles, kb0 = ((int)blockIdx.x / total_tiles) * g.kb_per_split;
+                if (cta0 < total_units) {
+                    const int tile = cta0 % total_tiles, kb0 = (cta0 / total_tiles) * g.kb_per_split;
                     const int n_blk = tile / g.tiles_m;
                     pre = min(S, g.kb_per_split);
                     for (int p = 0; p < pre; ++p) {
                         // fresh ring: every slot is free
-                        uint8_t* b_dst = smem + p * SB + AB;
-                        mbar_arrive_expect_tx(&full_bar[p], (uint32_t)(AB + BN * BK * 2));
-                        if constexpr (BMODE == B_TMA_K) {
-                            tma_load_2d(b_dst, &tmB, (kb0 + p) * BK, n_blk * BN, &full_bar[p]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < BN / 64; ++j)
-                                tma_load_2d(b_dst + j * 8192, &tmB, n_blk * BN + j * 64, (kb0 + p) * BK, &full_bar[p]);
-                        }
+                        expect((uint32_t)p);
+                        load_b(smem + p * SB + AB, kb0 + p, n_blk, (uint32_t)p);
                     }
                 }
             }
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            for (int unit = blockIdx.x; unit < total_units && !abort_flag; unit += gridDim.x) {
+            for (int unit = cta0; unit < total_units && !abort_flag; unit += ncta) {
                 const int tile = unit % total_tiles, kb0 = (unit / total_tiles) * g.kb_per_split;
                 const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
                 for (int kb = kb0; kb < kb0 + g.kb_per_split; ++kb, ++it) {
@@ -300,41 +352,40 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                     uint8_t* b_dst = a_dst + AB;
                     if ((int)it < pre) {
                         // B already in flight: A only
-#pragma unroll
-                        for (int mt = 0; mt < MT; ++mt)
-                            tma_load_2d(a_dst + mt * kABytes, &tmA, kb * BK, m_blk * TBM + mt * BM, &full_bar[s]);
+                        load_a(a_dst, kb, m_blk, s);
                         continue;
                     }
-                    if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
-                    const uint32_t tx = AB + (kQuant ? 0u : (uint32_t)(BN * BK * 2));
-                    mbar_arrive_expect_tx(&full_bar[s], tx);
-#pragma unroll
-                    for (int mt = 0; mt < MT; ++mt)
-                        tma_load_2d(a_dst + mt * kABytes, &tmA, kb * BK, m_blk * TBM + mt * BM, &full_bar[s]);
-                    if constexpr (BMODE == B_TMA_K) {
-                        tma_load_2d(b_dst, &tmB, kb * BK, n_blk * BN, &full_bar[s]);
-                    } else if constexpr (BMODE == B_TMA_MN) {
-#pragma unroll
-                        for (int j = 0; j < BN / 64; ++j)
-                            tma_load_2d(b_dst + j * 8192, &tmB, n_blk * BN + j * 64, kb * BK, &full_bar[s]);
+                    if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) {
+                        abort_flag = 1;
+                        break;
                     }
+                    expect(s);
+                    load_a(a_dst, kb, m_blk, s);
+                    load_b(b_dst, kb, n_blk, s);
                 }
             }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
+        // (pair mode: the even CTA's lane 0 issues for both CTAs; the odd CTA's warp idles)
+        if (lane == 0 && rank == 0) {
             uint32_t it = 0, tcount = 0;
             bool issued = false;
-            for (int unit = blockIdx.x; unit < total_units && !abort_flag; unit += gridDim.x, ++tcount) {
+            for (int unit = cta0; unit < total_units && !abort_flag; unit += ncta, ++tcount) {
                 const int kb0 = (unit / total_tiles) * g.kb_per_split;
                 const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
-                if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, g.status)) { abort_flag = 1; break; }
+                if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, g.status)) {
+                    abort_flag = 1;
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * (MT * BN);
                 for (int kb = kb0; kb < kb0 + g.kb_per_split; ++kb, ++it) {
                     const uint32_t s = it % S, ph = (it / S) & 1u;
-                    if (!mbar_wait(&full_bar[s], ph, g.status)) { abort_flag = 1; break; }
+                    if (!mbar_wait(&full_bar[s], ph, g.status)) {
+                        abort_flag = 1;
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + s * SB);
                     const uint32_t b_addr = a_addr + AB;
@@ -348,18 +399,24 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
 #pragma unroll
                         for (int mt = 0; mt < MT; ++mt) {
                             const uint64_t adesc = smem_desc(a_addr + mt * kABytes + k * 32, 16, 1024, kSwizzle128B);
-                            umma_f16(d_tmem + mt * BN, adesc, bdesc, kIdesc, (kb != kb0 || k != 0) ? 1u : 0u);
+                            if constexpr (kPair)
+                                umma_f16_pair(d_tmem, adesc, bdesc, kIdesc, (kb != kb0 || k != 0) ? 1u : 0u);
+                            else
+                                umma_f16(d_tmem + mt * BN, adesc, bdesc, kIdesc, (kb != kb0 || k != 0) ? 1u : 0u);
                         }
                     }
                     issued = true;
-                    umma_commit(&empty_bar[s]);
+                    if constexpr (kPair) umma_commit_pair_both(&empty_bar[s]);
+                    else umma_commit(&empty_bar[s]);
                 }
                 if (abort_flag) break;
-                umma_commit(&tfull_bar[acc]);
+                if constexpr (kPair) umma_commit_pair_both(&tfull_bar[acc]);
+                else umma_commit(&tfull_bar[acc]);
             }
             if (issued) {
                 // All MMAs retire before TMEM is released.
-                umma_commit(&drain_bar);
+                if constexpr (kPair) umma_commit_pair(&drain_bar);
+                else umma_commit(&drain_bar);
                 mbar_wait(&drain_bar, 0, g.status);
             }
         }
@@ -368,16 +425,19 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         uint32_t tcount = 0;
         const bool vec_ok = (g.ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0);
-        for (int unit = blockIdx.x; unit < total_units; unit += gridDim.x, ++tcount) {
+        for (int unit = cta0; unit < total_units; unit += ncta, ++tcount) {
             const int tile = unit % total_tiles, split = unit / total_tiles;
             const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
             const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
-            if (abort_flag || !mbar_wait(&tfull_bar[acc], acc_ph, g.status)) { abort_flag = 1; break; }
+            if (abort_flag || !mbar_wait(&tfull_bar[acc], acc_ph, g.status)) {
+                abort_flag = 1;
+                break;
+            }
             tc_fence_after();
 #pragma unroll 1
             for (int cm = 0; cm < MT * (BN / 32); ++cm) {
             const int mt = cm / (BN / 32), cc = cm % (BN / 32);
-            const int row = m_blk * TBM + mt * BM + q * 32 + lane;
+            const int row = m_blk * TBM + ((int)rank * MT + mt) * BM + q * 32 + lane;
             {
                 float v[32];
                 tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * (MT * BN) + mt * BN + cc * 32, v);
@@ -430,7 +490,10 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+            if (lane == 0) {
+                if constexpr (kPair) mbar_arrive_cluster(tempty0_cl + 8u * acc);
+                else mbar_arrive(&tempty_bar[acc]);
+            }
             if (g.splits > 1) {
                 // The last of the tile's splits to arrive sums the partials in split order
                 // (deterministic) and writes C; it leaves the ticket at zero for the next call.
@@ -481,28 +544,34 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
     } else if constexpr (is_packed_tma(BMODE)) {
         // ---------------------------------------------------------------- dequantisers (TMA-staged)
         // Groups of 256 k (8 GGUF blocks per row) arrive by TMA in a two-slot ring; thread
-        // (row r, half h) decodes blocks 4h..4h+3 of its row, i.e. MMA k-stages 2h and 2h+1 of
-        // the group, straight from shared memory into the swizzled B tiles.
+        // (row r, part h) decodes SPT of the group's four MMA k-stages of its row (stages
+        // h * SPT ..; two blocks each), straight from shared memory into the swizzled B tiles.
+        // 128 B rows per CTA: two stages per thread; 64 rows: one.
+        static_assert(BNC == 128 || BNC == 64, "packed mode stages 64 or 128 B rows per CTA");
+        constexpr int SPT = BNC / 64;      // k-stages per thread per group
+        static_assert(SPT * (256 / BNC) == 4, "threads x stages cover the group's four k-stages");
+        static_assert((BNC / 32) * (256 / BNC) == kDqWarps, "each k-stage is decoded by BNC / 32 warps");
         constexpr int GB = group_bytes(BMODE);
-        constexpr int HB = GB / 2;         // bytes per half row
-        constexpr int HW = HB / 4;         // 32-bit words per half row (34 or 18)
+        constexpr int HB = GB * SPT / 4;   // bytes of the row this thread decodes
+        constexpr int HW = HB / 4;         // as 32-bit words (Q8_0: 34 / 17, Q4_0: 18 / 9)
         constexpr int BB = is_q4_mode(BMODE) ? 18 : 34;
         constexpr int NW = is_q4_mode(BMODE) ? 5 : 9;
-        static_assert(BN == 128, "packed mode uses 128-row B tiles");
         const int dt = tid - 192;
-        const int r = dt & (BN - 1), h = dt >> 7;
+        const int r = dt & (BNC - 1), h = dt / BNC;
         uint8_t* pk = smem + S * SB;
         const int groups = g.kb_per_split / 4;  // 256-k groups per unit
-        const int my_units = total_units > (int)blockIdx.x ? (total_units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const int my_units = total_units > cta0 ? (total_units - 1 - cta0) / ncta + 1 : 0;
         const uint32_t n_groups = (uint32_t)my_units * (uint32_t)groups;
         auto issue_group = [&](uint32_t gi) {
-            const int unit = (int)blockIdx.x + (int)(gi / groups) * (int)gridDim.x;
+            const int unit = cta0 + (int)(gi / groups) * ncta;
             const int tile = unit % total_tiles;
             const int grp = (unit / total_tiles) * groups + (int)(gi % groups);
             const uint32_t slot = gi & 1u;
             if (!mbar_wait(&pk_empty[slot], ((gi >> 1) & 1u) ^ 1u, g.status)) return false;
-            mbar_arrive_expect_tx(&pk_full[slot], (uint32_t)(BN * GB));
-            tma_load_2d(pk + slot * (BN * GB), &tmB, grp * (GB / 2), (tile / g.tiles_m) * BN, &pk_full[slot]);
+            mbar_arrive_expect_tx(&pk_full[slot], (uint32_t)(BNC * GB));
+            // this CTA's B rows of the tile (pair mode: rows BNC * rank ..), into its own ring
+            tma_load_2d(pk + slot * (BNC * GB), &tmB, grp * (GB / 2), (tile / g.tiles_m) * BN + (int)rank * BNC,
+                        &pk_full[slot]);
             return true;
         };
         if (dt == 0 && n_groups > 0 && !issue_group(0)) abort_flag = 1;
@@ -511,20 +580,28 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             const uint32_t slot = gi & 1u;
             if (!mbar_wait(&pk_full[slot], (gi >> 1) & 1u, g.status)) { abort_flag = 1; break; }
             uint32_t w[HW];
-            const uint2* src = reinterpret_cast<const uint2*>(pk + slot * (BN * GB) + r * GB + h * HB);
+            const uint8_t* src = pk + slot * (BNC * GB) + r * GB + h * HB;
+            if constexpr (HB % 8 == 0) {
 #pragma unroll
-            for (int i = 0; i < HW / 2; ++i) {
-                const uint2 v = src[i];
-                w[2 * i] = v.x;
-                w[2 * i + 1] = v.y;
+                for (int i = 0; i < HW / 2; ++i) {
+                    const uint2 v = reinterpret_cast<const uint2*>(src)[i];
+                    w[2 * i] = v.x;
+                    w[2 * i + 1] = v.y;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < HW; ++i) w[i] = reinterpret_cast<const uint32_t*>(src)[i];
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&pk_empty[slot]);
 #pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {
-                const uint32_t it = gi * 4 + 2 * h + jj;
+            for (int jj = 0; jj < SPT; ++jj) {
+                const uint32_t it = gi * 4 + SPT * h + jj;
                 const uint32_t s = it % S, ph = (it / S) & 1u;
-                if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) { abort_flag = 1; break; }
+                if (!mbar_wait(&empty_bar[s], ph ^ 1u, g.status)) {
+                    abort_flag = 1;
+                    break;
+                }
                 uint8_t* row_base = smem + s * SB + AB + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
@@ -544,7 +621,10 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full_bar[s]);
+                if (lane == 0) {
+                    if constexpr (kPair) mbar_arrive_cluster(full0_cl + 8u * s);
+                    else mbar_arrive(&full_bar[s]);
+                }
             }
         }
     } else if constexpr (kQuant) {
@@ -614,9 +694,13 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
 
     tc_fence_before();
     __syncthreads();
+    // pair mode: neither CTA releases its TMEM or shared memory (which the pair's MMAs read)
+    // before both are done
+    if constexpr (kPair) cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
+        if constexpr (kPair) tmem_dealloc_pair(tmem_base, kTmemCols);
+        else tmem_dealloc(tmem_base, kTmemCols);
     }
 }
 
@@ -668,10 +752,10 @@ bool make_map_plain(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int BMODE, typename T, int MT = 1>
+template <int BN, int BMODE, typename T, int MT = 1, int CG = 1>
 cudaError_t launch_gemm(const mgpu_k::LaunchCtx& c, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g) {
-    auto kern = gemm_tc_kernel<BN, BMODE, T, MT>;
-    const int smem = smem_bytes(BN, BMODE, MT);
+    auto kern = gemm_tc_kernel<BN, BMODE, T, MT, CG>;
+    const int smem = smem_bytes(BN, BMODE, MT, CG);
     // The shared-memory opt-in is a per-device function attribute: set it once per device.
     static std::atomic<uint64_t> configured{0};
     int ordinal = 0;
@@ -684,33 +768,56 @@ cudaError_t launch_gemm(const mgpu_k::LaunchCtx& c, const CUtensorMap& ma, const
         configured.fetch_or(bit, std::memory_order_acq_rel);
     }
     const int units = g.tiles_m * g.tiles_n * g.splits;
-    const int grid = units < c.sm_count ? units : c.sm_count;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(gemm_threads(BMODE));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = c.stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    int grid = units < c.sm_count ? units : c.sm_count;
+    if constexpr (CG == 2) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
+        cfg.gridDim = dim3(2);
+        // clusters that fit on the device at once (per device, for this instantiation)
+        static std::atomic<int> cached[64];
+        int clusters = ordinal < 64 ? cached[ordinal].load(std::memory_order_acquire) : 0;
+        if (clusters <= 0) {
+            if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+                (void)cudaGetLastError();
+                clusters = c.sm_count / 2;
+            }
+            if (ordinal < 64) cached[ordinal].store(clusters, std::memory_order_release);
+        }
+        grid = 2 * (units < clusters ? units : clusters);
+    }
+    cfg.gridDim = dim3(grid);
     return cudaLaunchKernelEx(&cfg, kern, ma, mb, g);
 }
 
 template <int BN, typename T>
-cudaError_t launch_mode(const mgpu_k::LaunchCtx& c, int bmode, int mt, const CUtensorMap& ma, const CUtensorMap& mb,
+cudaError_t launch_mode(const mgpu_k::LaunchCtx& c, int bmode, int mt, int cg, const CUtensorMap& ma, const CUtensorMap& mb,
                         const GemmArgs& g) {
     switch (bmode) {
-        case B_TMA_K: return launch_gemm<BN, B_TMA_K, T>(c, ma, mb, g);
-        case B_TMA_MN: return launch_gemm<BN, B_TMA_MN, T>(c, ma, mb, g);
+        case B_TMA_K:
+            return cg == 2 ? launch_gemm<BN, B_TMA_K, T, 1, 2>(c, ma, mb, g) : launch_gemm<BN, B_TMA_K, T>(c, ma, mb, g);
+        case B_TMA_MN:
+            return cg == 2 ? launch_gemm<BN, B_TMA_MN, T, 1, 2>(c, ma, mb, g) : launch_gemm<BN, B_TMA_MN, T>(c, ma, mb, g);
         case B_Q8: return launch_gemm<BN, B_Q8, T>(c, ma, mb, g);
         case B_Q4: return launch_gemm<BN, B_Q4, T>(c, ma, mb, g);
         case B_Q8_TMA:
+            if (cg == 2) return launch_gemm<BN, B_Q8_TMA, T, 1, 2>(c, ma, mb, g);
             if constexpr (BN == 128)
                 return mt == 2 ? launch_gemm<BN, B_Q8_TMA, T, 2>(c, ma, mb, g) : launch_gemm<BN, B_Q8_TMA, T, 1>(c, ma, mb, g);
             return cudaErrorInvalidValue;
         default:
+            if (cg == 2) return launch_gemm<BN, B_Q4_TMA, T, 1, 2>(c, ma, mb, g);
             if constexpr (BN == 128)
                 return mt == 2 ? launch_gemm<BN, B_Q4_TMA, T, 2>(c, ma, mb, g) : launch_gemm<BN, B_Q4_TMA, T, 1>(c, ma, mb, g);
             return cudaErrorInvalidValue;
@@ -756,19 +863,49 @@ GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& 
     else if (B.type == MGPU_Q4_0) p.bmode = packed_ok ? B_Q4_TMA : B_Q4;
     else p.bmode = (B.layout == MGPU_LAYOUT_NK) ? B_TMA_K : B_TMA_MN;
 
-    // Pick the tile by the estimated makespan over the SMs.  Dense: BN in {128, 256}, tile time
-    // ~ BN + a fixed overhead.  Packed quantised: BN = 128 and 128 or 256 rows; a 256-row tile
-    // decodes its B stages once for twice the MMAs and takes about 1.4x as long as a 128-row
-    // one (measured on M = 761 prefill shapes).
-    auto waves = [&](int bm, int bn) {
-        const long tiles = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
-        return (tiles + c.sm_count - 1) / c.sm_count;
+    // Pick the tiling by its estimated makespan in SM cycles: waves x 16-k steps x step cost +
+    // a fixed cost per CTA (pipeline fill, epilogue; the persistent CTAs overlap a tile's
+    // epilogue with the next tile).  A step's MMA cost on one SM is bounded by the tensor
+    // core's shared-memory operand reads, ~64 bytes per cycle (4 KB of A per 128 rows, 32
+    // bytes per B column this CTA holds), and by its rate (BN / 2 cycles per 128 rows of this
+    // CTA); a quantised B also costs ~1 cycle per B row this CTA decodes, overlapped with the
+    // MMAs.  Candidates: one CTA per 128 x BN tile; one CTA per 256 x 128 tile (two
+    // accumulators sharing each decoded B stage, packed quantised B only); a CTA pair per
+    // 256 x BN tile (cta_group::2, A and B staged by TMA).  Dense pairs start and finish more
+    // slowly (measured: SigLIP B = 1 shapes ~1 us slower as pairs, B = 8 shapes 10-50 % faster);
+    // packed pairs won on every M = 761 prefill shape.
+    struct Cand {
+        int bn, mt, cg;
     };
+    const bool packed = is_packed_tma(p.bmode);
+    const Cand dense_c[4] = {{128, 1, 1}, {256, 1, 1}, {128, 1, 2}, {256, 1, 2}};
+    const Cand packed_c[4] = {{128, 1, 1}, {128, 2, 1}, {128, 1, 2}, {256, 1, 2}};
+    const Cand* cands = packed ? packed_c : dense_c;
+    const int n_cands = quant && !packed ? 1 : 4;  // GGUF rows read with plain loads: 128 x 128
+    const double steps = (double)((K + 15) / 16);
+    double best = 0.0;
     p.BN = 128;
     p.mt = 1;
-    if (is_packed_tma(p.bmode)) p.mt = waves(2 * BM, 128) * 14 < waves(BM, 128) * 10 ? 2 : 1;
-    else p.BN = waves(BM, 128) * (128 + 32) < waves(BM, 256) * (256 + 32) ? 128 : 256;
-    p.tiles_m = (M + BM * p.mt - 1) / (BM * p.mt);
+    p.cg = 1;
+    for (int i = 0; i < n_cands; ++i) {
+        const Cand& cd = cands[i];
+        if (cd.cg == 2 && M <= BM) continue;  // a pair needs two 128-row blocks
+        const long rows = 128L * cd.mt * cd.cg;
+        const long tiles = ((M + rows - 1) / rows) * (long)((N + cd.bn - 1) / cd.bn);
+        const long slots = cd.cg == 2 ? c.sm_count / 2 : c.sm_count;
+        const double bytes = 4096.0 * cd.mt + 32.0 * (cd.bn / cd.cg);
+        const double rate = cd.mt * cd.bn / 2.0;
+        double step = bytes / 64.0 > rate ? bytes / 64.0 : rate;
+        if (quant && (double)(cd.bn / cd.cg) > step) step = (double)(cd.bn / cd.cg);
+        const double cost = (double)((tiles + slots - 1) / slots) * steps * step + (cd.cg == 2 && !quant ? 14000.0 : 4000.0);
+        if (i == 0 || cost < best) {
+            best = cost;
+            p.BN = cd.bn;
+            p.mt = cd.mt;
+            p.cg = cd.cg;
+        }
+    }
+    p.tiles_m = (M + BM * p.mt * p.cg - 1) / (BM * p.mt * p.cg);
     p.tiles_n = (N + p.BN - 1) / p.BN;
     p.num_kb = (K + BK - 1) / BK;
     // Split K for skinny M (M <= 16, e.g. a decode batch of up to 16 sequences) when the tiles
@@ -778,7 +915,7 @@ GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& 
     // decode shapes.)
     p.splits = 1;
     const int tiles = p.tiles_m * p.tiles_n;
-    if (M <= 16 && K % 256 == 0 && tiles * 2 <= c.sm_count) {
+    if (p.cg == 1 && M <= 16 && K % 256 == 0 && tiles * 2 <= c.sm_count) {
         const int groups = p.num_kb / 4;
         for (int sp = min(groups, c.sm_count / tiles); sp >= 2; --sp)
             if (groups % sp == 0) {
@@ -813,7 +950,7 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
         p.splits = 1;
         p.kb_per_split = p.num_kb;
     }
-    const int bmode = p.bmode, BN = p.BN, mt = p.mt, tiles_m = p.tiles_m;
+    const int bmode = p.bmode, BN = p.BN, mt = p.mt, cg = p.cg, tiles_m = p.tiles_m;
 
     GemmArgs g;
     g.M = M;
@@ -840,7 +977,7 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
     memset(&mb, 0, sizeof(mb));
     if (!make_map(&ma, A.ptr, M, K, A.ld, BK, BM)) return cudaErrorInvalidValue;
     if (bmode == B_TMA_K) {
-        if (!make_map(&mb, B.ptr, N, K, B.ld, BK, BN)) return cudaErrorInvalidValue;
+        if (!make_map(&mb, B.ptr, N, K, B.ld, BK, BN / cg)) return cudaErrorInvalidValue;
     } else if (bmode == B_TMA_MN) {
         if (!make_map(&mb, B.ptr, K, N, B.ld, 64, BK)) return cudaErrorInvalidValue;
     } else {
@@ -848,15 +985,18 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
         g.bq_row_bytes = B.ld;
         g.bq_end = g.Bq + (size_t)N * B.ld;
         if (is_packed_tma(bmode)) {
-            // the packed rows as a 2-D array of 16-bit units: box = one 256-k group x BN rows
-            if (!make_map_plain(&mb, B.ptr, N, B.ld / 2, B.ld / 2, group_bytes(bmode) / 2, BN))
+            // the packed rows as a 2-D array of 16-bit units: box = one 256-k group x the B rows
+            // one CTA stages
+            if (!make_map_plain(&mb, B.ptr, N, B.ld / 2, B.ld / 2, group_bytes(bmode) / 2, BN / cg))
                 return cudaErrorInvalidValue;
         }
     }
     const bool bf16 = A.type == MGPU_BF16;
     if (BN == 256)
-        return bf16 ? launch_mode<256, __nv_bfloat16>(c, bmode, mt, ma, mb, g) : launch_mode<256, __half>(c, bmode, mt, ma, mb, g);
-    return bf16 ? launch_mode<128, __nv_bfloat16>(c, bmode, mt, ma, mb, g) : launch_mode<128, __half>(c, bmode, mt, ma, mb, g);
+        return bf16 ? launch_mode<256, __nv_bfloat16>(c, bmode, mt, cg, ma, mb, g)
+                    : launch_mode<256, __half>(c, bmode, mt, cg, ma, mb, g);
+    return bf16 ? launch_mode<128, __nv_bfloat16>(c, bmode, mt, cg, ma, mb, g)
+                : launch_mode<128, __half>(c, bmode, mt, cg, ma, mb, g);
 }
 
 }  // namespace mgpu_k
