@@ -183,13 +183,23 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
-// The same, arriving on `bar` at the same offset in both CTAs of the pair (CTA mask 0b11).
-__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
+// The same, arriving on `bar` at the same offset in both CTAs of the pair (`mask`: the pair's
+// two bits of the cluster's CTA ranks).
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar, uint16_t mask) {
     asm volatile(
         "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
             smem_u32(bar)),
-        "h"((uint16_t)3)
+        "h"(mask)
         : "memory");
+}
+// 16 bytes of another CTA's shared memory (an address from cluster_addr).
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t cl_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cl_addr)
+                 : "memory");
+    return v;
 }
 // 2-D tensor-map load into this CTA's own shared memory whose completion (bytes) is counted on
 // the barrier at cluster address `bar_cl` (the even CTA's barrier of the pair).

@@ -93,6 +93,11 @@ struct GemmArgs {
     int splits, kb_per_split;
     unsigned int* tickets;
     float* partials;
+    // cluster split-K: csplit > 1 runs each tile as one cluster of csplit CTAs (CTA pairs in
+    // pair mode), the i-th over k-blocks [i * kb_per_split, ..) (the last may be shorter); the
+    // fp32 partials stay in shared memory and the cluster sums them over DSMEM (splits ==
+    // csplit, tickets and partials unused).
+    int csplit;
 };
 
 template <typename T>
@@ -152,7 +157,11 @@ __device__ __forceinline__ void load_block(RawBlock<NW>& rb, const uint8_t* p, c
     }
 }
 
-#define MAGIC_F(v, byte_sel) __uint_as_float(prmt((v), 0x4B000000u, 0x7540u | (byte_sel)))
+// Byte `byte_sel` of v placed at bits 8-15 of the float 2^23: the value 2^23 + 256 * byte.
+// Then fma(that, d / 256, -(2^15 + z) * d) = (byte - z) * d exactly: d / 256 and (2^15 + z) * d
+// (z = 128 or 8: 9 or 13 significant bits times d's 11) are exact in fp32, the fma rounds once,
+// and (byte - z) * d needs at most 19 bits.
+#define MAGIC_F(v, byte_sel) __uint_as_float(prmt((v), 0x4B000000u, 0x7504u | ((byte_sel) << 4)))
 
 // Decode one block into 32 values of T (4 x 16 bytes) and store them to the four swizzled
 // 16-byte chunks `dst[0..3]`.
@@ -166,9 +175,9 @@ __device__ __forceinline__ void decode_store(const RawBlock<NW>& rb, uint4* cons
     const uint32_t sel = rb.par ? 0x7654u : 0x5432u;
     const uint32_t dsel = rb.par ? 0x4432u : 0x4410u;
     const float d = __half2float(__ushort_as_half((unsigned short)prmt(rb.w[0], 0u, dsel)));
-    const float2 dd = make_float2(d, d);
+    const float2 d8 = make_float2(d * 0.00390625f, d * 0.00390625f);
     if constexpr (is_q4_mode(BMODE)) {
-        const float2 off = make_float2(-8388616.0f, -8388616.0f);
+        const float2 off = make_float2(-32776.0f * d, -32776.0f * d);
         uint32_t lo[4], hi[4];
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
@@ -185,15 +194,15 @@ __device__ __forceinline__ void decode_store(const RawBlock<NW>& rb, uint4* cons
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const uint32_t v = src[w0 + h];
-                const float2 a = __fmul2_rn(__fadd2_rn(make_float2(MAGIC_F(v, 0), MAGIC_F(v, 1)), off), dd);
-                const float2 b = __fmul2_rn(__fadd2_rn(make_float2(MAGIC_F(v, 2), MAGIC_F(v, 3)), off), dd);
+                const float2 a = __ffma2_rn(make_float2(MAGIC_F(v, 0), MAGIC_F(v, 1)), d8, off);
+                const float2 b = __ffma2_rn(make_float2(MAGIC_F(v, 2), MAGIC_F(v, 3)), d8, off);
                 o[2 * h] = pack2<T>(a.x, a.y);
                 o[2 * h + 1] = pack2<T>(b.x, b.y);
             }
             *dst[j] = make_uint4(o[0], o[1], o[2], o[3]);
         }
     } else {
-        const float2 off = make_float2(-8388736.0f, -8388736.0f);
+        const float2 off = make_float2(-32896.0f * d, -32896.0f * d);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             uint32_t o[4];
@@ -201,8 +210,8 @@ __device__ __forceinline__ void decode_store(const RawBlock<NW>& rb, uint4* cons
             for (int h = 0; h < 2; ++h) {
                 const int m = 2 * j + h;
                 const uint32_t v = prmt(rb.w[m], rb.w[m + 1], sel) ^ 0x80808080u;
-                const float2 a = __fmul2_rn(__fadd2_rn(make_float2(MAGIC_F(v, 0), MAGIC_F(v, 1)), off), dd);
-                const float2 b = __fmul2_rn(__fadd2_rn(make_float2(MAGIC_F(v, 2), MAGIC_F(v, 3)), off), dd);
+                const float2 a = __ffma2_rn(make_float2(MAGIC_F(v, 0), MAGIC_F(v, 1)), d8, off);
+                const float2 b = __ffma2_rn(make_float2(MAGIC_F(v, 2), MAGIC_F(v, 3)), d8, off);
                 o[2 * h] = pack2<T>(a.x, a.y);
                 o[2 * h + 1] = pack2<T>(b.x, b.y);
             }
@@ -245,9 +254,16 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
     const int total_tiles = g.tiles_m * g.tiles_n;
     const int total_units = total_tiles * g.splits;  // unit = (split, tile): split-major
     // CTA pairs walk the units together: cluster index and count stand in for the block's.
-    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
-    const int cta0 = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
-    const int ncta = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    // With cluster split-K each cluster owns one unit: (K slice, tile).
+    const int csplit = g.csplit;
+    const uint32_t crank = (kPair || csplit > 1) ? cluster_ctarank() : 0u;
+    const uint32_t rank = kPair ? (crank & 1u) : 0u;         // CTA within its pair
+    const uint32_t ksplit = kPair ? (crank >> 1) : crank;    // K slice (cluster split-K)
+    const uint32_t lead = crank - rank;                      // the pair's even CTA
+    const int ufirst = csplit > 1 ? (int)ksplit * total_tiles + (int)blockIdx.x / (CG * csplit)
+                                  : (kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x);
+    const int ustep = csplit > 1 ? total_units : (kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x);
+    auto kb_end = [&](int kb0) { return min(kb0 + g.kb_per_split, g.num_kb); };
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -291,9 +307,10 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
     if constexpr (kPair) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = tmem_base_slot;
-    // the even CTA's barriers, in the cluster window (pair mode)
-    const uint32_t full0_cl = kPair ? cluster_addr(&full_bar[0], 0) : 0u;
-    const uint32_t tempty0_cl = kPair ? cluster_addr(&tempty_bar[0], 0) : 0u;
+    // the pair's even CTA's barriers, in the cluster window (pair mode)
+    const uint32_t full0_cl = kPair ? cluster_addr(&full_bar[0], lead) : 0u;
+    const uint32_t tempty0_cl = kPair ? cluster_addr(&tempty_bar[0], lead) : 0u;
+    const uint16_t pair_mask = (uint16_t)(3u << lead);
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
@@ -331,10 +348,10 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             uint32_t it = 0;
             int pre = 0;
             if constexpr (!kQuant) {
-                if (cta0 < total_units) {
-                    const int tile = cta0 % total_tiles, kb0 = (cta0 / total_tiles) * g.kb_per_split;
+                if (ufirst < total_units) {
+                    const int tile = ufirst % total_tiles, kb0 = (ufirst / total_tiles) * g.kb_per_split;
                     const int n_blk = tile / g.tiles_m;
-                    pre = min(S, g.kb_per_split);
+                    pre = min(S, kb_end(kb0) - kb0);
                     for (int p = 0; p < pre; ++p) {
                         // fresh ring: every slot is free
                         expect((uint32_t)p);
@@ -343,10 +360,10 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                 }
             }
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            for (int unit = cta0; unit < total_units && !abort_flag; unit += ncta) {
+            for (int unit = ufirst; unit < total_units && !abort_flag; unit += ustep) {
                 const int tile = unit % total_tiles, kb0 = (unit / total_tiles) * g.kb_per_split;
                 const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
-                for (int kb = kb0; kb < kb0 + g.kb_per_split; ++kb, ++it) {
+                for (int kb = kb0; kb < kb_end(kb0); ++kb, ++it) {
                     const uint32_t s = it % S, ph = (it / S) & 1u;
                     uint8_t* a_dst = smem + s * SB;
                     uint8_t* b_dst = a_dst + AB;
@@ -371,7 +388,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         if (lane == 0 && rank == 0) {
             uint32_t it = 0, tcount = 0;
             bool issued = false;
-            for (int unit = cta0; unit < total_units && !abort_flag; unit += ncta, ++tcount) {
+            for (int unit = ufirst; unit < total_units && !abort_flag; unit += ustep, ++tcount) {
                 const int kb0 = (unit / total_tiles) * g.kb_per_split;
                 const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
                 if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, g.status)) {
@@ -380,7 +397,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * (MT * BN);
-                for (int kb = kb0; kb < kb0 + g.kb_per_split; ++kb, ++it) {
+                for (int kb = kb0; kb < kb_end(kb0); ++kb, ++it) {
                     const uint32_t s = it % S, ph = (it / S) & 1u;
                     if (!mbar_wait(&full_bar[s], ph, g.status)) {
                         abort_flag = 1;
@@ -406,11 +423,11 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                         }
                     }
                     issued = true;
-                    if constexpr (kPair) umma_commit_pair_both(&empty_bar[s]);
+                    if constexpr (kPair) umma_commit_pair_both(&empty_bar[s], pair_mask);
                     else umma_commit(&empty_bar[s]);
                 }
                 if (abort_flag) break;
-                if constexpr (kPair) umma_commit_pair_both(&tfull_bar[acc]);
+                if constexpr (kPair) umma_commit_pair_both(&tfull_bar[acc], pair_mask);
                 else umma_commit(&tfull_bar[acc]);
             }
             if (issued) {
@@ -425,7 +442,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         uint32_t tcount = 0;
         const bool vec_ok = (g.ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0);
-        for (int unit = cta0; unit < total_units; unit += ncta, ++tcount) {
+        for (int unit = ufirst; unit < total_units; unit += ustep, ++tcount) {
             const int tile = unit % total_tiles, split = unit / total_tiles;
             const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
             const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
@@ -442,6 +459,15 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                 float v[32];
                 tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * (MT * BN) + mt * BN + cc * 32, v);
                 const int n0 = n_blk * BN + cc * 32;
+                if (csplit > 1) {
+                    // cluster split-K: this CTA's fp32 partial into its shared memory (the ring
+                    // is idle: the tile's MMAs have all completed), summed after the cluster sync
+                    float* red = reinterpret_cast<float*>(smem) + (q * 32 + lane) * (BN + 4) + cc * 32;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        reinterpret_cast<float4*>(red)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    continue;
+                }
                 if (g.splits > 1) {
                     // split-K: this CTA's fp32 partial of the tile
                     if (row < g.M && n0 < g.N) {
@@ -494,7 +520,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                 if constexpr (kPair) mbar_arrive_cluster(tempty0_cl + 8u * acc);
                 else mbar_arrive(&tempty_bar[acc]);
             }
-            if (g.splits > 1) {
+            if (g.splits > 1 && csplit == 1) {
                 // The last of the tile's splits to arrive sums the partials in split order
                 // (deterministic) and writes C; it leaves the ticket at zero for the next call.
                 __threadfence();
@@ -560,10 +586,13 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         const int r = dt & (BNC - 1), h = dt / BNC;
         uint8_t* pk = smem + S * SB;
         const int groups = g.kb_per_split / 4;  // 256-k groups per unit
-        const int my_units = total_units > cta0 ? (total_units - 1 - cta0) / ncta + 1 : 0;
-        const uint32_t n_groups = (uint32_t)my_units * (uint32_t)groups;
+        const int my_units = total_units > ufirst ? (total_units - 1 - ufirst) / ustep + 1 : 0;
+        // cluster split-K: one unit, whose K slice may be the shorter last one
+        const int kb_first = (ufirst / total_tiles) * g.kb_per_split;
+        const uint32_t n_groups = csplit > 1 ? (uint32_t)(my_units ? (kb_end(kb_first) - kb_first) / 4 : 0)
+                                             : (uint32_t)my_units * (uint32_t)groups;
         auto issue_group = [&](uint32_t gi) {
-            const int unit = cta0 + (int)(gi / groups) * ncta;
+            const int unit = ufirst + (int)(gi / groups) * ustep;
             const int tile = unit % total_tiles;
             const int grp = (unit / total_tiles) * groups + (int)(gi % groups);
             const uint32_t slot = gi & 1u;
@@ -694,9 +723,63 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
 
     tc_fence_before();
     __syncthreads();
-    // pair mode: neither CTA releases its TMEM or shared memory (which the pair's MMAs read)
-    // before both are done
-    if constexpr (kPair) cluster_sync_all();
+    if (csplit > 1) {
+        // Cluster split-K: every CTA's partial (its 128 rows x BN) is in its shared memory.
+        // The csplit CTAs holding the same rows (same place in their pairs) sum them, each a
+        // share of the rows, reading the others' over DSMEM in K-slice order (deterministic),
+        // then add the bias, convert and store.
+        cluster_sync_all();
+        constexpr int RP = BN + 4;  // partial row pitch in floats
+        constexpr int C4 = BN / 4;
+        const int tile = ufirst % total_tiles;
+        const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
+        const int rows_per = (BM + csplit - 1) / csplit;
+        const int r0 = (int)ksplit * rows_per, r1 = min(BM, r0 + rows_per);
+        uint32_t src[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) src[i] = i < csplit ? cluster_addr(smem, (uint32_t)i * CG + rank) : 0u;
+        const bool vec = (g.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0);
+        for (int idx = tid; idx < (r1 - r0) * C4; idx += (int)blockDim.x) {
+            const int lr = r0 + idx / C4, c = (idx % C4) * 4;
+            const int row = m_blk * TBM + (int)rank * BM + lr, n = n_blk * BN + c;
+            if (row >= g.M || n >= g.N) continue;
+            const uint32_t off = (uint32_t)((lr * RP + c) * 4);
+            float4 part[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (i < csplit) part[i] = ld_cluster_f4(src[i] + off);
+            float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (i < csplit) {
+                    o[0] += part[i].x;
+                    o[1] += part[i].y;
+                    o[2] += part[i].z;
+                    o[3] += part[i].w;
+                }
+            if (g.bias) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (n + j < g.N) o[j] += bias_at(g.bias, g.bias_type, n + j);
+            }
+            const size_t base = (size_t)row * g.ldc + n;
+            if (vec && n + 4 <= g.N) {
+                if (g.c_type == MGPU_F32) {
+                    *reinterpret_cast<float4*>(reinterpret_cast<float*>(g.C) + base) = make_float4(o[0], o[1], o[2], o[3]);
+                } else {
+                    const uint2 w = g.c_type == MGPU_BF16
+                                        ? make_uint2(pack2<__nv_bfloat16>(o[0], o[1]), pack2<__nv_bfloat16>(o[2], o[3]))
+                                        : make_uint2(pack2<__half>(o[0], o[1]), pack2<__half>(o[2], o[3]));
+                    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(g.C) + base) = w;
+                }
+            } else {
+                for (int j = 0; j < 4 && n + j < g.N; ++j) store_out(g.C, g.c_type, base + j, o[j]);
+            }
+        }
+    }
+    // pair mode / cluster split-K: no CTA releases its TMEM or shared memory (which the pair's
+    // MMAs or the cluster's sums read) before all are done
+    if (kPair || csplit > 1) cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
         if constexpr (kPair) tmem_dealloc_pair(tmem_base, kTmemCols);
@@ -778,6 +861,17 @@ cudaError_t launch_gemm(const mgpu_k::LaunchCtx& c, const CUtensorMap& ma, const
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int grid = units < c.sm_count ? units : c.sm_count;
+    if (g.csplit > 1) {
+        // cluster split-K: one cluster of CG x csplit CTAs per tile, all tiles launched at once
+        if (MT != 1 || g.csplit * CG > 8 || BM * (BN + 4) * 4 > smem - 1024) return cudaErrorInvalidValue;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = CG * g.csplit;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
+        cfg.gridDim = dim3(g.tiles_m * g.tiles_n * CG * g.csplit);
+        return cudaLaunchKernelEx(&cfg, kern, ma, mb, g);
+    }
     if constexpr (CG == 2) {
         attr[1].id = cudaLaunchAttributeClusterDimension;
         attr[1].val.clusterDim.x = 2;
@@ -851,6 +945,46 @@ const char* gemm_check(const GemmOperand& A, const GemmOperand& B, const GemmOpe
     return nullptr;
 }
 
+}  // namespace
+
+namespace {
+// Clusters of `csize` CTAs (one CTA per SM: every instantiation takes ~200 KB of shared
+// memory) that the current device holds at once.  Clusters are placed within a GPC, so this
+// is below sm_count / csize for csize > 2 (measured on B200: 74, 45, 33, 22, 15 for 2, 3, 4,
+// 6, 8).  Queried once per device and size.
+int cluster_capacity(int sm_count, int csize) {
+    if (csize <= 1) return sm_count;
+    static std::atomic<int> cache[64][9];
+    int ordinal = 0;
+    if (csize > 8 || cudaGetDevice(&ordinal) != cudaSuccess || ordinal >= 64) return sm_count / csize;
+    int n = cache[ordinal][csize].load(std::memory_order_acquire);
+    if (n > 0) return n;
+    auto kern = gemm_tc_kernel<128, B_TMA_K, __nv_bfloat16, 1, 1>;
+    const int smem = smem_bytes(128, B_TMA_K);
+    n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(csize);
+        cfg.blockDim = dim3(gemm_threads(B_Q8_TMA));
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = csize;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    (void)cudaGetLastError();
+    if (n <= 0) n = sm_count / csize / 2;  // conservative when the query fails
+    cache[ordinal][csize].store(n, std::memory_order_release);
+    return n;
+}
+}  // namespace
+
+namespace mgpu_k {
+
 GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, int M, int N, int K) {
     (void)A;
     GemmPlan p;
@@ -869,7 +1003,8 @@ GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& 
     // core's shared-memory operand reads, ~64 bytes per cycle (4 KB of A per 128 rows, 32
     // bytes per B column this CTA holds), and by its rate (BN / 2 cycles per 128 rows of this
     // CTA); a quantised B also costs ~1 cycle per B row this CTA decodes, overlapped with the
-    // MMAs.  Candidates: one CTA per 128 x BN tile; one CTA per 256 x 128 tile (two
+    // MMAs.  Measured steps run ~1.7x that bound (pipeline latency) and the fixed cost is
+    // ~6000 cycles for one CTA per tile, ~11000 for packed and ~14000 for dense pairs.  Candidates: one CTA per 128 x BN tile; one CTA per 256 x 128 tile (two
     // accumulators sharing each decoded B stage, packed quantised B only); a CTA pair per
     // 256 x BN tile (cta_group::2, A and B staged by TMA).  Dense pairs start and finish more
     // slowly (measured: SigLIP B = 1 shapes ~1 us slower as pairs, B = 8 shapes 10-50 % faster);
@@ -887,6 +1022,13 @@ GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& 
     p.BN = 128;
     p.mt = 1;
     p.cg = 1;
+    // Cluster split-K (one CTA or pair per K slice, csplit of them per cluster, one tile per
+    // cluster, partials summed over DSMEM) when the tiles leave SMs idle.  Clusters are not
+    // persistent, so every wave of them pays the fill, drain and sums (~12000 cycles
+    // measured); how many clusters fit at once is queried from the device.
+    const int num_kb = (K + BK - 1) / BK;
+    const int gran = packed ? 4 : 1;  // k-blocks per slice unit (packed B: whole 256-k groups)
+    p.csplit = 1;
     for (int i = 0; i < n_cands; ++i) {
         const Cand& cd = cands[i];
         if (cd.cg == 2 && M <= BM) continue;  // a pair needs two 128-row blocks
@@ -897,17 +1039,39 @@ GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& 
         const double rate = cd.mt * cd.bn / 2.0;
         double step = bytes / 64.0 > rate ? bytes / 64.0 : rate;
         if (quant && (double)(cd.bn / cd.cg) > step) step = (double)(cd.bn / cd.cg);
-        const double cost = (double)((tiles + slots - 1) / slots) * steps * step + (cd.cg == 2 && !quant ? 14000.0 : 4000.0);
-        if (i == 0 || cost < best) {
-            best = cost;
-            p.BN = cd.bn;
-            p.mt = cd.mt;
-            p.cg = cd.cg;
+        step *= 1.7;
+        const double fixed = cd.cg == 1 ? 6000.0 : quant ? 11000.0 : 14000.0;
+        const bool split_ok = cd.mt == 1 && M > 16 && (packed || !quant) &&
+                              BM * (cd.bn + 4) * 4 <= smem_bytes(cd.bn, p.bmode, 1, cd.cg) - 1024;
+        for (int cs = 1; cs <= 8 / cd.cg; ++cs) {
+            double cost;
+            if (cs == 1) {
+                cost = (double)((tiles + slots - 1) / slots) * steps * step + fixed;
+            } else {
+                if (!split_ok) break;
+                const int kbps = (num_kb / gran + cs - 1) / cs * gran;
+                if ((cs - 1) * kbps >= num_kb) break;  // every slice gets some K
+                const long cap = cluster_capacity(c.sm_count, cd.cg * cs);
+                if (cap <= 0) break;
+                cost = (double)((tiles + cap - 1) / cap) * (kbps * 4.0 * step + 12000.0);
+            }
+            if ((i == 0 && cs == 1) || cost < best) {
+                best = cost;
+                p.BN = cd.bn;
+                p.mt = cd.mt;
+                p.cg = cd.cg;
+                p.csplit = cs;
+            }
         }
     }
     p.tiles_m = (M + BM * p.mt * p.cg - 1) / (BM * p.mt * p.cg);
     p.tiles_n = (N + p.BN - 1) / p.BN;
-    p.num_kb = (K + BK - 1) / BK;
+    p.num_kb = num_kb;
+    if (p.csplit > 1) {
+        p.splits = p.csplit;
+        p.kb_per_split = (num_kb / gran + p.csplit - 1) / p.csplit * gran;
+        return p;
+    }
     // Split K for skinny M (M <= 16, e.g. a decode batch of up to 16 sequences) when the tiles
     // fill at most half of the SMs: the largest split count that divides the 256-k groups
     // and keeps splits x tiles within the SMs; each split is at least one group.  (At
@@ -915,7 +1079,7 @@ GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& 
     // decode shapes.)
     p.splits = 1;
     const int tiles = p.tiles_m * p.tiles_n;
-    if (p.cg == 1 && M <= 16 && K % 256 == 0 && tiles * 2 <= c.sm_count) {
+    if (p.cg == 1 && M <= 16 && K % 256 == 0 && tiles * 2 <= c.sm_count) {  // fp32 partials in global memory
         const int groups = p.num_kb / 4;
         for (int sp = min(groups, c.sm_count / tiles); sp >= 2; --sp)
             if (groups % sp == 0) {
@@ -930,7 +1094,7 @@ GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& 
 size_t gemm_split_bytes(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, int M, int N, int K) {
     if (skinny_ok(A, B, M, N, K)) return 0;
     const GemmPlan p = plan_gemm(c, A, B, M, N, K);
-    return p.splits > 1 ? (size_t)p.splits * M * N * sizeof(float) : 0;
+    return p.splits > 1 && p.csplit == 1 ? (size_t)p.splits * M * N * sizeof(float) : 0;
 }
 
 bool make_tensor_map_u16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,
@@ -944,7 +1108,7 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
     // A few sequences against Q4_0 weights (batched decode): the streaming skinny kernel.
     if (skinny_ok(A, B, M, N, K)) return gemm_q4_skinny(c, A, B, C, bias, bias_type, M, N, K);
     GemmPlan p = plan_gemm(c, A, B, M, N, K);
-    if (p.splits > 1 && (!split || !split->tickets || !split->partials ||
+    if (p.splits > 1 && p.csplit == 1 && (!split || !split->tickets || !split->partials ||
                          (size_t)p.splits * M * N > split->max_partials ||
                          (size_t)p.tiles_m * p.tiles_n > split->max_tickets)) {
         p.splits = 1;
@@ -970,8 +1134,9 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
     g.status = c.status;
     g.splits = p.splits;
     g.kb_per_split = p.kb_per_split;
-    g.tickets = p.splits > 1 ? split->tickets : nullptr;
-    g.partials = p.splits > 1 ? split->partials : nullptr;
+    g.tickets = p.splits > 1 && p.csplit == 1 ? split->tickets : nullptr;
+    g.partials = p.splits > 1 && p.csplit == 1 ? split->partials : nullptr;
+    g.csplit = p.csplit;
 
     CUtensorMap ma, mb;
     memset(&mb, 0, sizeof(mb));

@@ -54,7 +54,7 @@ struct GemmOperand {
 };
 // How gemm() runs a shape: B mode, tile, and split-K.
 struct GemmPlan {
-    int bmode, BN, mt, cg, tiles_m, tiles_n, num_kb, splits, kb_per_split;
+    int bmode, BN, mt, cg, csplit, tiles_m, tiles_n, num_kb, splits, kb_per_split;
 };
 GemmPlan plan_gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, int M, int N, int K);
 // Split-K scratch: one ticket per output tile (zero between calls; the kernel leaves it so)

@@ -65,6 +65,28 @@ def test_quantised_ragged_and_batched(dev, qt, M, N, K):
         assert_close(C, ref, TOL_16, f"q{qt} {M}x{N}x{K} c{ct}")
 
 
+@pytest.mark.parametrize("qt,M,N,K", [(O.Q4_0, 128, 2040, 8192), (O.Q8_0, 128, 6144, 2048),
+                                      (O.Q8_0, 761, 2048, 2048), (O.Q4_0, 300, 1000, 8192)])
+def test_cluster_split_k(dev, qt, M, N, K):
+    # Shapes whose tiles leave SMs idle run as clusters that split K and sum the fp32 partials
+    # over distributed shared memory (one CTA or CTA pair per K slice).  Bias, ragged N and
+    # both output types; the sum is in slice order, so two calls give identical bits.
+    A = O.bf16(O.normal(M * K, 3 * M + N, 1.0))
+    W = O.quantize(O.normal(N * K, K + 1, 0.02), qt)
+    bias = O.normal(N, 99, 0.5)
+    ref = O.gemm_q(O.bf16_to_f32(A), W, M, N, K, qt, threads=True).reshape(M, N) + bias
+    dA, dW, dB = dev.array(A, mg.BF16), dev.array(W, qt, mg.LAYOUT_NK), dev.array(bias, mg.F32)
+    for ct in (mg.F32, mg.BF16):
+        outs = []
+        for _ in range(2):
+            dC = dev.empty(M * N, ct)
+            mg.gemm_q(dev, dA, dW, dC, M, N, K, qt, dB).wait()
+            outs.append(dC.read(mg.NP_DTYPE[ct]))
+        assert np.array_equal(outs[0], outs[1]), f"split-K sums not deterministic q{qt} {M}x{N}x{K}"
+        C = O.bf16_to_f32(outs[0]) if ct == mg.BF16 else outs[0]
+        assert_close(C, ref.reshape(-1), TOL_16, f"split-K q{qt} {M}x{N}x{K} c{ct}")
+
+
 @pytest.mark.parametrize("K,N", [(1152, 3456), (1152, 1152), (1152, 4304), (4304, 1152)])
 def test_siglip_layer_fp16(dev, K, N):
     # SigLIP per-layer GEMMs at B=1 (M=729): fp16 activations ~N(0,1), fp16 weights ~N(0,0.02)
