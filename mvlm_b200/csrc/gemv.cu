@@ -137,16 +137,19 @@ __device__ __forceinline__ void prepare_x_n(const XT* __restrict__ x, int K, uin
             int e = 0;
             frexpf(amax, &e);  // the block's |x| < 2^e
             const float up = __int_as_float((127 + 22 - e) << 23);  // 2^(22-e); |e| < 100 for finite x
-            uint32_t b0 = 0, b1 = 0, b2 = 0;
-            int sum = 0;
+            // X = round-to-nearest-even(v * 2^(22-e)), |X| <= 2^22: one fma against 1.5 * 2^23
+            // puts X + 2^23 + 2^22 in [2^23, 2^24] with a unit step, so its bits minus those of
+            // 1.5 * 2^23 are X (v * up is exact, so this equals __float2int_rn(v * up)).  The
+            // byte planes of the four elements are gathered with byte permutes.
+            uint32_t X[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int X = __float2int_rn(v[it][j] * up);  // |X| <= 2^22
-                sum += X;
-                b0 |= (uint32_t)(X & 0xFF) << (8 * j);
-                b1 |= (uint32_t)((X >> 8) & 0xFF) << (8 * j);
-                b2 |= (uint32_t)((X >> 16) & 0xFF) << (8 * j);
-            }
+            for (int j = 0; j < 4; ++j) X[j] = (uint32_t)(__float_as_int(fmaf(v[it][j], up, 12582912.0f)) - 0x4B400000);
+            int sum = (int)(X[0] + X[1] + X[2] + X[3]);
+            const uint32_t t01 = prmt(X[0], X[1], 0x5140u), t23 = prmt(X[2], X[3], 0x5140u);
+            const uint32_t u01 = prmt(X[0], X[1], 0x0062u), u23 = prmt(X[2], X[3], 0x0062u);
+            const uint32_t b0 = prmt(t01, t23, 0x5410u);  // byte 0 of X[0..3]
+            const uint32_t b1 = prmt(t01, t23, 0x7632u);  // byte 1
+            const uint32_t b2 = prmt(u01, u23, 0x5410u);  // byte 2
 #pragma unroll
             for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
             planes[w] = b0;
