@@ -76,6 +76,11 @@ inline cl_event dispatch_vision_proj(const DeviceInfo* dev, cl_program program, 
 // --- profiler.h:16 ---
 inline double profile_end(cl_event event) { return mgpu_profile_end(event); }
 
+// moondream2.cpp:551 argmax_logits(device, logits, vocab_size): on the device.
+inline int argmax_logits(const DeviceInfo* dev, cl_mem logits, int vocab_size) {
+    return mgpu_argmax_logits(dev, logits, vocab_size);
+}
+
 }  // namespace mgpu
 
 // OpenCL helpers used by the reference's call sites on these handles.

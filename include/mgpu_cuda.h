@@ -181,6 +181,16 @@ mgpu_event* mgpu_gemm(const mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf
 /* out[n] = dequant(W)[n] for n elements (out fp32, fp16 or bf16 per its tag). */
 mgpu_event* mgpu_dequant(const mgpu_device* dev, mgpu_buf* W, mgpu_buf* out, int64_t n, int type);
 
+/* Replaces argmax_logits (src/models/moondream2.cpp:551-591), which reads the fp16 logits back
+ * and scans them on the host.  Same result: the first index whose value is greater than every
+ * earlier one, starting from (-1e30, index 0), with values read as there (exponent field zero
+ * -> 0, all ones (Inf/NaN) -> +-1e30 by sign; bf16 / fp32 logits by the same rule on their own
+ * fields).  Computed on the device by one CTA; `out` (>= 8 bytes) receives the int32 index and
+ * the fp32 value, so shards of column-sharded logits combine by (larger value, smaller index). */
+mgpu_event* mgpu_argmax(const mgpu_device* dev, mgpu_buf* logits, int n, mgpu_buf* out);
+/* argmax_logits itself: waits for the stream and returns the index, or -1 on error. */
+int mgpu_argmax_logits(const mgpu_device* dev, mgpu_buf* logits, int vocab_size);
+
 /* ---------------------------------------------------------------- events ---------- */
 int mgpu_wait_event(mgpu_event* ev);                 /* clWaitForEvents(1, &ev) */
 void mgpu_release_event(mgpu_event* ev);             /* clReleaseEvent */

@@ -70,6 +70,8 @@ SIGNATURES = {
     "mgpu_gemm_q": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "mgpu_gemm": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "mgpu_dequant": (_vp, [_vp, _vp, _vp, _i64, _i]),
+    "mgpu_argmax": (_vp, [_vp, _vp, _i, _vp]),
+    "mgpu_argmax_logits": (_i, [_vp, _vp, _i]),
     "mgpu_wait_event": (_i, [_vp]),
     "mgpu_release_event": (None, [_vp]),
     "mgpu_profile_end": (_d, [_vp]),
@@ -396,6 +398,19 @@ def gemm(dev: Device, A: Buffer, B: Buffer, C: Buffer, M: int, N: int, K: int, b
 
 def dequant(dev: Device, W: Buffer, out: Buffer, n: int, qtype: int) -> Event:
     return _ev(lib().mgpu_dequant(dev.h, W.h, out.h, n, qtype), "dequant")
+
+
+def argmax(dev: Device, logits: Buffer, n: int, out: Buffer) -> Event:
+    """out (8 bytes) <- {int32 index, fp32 value}: the reference's argmax_logits on the device."""
+    return _ev(lib().mgpu_argmax(dev.h, logits.h, n, out.h), "argmax")
+
+
+def argmax_logits(dev: Device, logits: Buffer, vocab_size: int) -> int:
+    """argmax_logits(device, logits, vocab_size) (src/models/moondream2.cpp:551): the token id."""
+    idx = lib().mgpu_argmax_logits(dev.h, logits.h, vocab_size)
+    if idx < 0:
+        _raise_last("argmax_logits")
+    return idx
 
 
 def ggml_type_size(t: int) -> int:

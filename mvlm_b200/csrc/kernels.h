@@ -41,6 +41,8 @@ cudaError_t fill_normal(const LaunchCtx& c, int otype, void* out, int64_t n, uin
 cudaError_t convert(const LaunchCtx& c, int itype, const void* in, int otype, void* out, int64_t n);
 // One CTA waits on an mbarrier that never completes, bounded by limit_ns.
 cudaError_t selftest_bounded_wait(const LaunchCtx& c, uint64_t limit_ns);
+// out[0] = argmax index, out[1] = the value (fp32 bits), reference argmax semantics; n >= 1.
+cudaError_t argmax(const LaunchCtx& c, int type, const void* logits, int n, int* out);
 // patches[p][k] (k < kpad, zero for k >= C*ph*pw) from image [C][H][W]; same element type
 cudaError_t im2col(const LaunchCtx& c, int type, const void* img, void* patches, int C, int H, int W, int ph,
                    int pw, int kpad);

@@ -1,7 +1,8 @@
 // misc.cu - element-wise device kernels around the matmul path: GGUF block dequantisation
 // (standalone, for testing the in-kernel decoders), the ggml reference quantiser (to build
 // synthetic GGUF weights on the device for benchmarks), seeded generators, type
-// conversion and the patch_embed im2col gather (vision.cl:154-176 order).
+// conversion, the patch_embed im2col gather (vision.cl:154-176 order) and the greedy-decode
+// argmax over the lm_head's logits (src/models/moondream2.cpp:551-591, done there on the host).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -144,6 +145,78 @@ __global__ void selftest_wait_kernel(int* status, uint64_t limit_ns) {
     if (threadIdx.x == 0) mbar_wait(&bar, 0, status, limit_ns);
 }
 
+// A logit as the reference's argmax compares it (moondream2.cpp:567-582, written there for
+// fp16): exponent field zero (zero or subnormal) -> 0, all ones (Inf or NaN) -> +-1e30 by the
+// sign bit, else the value.  bf16 and fp32 logits follow the same rule on their own fields.
+__device__ __forceinline__ float argmax_value(int type, const void* x, int64_t i) {
+    if (type == MGPU_F16) {
+        const uint32_t h = reinterpret_cast<const uint16_t*>(x)[i];
+        const uint32_t e = (h >> 10) & 0x1Fu;
+        if (e == 0) return 0.0f;
+        if (e == 31) return (h & 0x8000u) ? -1e30f : 1e30f;
+        return __half2float(__ushort_as_half((unsigned short)h));
+    }
+    const uint32_t b = type == MGPU_F32 ? reinterpret_cast<const uint32_t*>(x)[i]
+                                        : (uint32_t)reinterpret_cast<const uint16_t*>(x)[i] << 16;
+    const uint32_t e = (b >> 23) & 0xFFu;
+    if (e == 0) return 0.0f;
+    if (e == 255) return (b & 0x80000000u) ? -1e30f : 1e30f;
+    return __uint_as_float(b);
+}
+
+// One CTA: the first index whose value is greater than every earlier one, starting from
+// (-1e30, index 0) as the reference does; out[0] = index, out[1] = its value (fp32 bits).
+// Each thread scans a strided subsequence in index order keeping its first maximum; the
+// pairs then combine by larger value, then smaller index, which gives the same index.
+__global__ void __launch_bounds__(1024) argmax_kernel(int type, const void* __restrict__ x, int n, int* out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float best = -1e30f;
+    int bi = 0x7FFFFFFF;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = argmax_value(type, x, i);
+        if (v > best) {
+            best = v;
+            bi = i;
+        }
+    }
+    auto better = [](float v, int i, float w, int j) { return w > v || (w == v && j < i); };
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float w = __shfl_xor_sync(0xffffffffu, best, off);
+        const int j = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (better(best, bi, w, j)) {
+            best = w;
+            bi = j;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = best;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = (blockDim.x + 31) >> 5;
+        best = lane < nw ? sv[lane] : -1e30f;
+        bi = lane < nw ? si[lane] : 0x7FFFFFFF;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float w = __shfl_xor_sync(0xffffffffu, best, off);
+            const int j = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (better(best, bi, w, j)) {
+                best = w;
+                bi = j;
+            }
+        }
+        if (lane == 0) {
+            // nothing above -1e30: the reference's initial index 0
+            out[0] = best > -1e30f ? bi : 0;
+            out[1] = __float_as_int(best);
+        }
+    }
+}
+
 int grid_for(int64_t n, int sm_count) {
     const int64_t want = (n + 255) / 256;
     const int64_t cap = (int64_t)sm_count * 16;
@@ -183,6 +256,11 @@ cudaError_t fill_normal(const LaunchCtx& c, int otype, void* out, int64_t n, uin
 cudaError_t convert(const LaunchCtx& c, int itype, const void* in, int otype, void* out, int64_t n) {
     if (n <= 0) return cudaSuccess;
     convert_kernel<<<grid_for(n, c.sm_count), 256, 0, c.stream>>>(itype, in, otype, out, n);
+    return cudaGetLastError();
+}
+
+cudaError_t argmax(const LaunchCtx& c, int type, const void* logits, int n, int* out) {
+    argmax_kernel<<<1, 1024, 0, c.stream>>>(type, logits, n, out);
     return cudaGetLastError();
 }
 

@@ -737,6 +737,45 @@ mgpu_event* mgpu_dequant(const mgpu_device* cd, mgpu_buf* W, mgpu_buf* out, int6
     return event_end(d, ev);
 }
 
+// ------------------------------------------------------------------ argmax -----------
+// Greedy decode over the lm_head's logits (moondream2.cpp:551-591 reads them back and scans on
+// the host): one CTA on the device; out receives {int32 index, fp32 value}.
+mgpu_event* mgpu_argmax(const mgpu_device* cd, mgpu_buf* logits, int n, mgpu_buf* out) {
+    API_ENTRY();
+    REQUIRE(cd && logits && out && n > 0, "mgpu_argmax: bad arguments");
+    REQUIRE(is_float_type(logits->type), "mgpu_argmax: logits must be f32/f16/bf16");
+    REQUIRE(logits->bytes >= (size_t)n * elem_size(logits->type), "mgpu_argmax: logits too small");
+    REQUIRE(out->bytes >= 8, "mgpu_argmax: out needs 8 bytes");
+    mgpu_device* d = const_cast<mgpu_device*>(cd);
+    DeviceGuard g(d->ordinal);
+    mgpu_event* ev = event_begin(d);
+    if (!cuda_ok(mgpu_k::argmax(ctx_of(d), logits->type, logits->ptr, n, (int*)out->ptr), "mgpu_argmax")) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(d, ev);
+}
+
+// The reference's argmax_logits(device, logits, vocab_size): the index, or -1 on error.  Waits
+// for the device stream; the result goes through bytes 64..71 of the device's status block.
+int mgpu_argmax_logits(const mgpu_device* cd, mgpu_buf* logits, int vocab_size) {
+    API_ENTRY();
+    if (!cd || !logits || vocab_size <= 0 || !is_float_type(logits->type) ||
+        logits->bytes < (size_t)vocab_size * elem_size(logits->type)) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_argmax_logits: bad arguments");
+        return -1;
+    }
+    mgpu_device* d = const_cast<mgpu_device*>(cd);
+    DeviceGuard g(d->ordinal);
+    int* slot = d->d_status + 16;
+    int host[2] = {-1, 0};
+    if (!cuda_ok(mgpu_k::argmax(ctx_of(d), logits->type, logits->ptr, vocab_size, slot), "mgpu_argmax_logits") ||
+        !cuda_ok(cudaMemcpyAsync(host, slot, sizeof(host), cudaMemcpyDeviceToHost, d->stream), "read argmax") ||
+        !cuda_ok(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize") || !check_status(d))
+        return -1;
+    return host[0];
+}
+
 // ------------------------------------------------------------------ events -----------
 int mgpu_wait_event(mgpu_event* ev) {
     if (!ev) return MGPU_OK;

@@ -59,3 +59,32 @@ def gather_columns(local, n: int, group=None):
     slots = torch.empty(world * width, dtype=local.dtype, device=local.device)
     dist.all_gather(list(slots.split(width)), padded, group=group)
     return torch.cat([slots[r * width: r * width + sizes[r]] for r in range(world)])
+
+
+def combine_argmax(pairs: list[tuple[int, float]], n: int, world: int) -> int:
+    """The global greedy token from the ranks' (local index, value) argmax results over their
+    column shards (in rank order): the larger value wins and, between equal values, the
+    smaller global index (the lower rank), which is the reference's first maximum.  If no
+    shard saw a value above -1e30 the answer is index 0, as in the reference's scan."""
+    best_i, best_v = 0, -1e30
+    for r, (i, v) in enumerate(pairs):
+        g = column_shard(n, world, r)[0] + i
+        if v > best_v:
+            best_i, best_v = g, v
+    return best_i
+
+
+def distributed_argmax(local_pair, n: int, group=None) -> int:
+    """All-gather each rank's 8-byte (index, value) argmax of its lm_head shard (instead of its
+    logits: 8 bytes per rank rather than 4 * n / world) and combine them.  `local_pair` is a
+    2-element int32 tensor as mgpu_argmax writes it (index, fp32 value bits)."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    slots = torch.empty(2 * world, dtype=torch.int32, device=local_pair.device)
+    dist.all_gather_into_tensor(slots, local_pair.to(torch.int32).contiguous(), group=group)
+    s = slots.cpu()
+    vals = s.view(torch.float32)
+    pairs = [(int(s[2 * r]), float(vals[2 * r + 1])) for r in range(world)]
+    return combine_argmax(pairs, n, world)

@@ -235,3 +235,34 @@ def max_threads() -> int:
 def set_threads(n: int) -> None:
     """Use n host threads in the multithreaded variants."""
     lib().ora_set_threads(int(n))
+
+
+def argmax_logits(raw: np.ndarray, t: int) -> tuple[int, float]:
+    """Greedy decode as src/models/moondream2.cpp:551-591 (argmax_logits) scans fp16 logits on
+    the host: each value decoded with exponent field 0 -> 0.0, exponent all ones (Inf/NaN) ->
+    +-1e30 by the sign bit, else the number; best = (-1e30, index 0) and an index replaces it
+    only when its value is strictly greater (so the first maximum wins).  `raw` holds the
+    logits' bits: uint16 for F16 / BF16, uint32 for F32 (bf16 / fp32 use the same rule on
+    their own exponent fields).  Returns (index, value)."""
+    best_id, best_val = 0, np.float32(-1e30)
+    for i, h in enumerate(raw.tolist()):
+        if t == F16:
+            e, sign = (h >> 10) & 0x1F, h & 0x8000
+            if e == 0:
+                val = np.float32(0.0)
+            elif e == 31:
+                val = np.float32(-1e30 if sign else 1e30)
+            else:
+                val = np.array([h], np.uint16).view(np.float16)[0].astype(np.float32)
+        else:
+            b = h if t == F32 else h << 16
+            e, sign = (b >> 23) & 0xFF, b & 0x80000000
+            if e == 0:
+                val = np.float32(0.0)
+            elif e == 255:
+                val = np.float32(-1e30 if sign else 1e30)
+            else:
+                val = np.array([b], np.uint32).view(np.float32)[0]
+        if val > best_val:
+            best_val, best_id = val, i
+    return best_id, float(best_val)

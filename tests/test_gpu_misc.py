@@ -78,3 +78,33 @@ def test_graph_capture_replays_gemv(dev):
     dev.finish()
     assert_close(dy.read(np.float32), O.gemm_q(x2, W, 1, N, K, O.Q4_0, threads=True), TOL_F32)
     assert not np.array_equal(first, dy.read(np.float32))
+
+
+@pytest.mark.parametrize("t", [mg.F16, mg.BF16, mg.F32])
+def test_argmax_logits_matches_reference_scan(dev, t):
+    # greedy decode over an lm_head's logits (vocab 51200): random values plus a repeated
+    # maximum, subnormals, infinities and NaN, against the oracle of the reference's host scan
+    n = 51200
+    x = O.normal(n, 77, 4.0)
+    x[[1000, 40000]] = 30.0  # the first of the tied maxima wins
+    if t == mg.F16:
+        raw = O.f16(x)
+        raw[[7, 50000]] = [0x0003, 0x8002]      # subnormals read as 0
+        raw[123] = 0xFC00                       # -Inf reads -1e30
+    elif t == mg.BF16:
+        raw = O.bf16(x)
+        raw[123] = 0xFF80
+    else:
+        raw = x.view(np.uint32).copy()
+        raw[123] = 0xFF800000
+    buf = dev.array(raw, t)
+    out = dev.empty(2, mg.F32)
+    for _ in range(2):
+        assert mg.argmax_logits(dev, buf, n) == O.argmax_logits(raw, t)[0] == 1000
+        mg.argmax(dev, buf, n, out).wait()
+        got = out.read(np.int32)
+        assert got[0] == 1000 and np.float32(got[1:2].view(np.float32)[0]) == np.float32(O.argmax_logits(raw, t)[1])
+    # a NaN with a clear sign bit reads +1e30 and wins
+    raw2 = raw.copy()
+    raw2[9] = {mg.F16: 0x7E00, mg.BF16: 0x7FC0, mg.F32: 0x7FC00000}[t]
+    assert mg.argmax_logits(dev, dev.array(raw2, t), n) == O.argmax_logits(raw2, t)[0] == 9

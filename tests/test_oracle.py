@@ -174,3 +174,16 @@ def test_im2col_order():
     for idx in range(p.shape[0]):
         r, c = divmod(idx, W // pw)
         np.testing.assert_array_equal(p[idx], im[:, r * ph:(r + 1) * ph, c * pw:(c + 1) * pw].reshape(-1))
+
+
+def test_argmax_logits_known_answers():
+    # the reference's host scan (moondream2.cpp:551-591) on fp16 logits: subnormal -> 0,
+    # Inf/NaN -> +-1e30 by sign, strictly greater replaces, so the first maximum wins
+    h = lambda *v: np.array(v, np.uint16)
+    assert O.argmax_logits(h(0xFC00, 0x3C00, 0x7E00, 0x4000), O.F16)[0] == 2      # NaN reads +1e30
+    assert O.argmax_logits(h(0xBC00, 0x0001, 0xB800), O.F16)[0] == 1              # subnormal reads 0
+    assert O.argmax_logits(h(0x3C00, 0x4000, 0x4000), O.F16)[0] == 1              # first of a tie
+    assert O.argmax_logits(h(0xFC00, 0xFC00), O.F16) == (0, float(np.float32(-1e30)))  # nothing above -1e30
+    assert O.argmax_logits(h(0xFBFF, 0x7C00, 0x7BFF), O.F16)[0] == 1              # +Inf reads 1e30
+    f = np.array([-2.0, np.float32(1e-40), -1.0, 3.0, 3.0], np.float32)
+    assert O.argmax_logits(f.view(np.uint32), O.F32)[0] == 3

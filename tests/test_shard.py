@@ -68,3 +68,46 @@ def test_lm_head_column_shard_allgather_gloo(world):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     results = dict(q.get(timeout=5) for _ in range(world))
     assert all(results.values()), results
+
+
+def _argmax_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        import oracle as O
+        from mvlm_b200.shard import distributed_argmax
+        N = 101
+        ok = True
+        for case in range(3):
+            logits = O.normal(N, 40 + case, 1.0)
+            if case == 1:
+                # the same maximum in the last shard and in the first: the smaller index wins
+                logits[N - 3] = logits[5] = 9.0
+            if case == 2:
+                logits[:] = -np.inf  # nothing above -1e30: index 0, as the reference's scan
+            a, b = column_shard(N, world, rank)
+            i, v = O.argmax_logits(logits[a:b].view(np.uint32), O.F32)
+            pair = torch.tensor([i, 0], dtype=torch.int32)
+            pair[1] = torch.tensor([v], dtype=torch.float32).view(torch.int32)[0]
+            got = distributed_argmax(pair, N)
+            ok &= got == O.argmax_logits(logits.view(np.uint32), O.F32)[0]
+        q.put((rank, bool(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_lm_head_distributed_argmax_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_argmax_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    results = dict(q.get(timeout=5) for _ in range(world))
+    assert all(results.values()), results
