@@ -178,6 +178,29 @@ mgpu_event* mgpu_gemm_q(const mgpu_device* dev, mgpu_buf* A, mgpu_buf* W, mgpu_b
 /* General entry: C = A * op(B) + bias, every operand's type/layout taken from its tag. */
 mgpu_event* mgpu_gemm(const mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N,
                       int K, mgpu_buf* bias);
+/* Activation applied by mgpu_gemm_fused after the bias.
+ * GELU: the tanh approximation 0.5x(1 + tanh(sqrt(2/pi)(x + 0.044715x^3))) that
+ *   dispatch_gelu's declaration states (src/engine/compute.h:48-50).
+ * SILU: x / (1 + exp(-x)), the reference's silu kernel (src/kernels/activations.cl:30-65).
+ * GELU_AS_SHIPPED: what the reference's gelu kernel computes (activations.cl:78-117):
+ *   0.5x(1 - tanh(...)), because its tanh identity has the sign reversed; use it only to
+ *   reproduce that kernel's output. */
+enum mgpu_act {
+    MGPU_ACT_NONE = 0,
+    MGPU_ACT_GELU = 1,
+    MGPU_ACT_SILU = 2,
+    MGPU_ACT_GELU_AS_SHIPPED = 3
+};
+/* C = act(A * op(B) + bias) + residual, in the GEMM's epilogue (one pass over C).  Replaces
+ * dispatch_gemm_image (src/engine/compute.h:27-29) followed by dispatch_gelu / dispatch_silu
+ * (compute.h:44-50) and the residual add (dispatch_residual_add, src/models/moondream2.cpp:297-300,
+ * over dispatch_vector_add, compute.h:134) on its output, as moondream2_forward chains them
+ * (moondream2.cpp:454, :497-512).  bias [N] and
+ * residual [M][N] (its own type and row pitch, default N) may be NULL; residual may be C
+ * itself (in-place `hidden += ...`).  The sum and the activation are computed in fp32 and C
+ * is rounded once, where the reference rounds to fp16 after each kernel. */
+mgpu_event* mgpu_gemm_fused(const mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N,
+                            int K, mgpu_buf* bias, int act, mgpu_buf* residual);
 /* out[n] = dequant(W)[n] for n elements (out fp32, fp16 or bf16 per its tag). */
 mgpu_event* mgpu_dequant(const mgpu_device* dev, mgpu_buf* W, mgpu_buf* out, int64_t n, int type);
 

@@ -22,6 +22,7 @@ LIB_PATH = os.path.join(HERE, "libmgpu.so")
 
 F32, F16, Q4_0, Q8_0, BF16 = 0, 1, 2, 8, 30
 LAYOUT_KN, LAYOUT_NK = 0, 1
+ACT_NONE, ACT_GELU, ACT_SILU, ACT_GELU_AS_SHIPPED = 0, 1, 2, 3
 OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_OUT_OF_MEMORY, ERR_DEVICE_TIMEOUT = range(6)
 
 TYPE_SIZE = {F32: 4, F16: 2, BF16: 2}
@@ -69,6 +70,7 @@ SIGNATURES = {
     "mgpu_gemv_q": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i]),
     "mgpu_gemm_q": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "mgpu_gemm": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "mgpu_gemm_fused": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i, _vp]),
     "mgpu_dequant": (_vp, [_vp, _vp, _vp, _i64, _i]),
     "mgpu_argmax": (_vp, [_vp, _vp, _i, _vp]),
     "mgpu_argmax_logits": (_i, [_vp, _vp, _i]),
@@ -394,6 +396,13 @@ def gemm_q(dev: Device, A: Buffer, W: Buffer, C: Buffer, M: int, N: int, K: int,
 
 def gemm(dev: Device, A: Buffer, B: Buffer, C: Buffer, M: int, N: int, K: int, bias: Buffer | None = None) -> Event:
     return _ev(lib().mgpu_gemm(dev.h, A.h, B.h, C.h, M, N, K, _h(bias)), "gemm")
+
+
+def gemm_fused(dev: Device, A: Buffer, B: Buffer, C: Buffer, M: int, N: int, K: int, bias: Buffer | None = None,
+               act: int = ACT_NONE, residual: Buffer | None = None) -> Event:
+    """C = act(A . op(B) + bias) + residual in one GEMM (the reference's GEMM, activation and
+    residual-add kernels in sequence); residual may be C itself."""
+    return _ev(lib().mgpu_gemm_fused(dev.h, A.h, B.h, C.h, M, N, K, _h(bias), act, _h(residual)), "gemm_fused")
 
 
 def dequant(dev: Device, W: Buffer, out: Buffer, n: int, qtype: int) -> Event:

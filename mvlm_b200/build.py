@@ -12,6 +12,7 @@ import argparse
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
@@ -33,7 +34,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     os.makedirs(BUILD, exist_ok=True)
     deps = [os.path.join(CSRC, h) for h in HEADERS]
     deps.append(os.path.join(os.path.dirname(HERE), "include", "mgpu_cuda.h"))
-    objs = []
+    objs, jobs = [], []
     relinked = force or not os.path.exists(LIB)
     for s in SOURCES:
         src = os.path.join(CSRC, s)
@@ -47,7 +48,11 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
             cmd += ["-Xptxas", "-v"]
         if verbose:
             print(" ".join(cmd))
-        r = subprocess.run(cmd, capture_output=True, text=True)
+        jobs.append((s, cmd))
+    # the translation units are independent: compile them side by side
+    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as pool:
+        results = list(pool.map(lambda j: (j[0], subprocess.run(j[1], capture_output=True, text=True)), jobs))
+    for s, r in results:
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {s}:\n{r.stdout}\n{r.stderr}")
         if verbose or ptxas_info:

@@ -11,6 +11,7 @@
 #include <stdint.h>
 
 #include "../../include/mgpu_cuda.h"
+#include "kernels.h"
 
 namespace mgpu_dev {
 
@@ -259,6 +260,37 @@ template <typename T> __device__ __forceinline__ T from_f32(float v);
 template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
 template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
 template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// ------------------------------------------------------------------ fused epilogue --
+
+// act(v) in fp32.  GELU is the tanh approximation with tanh(a) = 1 - 2 / (exp(2a) + 1), which
+// saturates to +-1 without a NaN; GELU_AS_SHIPPED reverses tanh's sign as the reference's gelu
+// kernel does (activations.cl:94-106: 1 - 2 / (1 + exp(-2a)) = -tanh(a)); SILU is the
+// reference's x / (1 + exp(-x)) (activations.cl:48-56).  The fast intrinsics (the reference uses
+// native_exp / native_recip likewise) keep the epilogue's register footprint small; a
+// denominator that overflows to infinity gives 0, the function's limit.
+__device__ __forceinline__ float activate(int act, float v) {
+    if (act == MGPU_ACT_SILU) return __fdividef(v, 1.0f + __expf(-v));
+    if (act == MGPU_ACT_GELU || act == MGPU_ACT_GELU_AS_SHIPPED) {
+        const float inner = 0.7978845608f * fmaf(0.044715f, v * v * v, v);
+        float t = 1.0f - __fdividef(2.0f, __expf(2.0f * inner) + 1.0f);
+        if (act == MGPU_ACT_GELU_AS_SHIPPED) t = -t;
+        return 0.5f * v * (1.0f + t);
+    }
+    return v;
+}
+
+__device__ __forceinline__ float epilogue_finish(const mgpu_k::Epilogue& e, int row, int n, float v) {
+    v = activate(e.act, v);
+    if (e.resid) {
+        const size_t i = (size_t)row * e.ldr + n;
+        if (e.resid_type == MGPU_F32) v += reinterpret_cast<const float*>(e.resid)[i];
+        else if (e.resid_type == MGPU_F16) v += __half2float(reinterpret_cast<const __half*>(e.resid)[i]);
+        else v += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(e.resid)[i]);
+    }
+    return v;
+}
+__device__ __forceinline__ bool epilogue_active(const mgpu_k::Epilogue& e) { return e.act != MGPU_ACT_NONE || e.resid; }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t d;

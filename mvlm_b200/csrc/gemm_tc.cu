@@ -83,6 +83,7 @@ struct GemmArgs {
     int c_type;
     const void* bias;
     int bias_type;
+    mgpu_k::Epilogue epi;  // activation / residual after the bias
     const uint8_t* Bq;   // packed GGUF rows (quantised modes)
     int64_t bq_row_bytes;
     const uint8_t* bq_end;
@@ -489,6 +490,11 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                     for (int i = 0; i < 32; ++i)
                         if (n0 + i < g.N) v[i] += bias_at(g.bias, g.bias_type, n0 + i);
                 }
+                if (epilogue_active(g.epi) && row < g.M) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (n0 + i < g.N) v[i] = epilogue_finish(g.epi, row, n0 + i, v[i]);
+                }
                 if (row < g.M && n0 < g.N) {
                     const size_t base = (size_t)row * g.ldc + n0;
                     if (vec_ok && n0 + 32 <= g.N && g.c_type != MGPU_F32) {
@@ -560,6 +566,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                             if (n + i >= n_base + cols) break;
                             float o = sum[i];
                             if (g.bias) o += bias_at(g.bias, g.bias_type, n + i);
+                            o = epilogue_finish(g.epi, row, n + i, o);
                             store_out(g.C, g.c_type, (size_t)row * g.ldc + n + i, o);
                         }
                     }
@@ -761,6 +768,11 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     if (n + j < g.N) o[j] += bias_at(g.bias, g.bias_type, n + j);
+            }
+            if (epilogue_active(g.epi)) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (n + j < g.N) o[j] = epilogue_finish(g.epi, row, n + j, o[j]);
             }
             const size_t base = (size_t)row * g.ldc + n;
             if (vec && n + 4 <= g.N) {
@@ -1103,10 +1115,11 @@ bool make_tensor_map_u16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t 
 }
 
 cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
-                 const void* bias, int bias_type, int M, int N, int K, const GemmSplitScratch* split) {
+                 const void* bias, int bias_type, int M, int N, int K, const GemmSplitScratch* split,
+                 const Epilogue& epi) {
     if (gemm_check(A, B, C, M, N, K)) return cudaErrorInvalidValue;
     // A few sequences against Q4_0 weights (batched decode): the streaming skinny kernel.
-    if (skinny_ok(A, B, M, N, K)) return gemm_q4_skinny(c, A, B, C, bias, bias_type, M, N, K);
+    if (skinny_ok(A, B, M, N, K)) return gemm_q4_skinny(c, A, B, C, bias, bias_type, M, N, K, epi);
     GemmPlan p = plan_gemm(c, A, B, M, N, K);
     if (p.splits > 1 && p.csplit == 1 && (!split || !split->tickets || !split->partials ||
                          (size_t)p.splits * M * N > split->max_partials ||
@@ -1128,6 +1141,7 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
     g.c_type = C.type;
     g.bias = bias;
     g.bias_type = bias_type;
+    g.epi = epi;
     g.Bq = nullptr;
     g.bq_row_bytes = 0;
     g.bq_end = nullptr;

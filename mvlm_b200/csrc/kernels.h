@@ -7,6 +7,15 @@
 
 namespace mgpu_k {
 
+// What a GEMM epilogue applies after its bias: C = act(v) + residual[row][n] (mgpu_act; the
+// residual is [M][ldr] of resid_type f32 / f16 / bf16, or null).  Zero-initialised: nothing.
+struct Epilogue {
+    int act = 0;
+    const void* resid = nullptr;
+    int resid_type = 0;
+    int64_t ldr = 0;
+};
+
 struct LaunchCtx {
     cudaStream_t stream;
     int sm_count;
@@ -72,11 +81,12 @@ size_t gemm_split_bytes(const LaunchCtx& c, const GemmOperand& A, const GemmOper
 // C[M,N] = A[M,K] * op(B) (+ bias[N]); A row-major [M][lda].  `split` may be null (no
 // split-K, whatever the plan says).
 cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
-                 const void* bias, int bias_type, int M, int N, int K, const GemmSplitScratch* split);
+                 const void* bias, int bias_type, int M, int N, int K, const GemmSplitScratch* split,
+                 const Epilogue& epi = Epilogue());
 // Skinny GEMM for batched decode (skinny.cu): Q4_0 W [N][K/32] rows, bf16/fp16 A, M <= 32.
 bool skinny_ok(const GemmOperand& A, const GemmOperand& B, int M, int N, int K);
 cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
-                           const void* bias, int bias_type, int M, int N, int K);
+                           const void* bias, int bias_type, int M, int N, int K, const Epilogue& epi = Epilogue());
 // A 2-D TMA map over 16-bit units without swizzle: `rows` x `cols`, row pitch `ld` units, box
 // {box_cols, box_rows} (gemm_tc.cu).
 bool make_tensor_map_u16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,

@@ -203,7 +203,8 @@ int64_t ld_or(const mgpu_buf* b, int64_t dflt) { return b->ld > 0 ? b->ld : dflt
 
 // Validate and enqueue one GEMM; false (with the error set) when it cannot run.
 bool gemm_checked(mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N, int K, mgpu_buf* bias,
-                  const char* who, size_t scratch_base = kScratchOffset) {
+                  const char* who, size_t scratch_base = kScratchOffset, int act = MGPU_ACT_NONE,
+                  mgpu_buf* residual = nullptr) {
 #define GREQ(cond, ...)                                  \
     do {                                                 \
         if (!(cond)) {                                   \
@@ -266,6 +267,30 @@ bool gemm_checked(mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M
     if (bias)
         GREQ(is_float_type(bias->type) && bias->bytes >= (size_t)N * elem_size(bias->type),
              "%s: bias must hold N float values", who);
+    GREQ(act >= MGPU_ACT_NONE && act <= MGPU_ACT_GELU_AS_SHIPPED, "%s: unknown activation %d", who, act);
+    mgpu_k::Epilogue epi;
+    epi.act = act;
+    if (residual) {
+        epi.resid = residual->ptr;
+        epi.resid_type = residual->type;
+        epi.ldr = ld_or(residual, N);
+        GREQ(is_float_type(residual->type), "%s: residual must be f32, f16 or bf16", who);
+        GREQ(epi.ldr >= N, "%s: residual row pitch %lld is below N=%d", who, (long long)epi.ldr, N);
+        GREQ(residual->bytes >= ((size_t)(M - 1) * epi.ldr + N) * elem_size(residual->type),
+             "%s: residual buffer too small for M=%d N=%d", who, M, N);
+        // in place (residual == C) is fine: each element is read and written by one thread;
+        // any other overlap with C would be read after another thread wrote it
+        if (residual->ptr != C->ptr) {
+            const char* r0 = (const char*)residual->ptr;
+            const char* r1 = r0 + ((size_t)(M - 1) * epi.ldr + N) * elem_size(residual->type);
+            const char* c0 = (const char*)C->ptr;
+            const char* c1 = c0 + ((size_t)(M - 1) * c.ld + N) * elem_size(C->type);
+            GREQ(r1 <= c0 || c1 <= r0, "%s: residual overlaps C without being C", who);
+        } else {
+            GREQ(residual->type == C->type && epi.ldr == c.ld, "%s: an in-place residual must have C's type and pitch",
+                 who);
+        }
+    }
 #undef GREQ
     mgpu_k::GemmSplitScratch split{};
     if (split_bytes) {
@@ -275,18 +300,18 @@ bool gemm_checked(mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M
         split.max_partials = split_bytes / sizeof(float);
     }
     cudaError_t e = mgpu_k::gemm(ctx_of(dev), a, b, c, bias ? bias->ptr : nullptr, bias ? bias->type : 0, M, N, K,
-                                 split_bytes ? &split : nullptr);
+                                 split_bytes ? &split : nullptr, epi);
     return cuda_ok(e, who);
 }
 
 mgpu_event* run_gemm(const mgpu_device* cdev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N, int K,
-                     mgpu_buf* bias, const char* who) {
+                     mgpu_buf* bias, const char* who, int act = MGPU_ACT_NONE, mgpu_buf* residual = nullptr) {
     API_ENTRY();
     REQUIRE(cdev, "%s: null device", who);
     mgpu_device* dev = const_cast<mgpu_device*>(cdev);
     DeviceGuard g(dev->ordinal);
     mgpu_event* ev = event_begin(dev);
-    if (!gemm_checked(dev, A, B, C, M, N, K, bias, who)) {
+    if (!gemm_checked(dev, A, B, C, M, N, K, bias, who, kScratchOffset, act, residual)) {
         if (ev) dev->event_pool.push_back(ev);
         return nullptr;
     }
@@ -580,6 +605,11 @@ mgpu_event* mgpu_gemm(const mgpu_device* d, mgpu_buf* A, mgpu_buf* B, mgpu_buf* 
                       mgpu_buf* bias) {
     API_ENTRY();
     return run_gemm(d, A, B, C, M, N, K, bias, "mgpu_gemm");
+}
+mgpu_event* mgpu_gemm_fused(const mgpu_device* d, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N, int K,
+                            mgpu_buf* bias, int act, mgpu_buf* residual) {
+    API_ENTRY();
+    return run_gemm(d, A, B, C, M, N, K, bias, "mgpu_gemm_fused", act, residual);
 }
 mgpu_event* mgpu_gemm_q(const mgpu_device* d, mgpu_buf* A, mgpu_buf* W, mgpu_buf* C, int M, int N, int K, int type,
                         mgpu_buf* bias) {

@@ -50,6 +50,7 @@ struct SkinnyArgs {
     int c_type;
     const void* bias;
     int bias_type;
+    mgpu_k::Epilogue epi;  // activation / residual after the bias
     int S, N, K;
     int stages;
     uint32_t sub_bytes;    // one sub-slice: TR x 144 weight bytes, then 2 x 8 NT x 272 activation bytes
@@ -291,12 +292,14 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         if (!mbar_wait(&red_bar, (uint32_t)c & 1u, a.status)) return;
         const int row0 = r0 + c * TR;
         const int nrows = min(TR, r1 - row0);
+        const bool fused = epilogue_active(a.epi);
         for (int i = tid; i < nrows * ns; i += 256) {
             const int sq = i / nrows, r = i % nrows;  // consecutive threads: consecutive rows
             float v = 0.0f;
 #pragma unroll
             for (int w = 0; w < WPG; ++w) v += red[((size_t)w * TR + r) * SP + sq];
             if (a.bias) v += bias_value(a.bias, a.bias_type, row0 + r);
+            if (fused) v = epilogue_finish(a.epi, seq0 + sq, row0 + r, v);
             store_value(a.C, a.c_type, (size_t)(seq0 + sq) * a.ldc + row0 + r, v);
         }
         __syncwarp();
@@ -357,7 +360,7 @@ bool skinny_ok(const GemmOperand& A, const GemmOperand& B, int M, int N, int K) 
 }
 
 cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
-                           const void* bias, int bias_type, int M, int N, int K) {
+                           const void* bias, int bias_type, int M, int N, int K, const Epilogue& epi) {
     if (!skinny_ok(A, B, M, N, K)) return cudaErrorInvalidValue;
     const int NT = M <= 8 ? 1 : M <= 16 ? 2 : 4;
     const int SP = 8 * NT;
@@ -397,6 +400,7 @@ cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmO
     a.c_type = C.type;
     a.bias = bias;
     a.bias_type = bias_type;
+    a.epi = epi;
     a.S = M;
     a.N = N;
     a.K = K;

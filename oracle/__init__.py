@@ -62,6 +62,9 @@ def lib():
             getattr(L, n).argtypes = [vp, vp, i32, vp, i32, i32, i32]
         L.ora_add_bias.argtypes = [vp, vp, i32, i32]
         L.ora_im2col.argtypes = [vp, vp, i32, i32, i32, i32, i32]
+        L.ora_activate.argtypes = [ctypes.c_float, i32]
+        L.ora_activate.restype = ctypes.c_float
+        L.ora_activate_n.argtypes = [vp, sz, i32]
         for n in ("ora_f32_to_f16_n", "ora_f16_to_f32_n", "ora_f32_to_bf16_n", "ora_bf16_to_f32_n"):
             getattr(L, n).argtypes = [vp, vp, sz]
         L.ora_type_size.argtypes = [i32]
@@ -220,6 +223,40 @@ def add_bias(C, bias, M, N):
     C = np.ascontiguousarray(C, np.float32).copy()
     lib().ora_add_bias(_p(C), _p(np.ascontiguousarray(bias, np.float32)), M, N)
     return C
+
+
+def activate(x, act: int):
+    """activations.cl's silu / gelu on fp32 values (act 1 gelu with tanh, 2 silu, 3 gelu as
+    activations.cl:78-117 computes it)."""
+    y = np.ascontiguousarray(x, np.float32).copy()
+    lib().ora_activate_n(_p(y), y.size, int(act))
+    return y
+
+
+def round_to(x, t: int):
+    """x rounded to the storage type t (F32 0, F16 1, BF16 30) and read back as fp32."""
+    if t == 1:
+        return f16_to_f32(f16(x))
+    if t == 30:
+        return bf16_to_f32(bf16(x))
+    return np.ascontiguousarray(x, np.float32)
+
+
+def unfused_epilogue(acc, bias, act: int, resid, M: int, N: int, ctype: int):
+    """The reference's chain after a GEMM, each kernel storing its output in ctype: the GEMM
+    (+ bias, vision.cl:430-434) stores C, the activation kernel (activations.cl:30-117) reads
+    and rewrites it, the residual add (vector_add, activations.cl:271-299, through
+    dispatch_residual_add, moondream2.cpp:297-300) adds resid.  resid is fp32 values already
+    in their storage type."""
+    c = np.ascontiguousarray(acc, np.float32).reshape(M * N)
+    if bias is not None:
+        c = add_bias(c, bias, M, N)
+    c = round_to(c, ctype)
+    if act:
+        c = round_to(activate(c, act), ctype)
+    if resid is not None:
+        c = round_to(c + np.ascontiguousarray(resid, np.float32).reshape(M * N), ctype)
+    return c
 
 
 def im2col(img, C, H, W, ph, pw):

@@ -295,6 +295,27 @@ void ora_add_bias(float* C, const float* bias, int M, int N) {
         for (int n = 0; n < N; ++n) C[(size_t)m * N + n] += bias[n];
 }
 
+/* Elementwise kernels of src/kernels/activations.cl, one element as the kernels' scalar tails
+ * compute it (fp32 math; native_exp and native_recip taken as exp and 1/x):
+ *   act 2, silu (:30-65): x * 1 / (1 + exp(-x));
+ *   act 3, gelu as the kernel computes it (:78-117): inner = 0.7978845608 * fma(0.044715, x^3, x),
+ *          tanh_val = 1 - 2 / (1 + exp(-2 inner)), 0.5 x (1 + tanh_val);
+ *   act 1, gelu as compute.h:48 states it: the same with tanh_val = tanh(inner). */
+float ora_activate(float x, int act) {
+    if (act == 2) return x * (1.0f / (1.0f + expf(-x)));
+    if (act == 1 || act == 3) {
+        float x3 = x * x * x;
+        float inner = 0.7978845608f * fmaf(0.044715f, x3, x);
+        float t = act == 3 ? 1.0f - 2.0f * (1.0f / (1.0f + expf(-2.0f * inner))) : tanhf(inner);
+        return 0.5f * x * (1.0f + t);
+    }
+    return x;
+}
+
+void ora_activate_n(float* x, size_t n, int act) {
+    for (size_t i = 0; i < n; ++i) x[i] = ora_activate(x[i], act);
+}
+
 /* patch_embed (vision.cl:118-197): patch p = (row, col) of a (H/ph) x (W/pw) grid; its
  * feature index runs over c, then py, then px (the loop nest at :154-176). */
 void ora_im2col(const float* img, float* patches, int C, int H, int W, int ph, int pw) {

@@ -67,6 +67,10 @@ void ora_gemm_q(const float* A, const uint8_t* W, float* C, int M, int N, int K,
 void ora_gemm_nk(const float* A, const void* W, int wtype, float* C, int M, int N, int K);
 /* bias epilogue of patch_embed / vision_proj (vision.cl:180-186, :430-434): C[m,n] += bias[n]. */
 void ora_add_bias(float* C, const float* bias, int M, int N);
+/* activations.cl elementwise kernels on one fp32 value (act: 1 gelu with tanh, 2 silu,
+ * 3 gelu as activations.cl:78-117 computes it); the _n form works in place. */
+float ora_activate(float x, int act);
+void ora_activate_n(float* x, size_t n, int act);
 /* patch_embed im2col order (vision.cl:154-176): patches[p][c*ph*pw + py*pw + px]. */
 void ora_im2col(const float* img, float* patches, int C, int H, int W, int ph, int pw);
 

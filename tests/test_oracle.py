@@ -187,3 +187,27 @@ def test_argmax_logits_known_answers():
     assert O.argmax_logits(h(0xFBFF, 0x7C00, 0x7BFF), O.F16)[0] == 1              # +Inf reads 1e30
     f = np.array([-2.0, np.float32(1e-40), -1.0, 3.0, 3.0], np.float32)
     assert O.argmax_logits(f.view(np.uint32), O.F32)[0] == 3
+
+
+def test_activation_restatement():
+    # activations.cl:78-117 computes tanh as 1 - 2 / (1 + exp(-2a)) = -tanh(a), so the shipped
+    # gelu is x - gelu(x) where gelu is the tanh form compute.h:48 states
+    x = np.linspace(-12, 12, 4001).astype(np.float32)
+    g, shipped, silu = O.activate(x, 1), O.activate(x, 3), O.activate(x, 2)
+    assert np.max(np.abs(shipped - (x - g))) <= 2e-6 * np.max(np.abs(x))
+    assert abs(float(O.activate(np.float32([1.0]), 1)[0]) - 0.8411920) < 1e-6
+    assert abs(float(O.activate(np.float32([1.0]), 2)[0]) - 0.7310586) < 1e-6
+    assert np.all(np.isfinite(O.activate(np.float32([-1e30, 1e30, -100, 100]), 1)))
+    # silu = x * sigmoid(x): 0 at 0, -> x for large x, -> 0 for very negative x
+    assert silu[2000] == 0.0 and abs(silu[-1] - 12) < 1e-4 and abs(silu[0]) < 1e-4
+
+
+def test_unfused_epilogue_rounds_after_each_kernel():
+    M, N = 3, 5
+    acc = O.normal(M * N, 1, 3.0)
+    bias = O.normal(N, 2, 1.0)
+    resid = O.f16_to_f32(O.f16(O.normal(M * N, 3, 1.0)))
+    c = O.f16_to_f32(O.f16(acc.reshape(M, N) + bias)).reshape(-1)
+    c = O.f16_to_f32(O.f16(O.activate(c, 2)))
+    want = O.f16_to_f32(O.f16(c + resid))
+    assert np.array_equal(O.unfused_epilogue(acc, bias, 2, resid, M, N, 1), want)
