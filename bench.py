@@ -20,6 +20,8 @@ cpu_baseline: the CPU restatement of the reference's quantised path (dequantise 
           OpenMP over all host cores, on a bounded sample of the same workload.
 prefill : secondary metric: tcgen05 GEMM TFLOP/s on the Phi-1.5 prefill shapes (M=761, Q8_0
           weights dequantised to bf16 in the weight loads).
+fused_epilogues: the Phi-1.5 prefill MLP GEMMs with their activation / gate product /
+          residual add fused into the epilogue, each against the plain GEMM of the same shape.
 
 With --gpus N (launched by torchrun, one process per GPU, NCCL): the lm_head is
 column-sharded (51200/N output rows of W per rank) and the logits are all-gathered with NCCL
@@ -291,7 +293,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         if world == 1:
             secondary = {"fp32_gemv": run_fp32_gemv(dev, mg, torch, stream, peaks),
                          "batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head),
-                         "siglip": run_siglip(dev, mg, torch, stream, peaks)}
+                         "siglip": run_siglip(dev, mg, torch, stream, peaks),
+                         "fused_epilogues": _guarded(run_fused_epilogues, dev, mg, torch, stream, peaks)}
         else:
             # every rank takes part (collectives); rank 0 reports
             secondary = {"batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head,
@@ -487,6 +490,71 @@ def run_prefill(dev, mg, torch, stream, peaks) -> dict:
             "peak": peaks["bf16_tflops"], "peak_source": peaks["source"],
             "timing": "CUDA events around 5 replays of a captured graph of one launch per weight copy; "
                       "copies rotated so each pass reads ~256 MB of packed weights (2x L2)"}
+
+
+def _guarded(fn, *args) -> dict:
+    """Run a secondary measurement; a failure is reported in its place instead of losing the
+    headline line."""
+    try:
+        return fn(*args)
+    except Exception as e:  # noqa: BLE001
+        return {"error": f"{type(e).__name__}: {e}"}
+
+
+def run_fused_epilogues(dev, mg, torch, stream, peaks) -> dict:
+    """The fused GEMM epilogues on the Phi-1.5 prefill MLP shapes (M=761, bf16 A, Q8_0 W, bf16
+    C), each timed against the plain GEMM of the same shape: fc1 2048x8192 with bias + GELU,
+    the SiLU-gated MLP's gate GEMM (silu(A.W^T) * up), and fc2 8192x2048 with the residual added
+    in place.  Weight copies rotate through ~256 MB per pass (2x L2), one launch per copy in a
+    captured graph.  `unfused_floor_us` = plain GEMM time + the HBM time of the elementwise
+    passes the fusion removes (the reference's separate activation / multiply / add kernels at
+    the measured copy bandwidth, launch cost not counted): a lower bound on the unfused chain."""
+    M = 761
+    out = {}
+    tmp = dev.empty(8192 * 2048, mg.F32)
+    for name, K, N, variant, extra in (("fc1_bias_gelu", 2048, 8192, "gelu", 2),
+                                       ("gate_silu_mul_up", 2048, 8192, "silu_gate", 3),
+                                       ("fc2_residual_in_place", 8192, 2048, "residual", 3)):
+        wbytes = N * (K // 32) * 34
+        ncopy = max(4, -(-256_000_000 // wbytes))
+        A = dev.empty(M * K, mg.BF16)
+        dev.fill_normal(A, M * K, SEED + 3 * K, 1.0)
+        Ws = []
+        for c in range(ncopy):
+            w = dev.create_buffer(wbytes, None, mg.Q8_0, mg.LAYOUT_NK, N, K)
+            dev.fill_normal(tmp, N * K, SEED + 5 * N + 13 * c, 0.02)
+            dev.quantize(tmp, w, N * K, mg.Q8_0)
+            Ws.append(w)
+        C = dev.empty(M * N, mg.BF16)
+        R = dev.empty(M * N, mg.BF16)
+        dev.fill_normal(R, M * N, SEED + 7, 1.0)
+        bias = dev.empty(N, mg.F32)
+        dev.fill_normal(bias, N, SEED + 9, 0.5)
+
+        def plain():
+            for w in Ws:
+                mg.gemm_q(dev, A, w, C, M, N, K, mg.Q8_0)
+
+        def fused():
+            for w in Ws:
+                if variant == "gelu":
+                    mg.gemm_fused(dev, A, w, C, M, N, K, bias, mg.ACT_GELU, None)
+                elif variant == "silu_gate":
+                    mg.gemm_silu_gate(dev, A, w, R, C, M, N, K)
+                else:
+                    mg.gemm_fused(dev, A, w, R, M, N, K, None, mg.ACT_NONE, R)
+
+        us_plain = time_graph(dev, torch, stream, plain, reps=5) * 1e3 / ncopy
+        us_fused = time_graph(dev, torch, stream, fused, reps=5) * 1e3 / ncopy
+        saved = extra * M * N * 2
+        floor = us_plain + saved / (peaks["hbm_gbs"] * 1e3)
+        out[name] = {"K": K, "N": N, "plain_us": round(us_plain, 2), "fused_us": round(us_fused, 2),
+                     "epilogue_overhead": round(us_fused / us_plain - 1.0, 4),
+                     "hbm_bytes_saved": saved, "unfused_floor_us": round(floor, 2),
+                     "speedup_vs_unfused_floor": round(floor / us_fused, 3)}
+        del Ws, A, C, R
+    return {"M": M, "weights": "Q8_0", "activations": "bf16", "out": "bf16", "shapes": out,
+            "timing": "CUDA events around 5 replays of a captured graph of one launch per weight copy"}
 
 
 def time_graph(dev, torch, stream, enqueue, reps: int, flush=None) -> float:

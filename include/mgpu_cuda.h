@@ -201,6 +201,14 @@ enum mgpu_act {
  * is rounded once, where the reference rounds to fp16 after each kernel. */
 mgpu_event* mgpu_gemm_fused(const mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N,
                             int K, mgpu_buf* bias, int act, mgpu_buf* residual);
+/* out = silu(A * op(W_gate)) * up, elementwise, in the gate GEMM's epilogue.  Replaces the
+ * gate projection's dispatch_gemm_image followed by dispatch_silu_gate_multiply
+ * (src/engine/compute.h:57-60, activations.cl:219-265), as moondream2_forward chains them
+ * (src/models/moondream2.cpp:465-495): the gate activations are never stored.  up is [M][N]
+ * (f32 / f16 / bf16, own row pitch, default N), the up projection's output; out may be up
+ * itself. */
+mgpu_event* mgpu_gemm_silu_gate(const mgpu_device* dev, mgpu_buf* A, mgpu_buf* W_gate, mgpu_buf* up,
+                                mgpu_buf* out, int M, int N, int K);
 /* out[n] = dequant(W)[n] for n elements (out fp32, fp16 or bf16 per its tag). */
 mgpu_event* mgpu_dequant(const mgpu_device* dev, mgpu_buf* W, mgpu_buf* out, int64_t n, int type);
 

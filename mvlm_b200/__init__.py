@@ -71,6 +71,7 @@ SIGNATURES = {
     "mgpu_gemm_q": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "mgpu_gemm": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "mgpu_gemm_fused": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i, _vp]),
+    "mgpu_gemm_silu_gate": (_vp, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
     "mgpu_dequant": (_vp, [_vp, _vp, _vp, _i64, _i]),
     "mgpu_argmax": (_vp, [_vp, _vp, _i, _vp]),
     "mgpu_argmax_logits": (_i, [_vp, _vp, _i]),
@@ -403,6 +404,11 @@ def gemm_fused(dev: Device, A: Buffer, B: Buffer, C: Buffer, M: int, N: int, K: 
     """C = act(A . op(B) + bias) + residual in one GEMM (the reference's GEMM, activation and
     residual-add kernels in sequence); residual may be C itself."""
     return _ev(lib().mgpu_gemm_fused(dev.h, A.h, B.h, C.h, M, N, K, _h(bias), act, _h(residual)), "gemm_fused")
+
+
+def gemm_silu_gate(dev: Device, A: Buffer, W_gate: Buffer, up: Buffer, out: Buffer, M: int, N: int, K: int) -> Event:
+    """out = silu(A . op(W_gate)) * up (the gate GEMM and silu_gate_multiply in one kernel)."""
+    return _ev(lib().mgpu_gemm_silu_gate(dev.h, A.h, W_gate.h, up.h, out.h, M, N, K), "gemm_silu_gate")
 
 
 def dequant(dev: Device, W: Buffer, out: Buffer, n: int, qtype: int) -> Event:

@@ -280,17 +280,21 @@ __device__ __forceinline__ float activate(int act, float v) {
     return v;
 }
 
+__device__ __forceinline__ float load_float(const void* p, int type, size_t i) {
+    if (type == MGPU_F32) return reinterpret_cast<const float*>(p)[i];
+    if (type == MGPU_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+
 __device__ __forceinline__ float epilogue_finish(const mgpu_k::Epilogue& e, int row, int n, float v) {
     v = activate(e.act, v);
-    if (e.resid) {
-        const size_t i = (size_t)row * e.ldr + n;
-        if (e.resid_type == MGPU_F32) v += reinterpret_cast<const float*>(e.resid)[i];
-        else if (e.resid_type == MGPU_F16) v += __half2float(reinterpret_cast<const __half*>(e.resid)[i]);
-        else v += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(e.resid)[i]);
-    }
+    if (e.mul) v *= load_float(e.mul, e.mul_type, (size_t)row * e.ldm + n);
+    if (e.resid) v += load_float(e.resid, e.resid_type, (size_t)row * e.ldr + n);
     return v;
 }
-__device__ __forceinline__ bool epilogue_active(const mgpu_k::Epilogue& e) { return e.act != MGPU_ACT_NONE || e.resid; }
+__device__ __forceinline__ bool epilogue_active(const mgpu_k::Epilogue& e) {
+    return e.act != MGPU_ACT_NONE || e.resid || e.mul;
+}
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t d;

@@ -7,13 +7,16 @@
 
 namespace mgpu_k {
 
-// What a GEMM epilogue applies after its bias: C = act(v) + residual[row][n] (mgpu_act; the
-// residual is [M][ldr] of resid_type f32 / f16 / bf16, or null).  Zero-initialised: nothing.
+// What a GEMM epilogue applies after its bias: C = act(v) * mul[row][n] + residual[row][n]
+// (mgpu_act; mul and residual are [M][ld] of f32 / f16 / bf16, or null).  Default: nothing.
 struct Epilogue {
     int act = 0;
     const void* resid = nullptr;
     int resid_type = 0;
     int64_t ldr = 0;
+    const void* mul = nullptr;
+    int mul_type = 0;
+    int64_t ldm = 0;
 };
 
 struct LaunchCtx {

@@ -204,7 +204,7 @@ int64_t ld_or(const mgpu_buf* b, int64_t dflt) { return b->ld > 0 ? b->ld : dflt
 // Validate and enqueue one GEMM; false (with the error set) when it cannot run.
 bool gemm_checked(mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N, int K, mgpu_buf* bias,
                   const char* who, size_t scratch_base = kScratchOffset, int act = MGPU_ACT_NONE,
-                  mgpu_buf* residual = nullptr) {
+                  mgpu_buf* residual = nullptr, mgpu_buf* mul = nullptr) {
 #define GREQ(cond, ...)                                  \
     do {                                                 \
         if (!(cond)) {                                   \
@@ -270,26 +270,36 @@ bool gemm_checked(mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M
     GREQ(act >= MGPU_ACT_NONE && act <= MGPU_ACT_GELU_AS_SHIPPED, "%s: unknown activation %d", who, act);
     mgpu_k::Epilogue epi;
     epi.act = act;
-    if (residual) {
-        epi.resid = residual->ptr;
-        epi.resid_type = residual->type;
-        epi.ldr = ld_or(residual, N);
-        GREQ(is_float_type(residual->type), "%s: residual must be f32, f16 or bf16", who);
-        GREQ(epi.ldr >= N, "%s: residual row pitch %lld is below N=%d", who, (long long)epi.ldr, N);
-        GREQ(residual->bytes >= ((size_t)(M - 1) * epi.ldr + N) * elem_size(residual->type),
-             "%s: residual buffer too small for M=%d N=%d", who, M, N);
-        // in place (residual == C) is fine: each element is read and written by one thread;
-        // any other overlap with C would be read after another thread wrote it
-        if (residual->ptr != C->ptr) {
-            const char* r0 = (const char*)residual->ptr;
-            const char* r1 = r0 + ((size_t)(M - 1) * epi.ldr + N) * elem_size(residual->type);
+    // An [M][N] operand the epilogue reads (residual, multiplier): float type, room for M rows,
+    // and either C itself (same type and pitch: each element is read and then written by one
+    // thread) or disjoint from C (any other overlap would be read after another thread wrote it).
+    auto operand_ok = [&](mgpu_buf* X, const char* what, int64_t* ld_out) -> bool {
+        const int64_t ld = ld_or(X, N);
+        *ld_out = ld;
+        GREQ(is_float_type(X->type), "%s: %s must be f32, f16 or bf16", who, what);
+        GREQ(ld >= N, "%s: %s row pitch %lld is below N=%d", who, what, (long long)ld, N);
+        GREQ(X->bytes >= ((size_t)(M - 1) * ld + N) * elem_size(X->type), "%s: %s buffer too small for M=%d N=%d",
+             who, what, M, N);
+        if (X->ptr != C->ptr) {
+            const char* r0 = (const char*)X->ptr;
+            const char* r1 = r0 + ((size_t)(M - 1) * ld + N) * elem_size(X->type);
             const char* c0 = (const char*)C->ptr;
             const char* c1 = c0 + ((size_t)(M - 1) * c.ld + N) * elem_size(C->type);
-            GREQ(r1 <= c0 || c1 <= r0, "%s: residual overlaps C without being C", who);
+            GREQ(r1 <= c0 || c1 <= r0, "%s: %s overlaps C without being C", who, what);
         } else {
-            GREQ(residual->type == C->type && epi.ldr == c.ld, "%s: an in-place residual must have C's type and pitch",
-                 who);
+            GREQ(X->type == C->type && ld == c.ld, "%s: an in-place %s must have C's type and pitch", who, what);
         }
+        return true;
+    };
+    if (residual) {
+        if (!operand_ok(residual, "residual", &epi.ldr)) return false;
+        epi.resid = residual->ptr;
+        epi.resid_type = residual->type;
+    }
+    if (mul) {
+        if (!operand_ok(mul, "up", &epi.ldm)) return false;
+        epi.mul = mul->ptr;
+        epi.mul_type = mul->type;
     }
 #undef GREQ
     mgpu_k::GemmSplitScratch split{};
@@ -305,13 +315,14 @@ bool gemm_checked(mgpu_device* dev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M
 }
 
 mgpu_event* run_gemm(const mgpu_device* cdev, mgpu_buf* A, mgpu_buf* B, mgpu_buf* C, int M, int N, int K,
-                     mgpu_buf* bias, const char* who, int act = MGPU_ACT_NONE, mgpu_buf* residual = nullptr) {
+                     mgpu_buf* bias, const char* who, int act = MGPU_ACT_NONE, mgpu_buf* residual = nullptr,
+                     mgpu_buf* mul = nullptr) {
     API_ENTRY();
     REQUIRE(cdev, "%s: null device", who);
     mgpu_device* dev = const_cast<mgpu_device*>(cdev);
     DeviceGuard g(dev->ordinal);
     mgpu_event* ev = event_begin(dev);
-    if (!gemm_checked(dev, A, B, C, M, N, K, bias, who, kScratchOffset, act, residual)) {
+    if (!gemm_checked(dev, A, B, C, M, N, K, bias, who, kScratchOffset, act, residual, mul)) {
         if (ev) dev->event_pool.push_back(ev);
         return nullptr;
     }
@@ -610,6 +621,12 @@ mgpu_event* mgpu_gemm_fused(const mgpu_device* d, mgpu_buf* A, mgpu_buf* B, mgpu
                             mgpu_buf* bias, int act, mgpu_buf* residual) {
     API_ENTRY();
     return run_gemm(d, A, B, C, M, N, K, bias, "mgpu_gemm_fused", act, residual);
+}
+mgpu_event* mgpu_gemm_silu_gate(const mgpu_device* d, mgpu_buf* A, mgpu_buf* W_gate, mgpu_buf* up, mgpu_buf* out,
+                                int M, int N, int K) {
+    API_ENTRY();
+    REQUIRE(up, "mgpu_gemm_silu_gate: null up");
+    return run_gemm(d, A, W_gate, out, M, N, K, nullptr, "mgpu_gemm_silu_gate", MGPU_ACT_SILU, nullptr, up);
 }
 mgpu_event* mgpu_gemm_q(const mgpu_device* d, mgpu_buf* A, mgpu_buf* W, mgpu_buf* C, int M, int N, int K, int type,
                         mgpu_buf* bias) {

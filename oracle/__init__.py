@@ -65,6 +65,7 @@ def lib():
         L.ora_activate.argtypes = [ctypes.c_float, i32]
         L.ora_activate.restype = ctypes.c_float
         L.ora_activate_n.argtypes = [vp, sz, i32]
+        L.ora_silu_gate_n.argtypes = [vp, vp, vp, sz]
         for n in ("ora_f32_to_f16_n", "ora_f16_to_f32_n", "ora_f32_to_bf16_n", "ora_bf16_to_f32_n"):
             getattr(L, n).argtypes = [vp, vp, sz]
         L.ora_type_size.argtypes = [i32]
@@ -257,6 +258,17 @@ def unfused_epilogue(acc, bias, act: int, resid, M: int, N: int, ctype: int):
     if resid is not None:
         c = round_to(c + np.ascontiguousarray(resid, np.float32).reshape(M * N), ctype)
     return c
+
+
+def unfused_silu_gate(gate_acc, up, ctype: int):
+    """The reference's gate chain: the gate GEMM stores its output in ctype, then
+    silu_gate_multiply (activations.cl:219-265) reads gate and up and stores
+    silu(gate) * up in ctype.  up is fp32 values already in their storage type."""
+    g = round_to(gate_acc, ctype)
+    u = np.ascontiguousarray(up, np.float32).reshape(-1)
+    out = np.empty_like(g)
+    lib().ora_silu_gate_n(_p(g), _p(u), _p(out), g.size)
+    return round_to(out, ctype)
 
 
 def im2col(img, C, H, W, ph, pw):

@@ -316,6 +316,15 @@ void ora_activate_n(float* x, size_t n, int act) {
     for (size_t i = 0; i < n; ++i) x[i] = ora_activate(x[i], act);
 }
 
+/* silu_gate_multiply (activations.cl:219-265), scalar tail: gf * (1 / (1 + exp(-gf))) * uf. */
+void ora_silu_gate_n(const float* gate, const float* up, float* out, size_t n) {
+    for (size_t i = 0; i < n; ++i) {
+        float g = gate[i];
+        float sig = 1.0f / (1.0f + expf(-g));
+        out[i] = g * sig * up[i];
+    }
+}
+
 /* patch_embed (vision.cl:118-197): patch p = (row, col) of a (H/ph) x (W/pw) grid; its
  * feature index runs over c, then py, then px (the loop nest at :154-176). */
 void ora_im2col(const float* img, float* patches, int C, int H, int W, int ph, int pw) {

@@ -71,6 +71,8 @@ void ora_add_bias(float* C, const float* bias, int M, int N);
  * 3 gelu as activations.cl:78-117 computes it); the _n form works in place. */
 float ora_activate(float x, int act);
 void ora_activate_n(float* x, size_t n, int act);
+/* silu_gate_multiply (activations.cl:219-265) on fp32 values: out = silu(gate) * up. */
+void ora_silu_gate_n(const float* gate, const float* up, float* out, size_t n);
 /* patch_embed im2col order (vision.cl:154-176): patches[p][c*ph*pw + py*pw + px]. */
 void ora_im2col(const float* img, float* patches, int C, int H, int W, int ph, int pw);
 

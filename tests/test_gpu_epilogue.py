@@ -110,3 +110,23 @@ def test_fused_rejects_bad_arguments(dev):
     with pytest.raises(mg.MgpuError, match="overlaps C"):
         mg.gemm_fused(dev, dA, dW, C16, 16, 64, 256, None, mg.ACT_NONE, C16.view(16, 16 * 64 * 2))
     dev.finish()
+
+
+@pytest.mark.parametrize("qt,M,N,K", [(O.Q8_0, 761, 8192, 2048), (O.Q4_0, 8, 8192, 2048), (O.Q8_0, 8, 2048, 2048),
+                                      (O.Q8_0, 130, 300, 160)])
+def test_silu_gate(dev, qt, M, N, K):
+    # the SiLU-gated MLP of moondream2_forward (moondream2.cpp:465-495): up = A . W_up^T first,
+    # then out = silu(A . W_gate^T) * up in the gate GEMM's epilogue, against the reference's
+    # gate GEMM + silu_gate_multiply with fp16 stores in between
+    a, b, acc = _quant_case(qt, M, N, K, 3000 + M + N)
+    ct = mg.F16
+    up = O.f16_to_f32(O.f16(O.normal(M * N, 31, 1.0)))
+    ref = O.unfused_silu_gate(acc, up, ct)
+    dA, dW = dev.array(a[0], a[1]), dev.array(*b)
+    dU = dev.array(O.f16(up), ct)
+    out = dev.empty(M * N, ct)
+    mg.gemm_silu_gate(dev, dA, dW, dU, out, M, N, K).wait()
+    assert_close(O.f16_to_f32(out.read(np.uint16)), ref, TOL_16, f"silu gate q{qt} {M}x{N}x{K}")
+    # in place: the product overwrites up
+    mg.gemm_silu_gate(dev, dA, dW, dU, dU, M, N, K).wait()
+    assert_close(O.f16_to_f32(dU.read(np.uint16)), ref, TOL_16, f"silu gate in place q{qt} {M}x{N}x{K}")

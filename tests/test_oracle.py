@@ -211,3 +211,10 @@ def test_unfused_epilogue_rounds_after_each_kernel():
     c = O.f16_to_f32(O.f16(O.activate(c, 2)))
     want = O.f16_to_f32(O.f16(c + resid))
     assert np.array_equal(O.unfused_epilogue(acc, bias, 2, resid, M, N, 1), want)
+
+
+def test_silu_gate_restatement():
+    g = np.float32([-3.0, 0.0, 1.0, 2.5])
+    u = np.float32([2.0, 5.0, -1.0, 0.5])
+    want = O.round_to(O.activate(g, 2) * u, 1)
+    assert np.allclose(O.unfused_silu_gate(g, u, 1), want, rtol=1e-3, atol=0)
