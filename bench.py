@@ -293,8 +293,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         if world == 1:
             secondary = {"fp32_gemv": run_fp32_gemv(dev, mg, torch, stream, peaks),
                          "batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head),
-                         "siglip": run_siglip(dev, mg, torch, stream, peaks),
-                         "fused_epilogues": _guarded(run_fused_epilogues, dev, mg, torch, stream, peaks)}
+                         # before SigLIP, whose seconds of dense MMAs can leave the clocks power-capped
+                         "fused_epilogues": _guarded(run_fused_epilogues, dev, mg, torch, stream, peaks),
+                         "siglip": run_siglip(dev, mg, torch, stream, peaks)}
         else:
             # every rank takes part (collectives); rank 0 reports
             secondary = {"batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head,

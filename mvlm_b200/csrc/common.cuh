@@ -292,6 +292,83 @@ __device__ __forceinline__ float epilogue_finish(const mgpu_k::Epilogue& e, int 
     if (e.resid) v += load_float(e.resid, e.resid_type, (size_t)row * e.ldr + n);
     return v;
 }
+// Eight values of an [M][ld] operand at (row, n) .. (row, n + 7); columns at or past N read 0.
+__device__ __forceinline__ void load8(const void* p, int type, int64_t ld, int row, int n, int N, float (&o)[8]) {
+    const size_t base = (size_t)row * ld + n;
+    if (type == MGPU_F32) {
+        const float* q = reinterpret_cast<const float*>(p) + base;
+        if (n + 8 <= N && (reinterpret_cast<uintptr_t>(q) & 15) == 0) {
+            const float4 a = reinterpret_cast<const float4*>(q)[0], b = reinterpret_cast<const float4*>(q)[1];
+            o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = n + i < N ? q[i] : 0.0f;
+        }
+        return;
+    }
+    const uint16_t* q = reinterpret_cast<const uint16_t*>(p) + base;
+    uint32_t w[4];
+    if (n + 8 <= N && (reinterpret_cast<uintptr_t>(q) & 15) == 0) {
+        const uint4 t = *reinterpret_cast<const uint4*>(q);
+        w[0] = t.x; w[1] = t.y; w[2] = t.z; w[3] = t.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t lo = n + 2 * i < N ? q[2 * i] : 0u, hi = n + 2 * i + 1 < N ? q[2 * i + 1] : 0u;
+            w[i] = lo | (hi << 16);
+        }
+    }
+    if (type == MGPU_BF16) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            o[2 * i] = __uint_as_float(w[i] << 16);
+            o[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            o[2 * i] = f.x;
+            o[2 * i + 1] = f.y;
+        }
+    }
+}
+
+// The epilogue over one thread's 32 consecutive columns of a row (the tile epilogue's unit):
+// each choice (activation, operand types) is taken once per 32 values, and the operands are
+// read 16 bytes at a time, so the unrolled code stays small and its loads few.
+template <int ACT>
+__device__ __forceinline__ void activate32(float (&v)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = activate(ACT, v[i]);
+}
+__device__ __forceinline__ void epilogue_row32(const mgpu_k::Epilogue& e, int row, int n0, int N, float (&v)[32]) {
+    switch (e.act) {
+        case MGPU_ACT_GELU: activate32<MGPU_ACT_GELU>(v); break;
+        case MGPU_ACT_SILU: activate32<MGPU_ACT_SILU>(v); break;
+        case MGPU_ACT_GELU_AS_SHIPPED: activate32<MGPU_ACT_GELU_AS_SHIPPED>(v); break;
+        default: break;
+    }
+    if (e.mul) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            float m[8];
+            load8(e.mul, e.mul_type, e.ldm, row, n0 + 8 * g, N, m);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[8 * g + i] *= m[i];
+        }
+    }
+    if (e.resid) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            float r[8];
+            load8(e.resid, e.resid_type, e.ldr, row, n0 + 8 * g, N, r);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[8 * g + i] += r[i];
+        }
+    }
+}
+
 __device__ __forceinline__ bool epilogue_active(const mgpu_k::Epilogue& e) {
     return e.act != MGPU_ACT_NONE || e.resid || e.mul;
 }

@@ -485,16 +485,17 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
                     }
                     continue;
                 }
-                if (g.bias) {
+                if (g.bias && n0 < g.N) {
+                    // 16-byte loads, the type chosen once per eight values (columns past N add 0)
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (n0 + i < g.N) v[i] += bias_at(g.bias, g.bias_type, n0 + i);
-                }
-                if (epilogue_active(g.epi) && row < g.M) {
+                    for (int q8 = 0; q8 < 4; ++q8) {
+                        float b[8];
+                        load8(g.bias, g.bias_type, 0, 0, n0 + 8 * q8, g.N, b);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (n0 + i < g.N) v[i] = epilogue_finish(g.epi, row, n0 + i, v[i]);
+                        for (int i = 0; i < 8; ++i) v[8 * q8 + i] += b[i];
+                    }
                 }
+                if (epilogue_active(g.epi) && row < g.M && n0 < g.N) epilogue_row32(g.epi, row, n0, g.N, v);
                 if (row < g.M && n0 < g.N) {
                     const size_t base = (size_t)row * g.ldc + n0;
                     if (vec_ok && n0 + 32 <= g.N && g.c_type != MGPU_F32) {
