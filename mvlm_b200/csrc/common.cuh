@@ -263,19 +263,29 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 
 // ------------------------------------------------------------------ fused epilogue --
 
-// act(v) in fp32.  GELU is the tanh approximation with tanh(a) = 1 - 2 / (exp(2a) + 1), which
-// saturates to +-1 without a NaN; GELU_AS_SHIPPED reverses tanh's sign as the reference's gelu
-// kernel does (activations.cl:94-106: 1 - 2 / (1 + exp(-2a)) = -tanh(a)); SILU is the
-// reference's x / (1 + exp(-x)) (activations.cl:48-56).  The fast intrinsics (the reference uses
-// native_exp / native_recip likewise) keep the epilogue's register footprint small; a
-// denominator that overflows to infinity gives 0, the function's limit.
+// One MUFU tanh (PTX tanh.approx.f32: relative error about 2^-11, saturates to +-1).
+__device__ __forceinline__ float tanh_fast(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// act(v) in fp32, each with one tanh so the epilogue's instruction count stays low.  GELU is the
+// tanh approximation 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))); GELU_AS_SHIPPED reverses
+// tanh's sign as the reference's gelu kernel does (activations.cl:94-106 compute
+// 1 - 2 / (1 + exp(-2a)) = -tanh(a)); SILU is the reference's v / (1 + exp(-v))
+// (activations.cl:48-56), written as 0.5 v (1 + tanh(v / 2)) since sigmoid(x) = (1 + tanh(x/2)) / 2.
 __device__ __forceinline__ float activate(int act, float v) {
-    if (act == MGPU_ACT_SILU) return __fdividef(v, 1.0f + __expf(-v));
+    if (act == MGPU_ACT_SILU) {
+        const float hv = 0.5f * v;
+        return fmaf(hv, tanh_fast(hv), hv);
+    }
     if (act == MGPU_ACT_GELU || act == MGPU_ACT_GELU_AS_SHIPPED) {
-        const float inner = 0.7978845608f * fmaf(0.044715f, v * v * v, v);
-        float t = 1.0f - __fdividef(2.0f, __expf(2.0f * inner) + 1.0f);
+        const float inner = 0.7978845608f * fmaf(0.044715f * v, v * v, v);
+        float t = tanh_fast(inner);
         if (act == MGPU_ACT_GELU_AS_SHIPPED) t = -t;
-        return 0.5f * v * (1.0f + t);
+        const float hv = 0.5f * v;
+        return fmaf(hv, t, hv);
     }
     return v;
 }
