@@ -208,10 +208,6 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     step_bytes = sum(gemv_bytes(K, N) for _, K, N in LAYER_SHAPES) * LAYERS + gemv_bytes(K_h, HEAD[2])
     launches_per_step = LAYERS * len(LAYER_SHAPES) + 1
-    if args.batched_only:
-        # profiling aid: only the batched-decode section, one GPU
-        return {"batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head,
-                                                     seqs=tuple(args.batched_only))}
 
     # ---------------- capture one step ----------------
     def enqueue_step():
@@ -776,9 +772,6 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the fp32 GEMV, batched-decode and SigLIP sections")
-    ap.add_argument("--batched-only", type=int, nargs="+", metavar="S",
-                    help="profiling aid: run only the batched-decode section for these sequence counts "
-                         "(one GPU) and print its result")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

@@ -263,31 +263,27 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 
 // ------------------------------------------------------------------ fused epilogue --
 
-// One MUFU tanh (PTX tanh.approx.f32: relative error about 2^-11, saturates to +-1).
-__device__ __forceinline__ float tanh_fast(float x) {
-    float y;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-// act(v) in fp32, each with one tanh so the epilogue's instruction count stays low.  GELU is the
-// tanh approximation 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))); GELU_AS_SHIPPED reverses
-// tanh's sign as the reference's gelu kernel does (activations.cl:94-106 compute
-// 1 - 2 / (1 + exp(-2a)) = -tanh(a)); SILU is the reference's v / (1 + exp(-v))
-// (activations.cl:48-56), written as 0.5 v (1 + tanh(v / 2)) since sigmoid(x) = (1 + tanh(x/2)) / 2.
+// act(v) in fp32, every form written as v * sigmoid(z) = v / (1 + exp(-z)):
+//   SILU             z = v: the reference's v / (1 + exp(-v)) (activations.cl:48-56);
+//   GELU             z = 2 inner, inner = sqrt(2/pi) (v + 0.044715 v^3): the tanh approximation
+//                    0.5 v (1 + tanh(inner)) = v sigmoid(2 inner);
+//   GELU_AS_SHIPPED  z = -2 inner: the reference's gelu kernel reverses tanh's sign
+//                    (activations.cl:94-106 compute 1 - 2 / (1 + exp(-2a)) = -tanh(a)), so it
+//                    outputs 0.5 v (1 - tanh(inner)) = v sigmoid(-2 inner).
+// No form subtracts two nearly equal numbers (a 1 + tanh(.) form cancels where tanh is near -1,
+// which turns tanh's absolute error into the whole result in the tails), so the relative error
+// stays a few fp32 ulps for every finite v.  1 + exp(-z) = inf (z < -88) gives v * 0 = -0 or 0.
 __device__ __forceinline__ float activate(int act, float v) {
+    float z;
     if (act == MGPU_ACT_SILU) {
-        const float hv = 0.5f * v;
-        return fmaf(hv, tanh_fast(hv), hv);
-    }
-    if (act == MGPU_ACT_GELU || act == MGPU_ACT_GELU_AS_SHIPPED) {
+        z = v;
+    } else if (act == MGPU_ACT_GELU || act == MGPU_ACT_GELU_AS_SHIPPED) {
         const float inner = 0.7978845608f * fmaf(0.044715f * v, v * v, v);
-        float t = tanh_fast(inner);
-        if (act == MGPU_ACT_GELU_AS_SHIPPED) t = -t;
-        const float hv = 0.5f * v;
-        return fmaf(hv, t, hv);
+        z = act == MGPU_ACT_GELU ? 2.0f * inner : -2.0f * inner;
+    } else {
+        return v;
     }
-    return v;
+    return __fdividef(v, 1.0f + __expf(-z));
 }
 
 __device__ __forceinline__ float load_float(const void* p, int type, size_t i) {

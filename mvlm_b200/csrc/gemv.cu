@@ -1269,7 +1269,11 @@ cudaError_t gemv_kn_noalloc(const LaunchCtx& c, int wtype, const void* W, int64_
                             int ytype, void* y, int N, int K) {
     if (N <= 0 || (size_t)N > kNoAllocPartials || (N + kKnCols - 1) / kKnCols > kNoAllocTickets)
         return cudaErrorInvalidValue;
-    // The array's device address, looked up once per device with that device current.
+    // The array's device address, looked up once per device with that device current.  The
+    // lookup also clears the tickets once (stream-ordered before this call's kernel); after
+    // that every call leaves them zero, because the last CTA of each column tile resets its
+    // ticket before it exits.  The cache would hold a stale address after cudaDeviceReset,
+    // which unloads this library's device code: do not call this entry point after one.
     static void* addr[64] = {};
     static std::mutex mu;
     int ordinal = 0;
@@ -1280,11 +1284,12 @@ cudaError_t gemv_kn_noalloc(const LaunchCtx& c, int wtype, const void* W, int64_
     {
         std::lock_guard<std::mutex> lock(mu);
         if (!addr[ordinal]) {
-            e = cudaGetSymbolAddress(&addr[ordinal], g_noalloc_scratch);
-            if (e != cudaSuccess) {
-                addr[ordinal] = nullptr;
-                return e;
-            }
+            void* a = nullptr;
+            e = cudaGetSymbolAddress(&a, g_noalloc_scratch);
+            if (e != cudaSuccess) return e;
+            e = cudaMemsetAsync(a, 0, kNoAllocTickets * sizeof(unsigned int), c.stream);
+            if (e != cudaSuccess) return e;
+            addr[ordinal] = a;
         }
         base = addr[ordinal];
     }
@@ -1295,10 +1300,6 @@ cudaError_t gemv_kn_noalloc(const LaunchCtx& c, int wtype, const void* W, int64_
     gemv_kn_scratch_bytes(N, K, c.sm_count, &splits);
     splits = max(1, min(splits, (int)(kNoAllocPartials / (size_t)N)));
     const int col_tiles = (N + kKnCols - 1) / kKnCols;
-    // The tickets must start at zero; a previous call leaves them zero, but an aborted one
-    // might not, so clear them (an async memset: no allocation).
-    e = cudaMemsetAsync(tickets, 0, (size_t)col_tiles * sizeof(unsigned int), c.stream);
-    if (e != cudaSuccess) return e;
     const int kchunk = (K + splits - 1) / splits;
     dim3 grid(col_tiles, splits);
 #define MGPU_NA_LAUNCH(WT, XT, YT) \

@@ -11,7 +11,7 @@ import pytest
 
 import mvlm_b200 as mg
 import oracle as O
-from tests.numerics import TOL_16, assert_close
+from tests.numerics import TOL_16, TOL_F32, assert_close
 
 pytestmark = pytest.mark.gpu
 
@@ -51,6 +51,9 @@ def _run(dev, a, b, M, N, K, ct, bias, act, resid, in_place):
 ])
 @pytest.mark.parametrize("act", ACTS, ids=["gelu", "silu", "gelu_as_shipped"])
 def test_fused_quantised(dev, qt, M, N, K, path, act):
+    # The GEMM's operands are bf16 (the packed weights are dequantised to bf16 tiles), so the
+    # product meets the 16-bit tensor-core tolerance against the oracle's exact fp32 dequant
+    # whatever C's type; the epilogue's own element-wise accuracy is checked separately below.
     a, b, acc = _quant_case(qt, M, N, K, 1000 + M + N + act)
     bias = O.normal(N, 77 + N, 0.5)
     for ct in (mg.BF16, mg.F32):
@@ -58,6 +61,42 @@ def test_fused_quantised(dev, qt, M, N, K, path, act):
         ref = O.unfused_epilogue(acc, bias, act, resid, M, N, ct)
         out = _run(dev, a, b, M, N, K, ct, bias, act, resid, in_place=False)
         assert_close(out, ref, TOL_16, f"{path} q{qt} {M}x{N}x{K} act{act} c{ct}")
+
+
+def _act_truth(v, act):
+    """act on fp32 pre-activations, in float64 through the sigmoid identities
+    0.5 v (1 + tanh(u)) = v / (1 + exp(-2u)) and 0.5 v (1 - tanh(u)) = v / (1 + exp(2u)), which
+    cancel nowhere (a 1 + tanh(u) evaluation loses all digits where tanh(u) is near -1)."""
+    v = np.asarray(v, np.float64)
+    inner = np.float64(np.float32(0.7978845608)) * (v + np.float64(np.float32(0.044715)) * v ** 3)
+    z = {mg.ACT_SILU: v, mg.ACT_GELU: 2.0 * inner, mg.ACT_GELU_AS_SHIPPED: -2.0 * inner}[act]
+    with np.errstate(over="ignore"):
+        return v / (1.0 + np.exp(-z))
+
+
+@pytest.mark.parametrize("qt,M,path", [(O.Q8_0, 761, "cluster split-K"), (O.Q8_0, 2048, "tiles / CTA pairs"),
+                                       (O.Q8_0, 8, "split-K over global partials"), (O.Q4_0, 8, "skinny")])
+@pytest.mark.parametrize("act", ACTS, ids=["gelu", "silu", "gelu_as_shipped"])
+def test_fused_activation_elementwise(dev, qt, M, path, act):
+    # A = 0 makes the accumulator exactly 0, so C = act(bias) with the bias spanning the
+    # pre-activations [-12, 12]: each output is checked on its own against the float64 value,
+    # tails included (silu(-10) = -4.5e-4 must come out with its sign and ~fp32 precision).
+    N, K = 2048, 2048
+    A = np.zeros(M * K, np.uint16)
+    W = O.quantize(O.normal(N * K, 5, 0.02), qt)
+    bias = np.linspace(-12.0, 12.0, N).astype(np.float32)
+    truth = _act_truth(bias, act)
+    dA, dW, db = dev.array(A, mg.BF16), dev.array(W, qt, mg.LAYOUT_NK), dev.array(bias, mg.F32)
+    for ct, rtol in ((mg.F32, TOL_F32), (mg.BF16, 2.0 ** -8 + TOL_F32)):
+        dC = dev.empty(M * N, ct)
+        mg.gemm_fused(dev, dA, dW, dC, M, N, K, db, act, None).wait()
+        out = BACK[ct](dC.read(mg.NP_DTYPE[ct])).reshape(M, N).astype(np.float64)
+        err = np.abs(out - truth[None, :])
+        bad = err > rtol * np.abs(truth)[None, :] + 1e-30
+        assert not bad.any(), (f"{path} act{act} c{ct}: {int(bad.sum())} outputs off, worst at pre-activation "
+                               f"{bias[np.argwhere(bad)[0][1]]}: {out[bad][0]} vs {truth[np.argwhere(bad)[0][1]]}")
+        neg = truth < -1e-30
+        assert np.all(np.signbit(out[:, neg])), f"{path} act{act} c{ct}: sign lost for negative outputs"
 
 
 @pytest.mark.parametrize("qt,M,N,K", [(O.Q8_0, 761, 2048, 2048), (O.Q4_0, 8, 2048, 2048), (O.Q8_0, 8, 2048, 2048)])

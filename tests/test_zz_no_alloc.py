@@ -25,6 +25,8 @@ def test_noalloc_matches_allocating_entry_fp32(dev, K, N):
     y_ref, y_new = dev.empty(N, mg.F32), dev.empty(N, mg.F32)
     mg.dispatch_gemv(dev, None, dx, dW, y_ref, N, K).wait()
     ref = y_ref.read(np.float32)
+    # the allocating entry itself against the oracle's restatement of the reference gemv
+    assert_close(ref, O.gemv_f32(x, W, N, K), TOL_F32, f"dispatch_gemv fp32 {K}x{N}")
     for _ in range(2):  # two calls in a row: the shared array must come back clean
         y_new.write(np.full(N, np.nan, np.float32))
         mg.dispatch_gemv_noalloc(dev, dx, dW, y_new, N, K)
@@ -45,6 +47,35 @@ def test_noalloc_matches_allocating_entry_fp16_image(dev):
         mg.dispatch_gemv_noalloc(dev, dx, img, y_new, N, K)
         dev.finish()
         assert_close(O.f16_to_f32(y_new.read(np.uint16)), ref, TOL_16, "noalloc fp16 image")
+
+
+def test_noalloc_largest_size_and_mixed_types(dev):
+    # N = 262144 is the largest size the array holds: the K split drops to one and the fp32
+    # partials fill the whole array.  Then bf16 x against f16 weights with an f16 y, which
+    # take other instantiations of the launcher's type switch.
+    K, N = 64, 262144
+    x = O.uniform(K, 11)
+    W = O.uniform(K * N, 12)
+    dx, dW = dev.array(x, mg.F32), dev.array(W, mg.F32, mg.LAYOUT_KN)
+    y_ref, y_new = dev.empty(N, mg.F32), dev.empty(N, mg.F32)
+    mg.dispatch_gemv(dev, None, dx, dW, y_ref, N, K).wait()
+    ref = y_ref.read(np.float32)
+    for _ in range(2):
+        y_new.write(np.full(N, np.nan, np.float32))
+        mg.dispatch_gemv_noalloc(dev, dx, dW, y_new, N, K)
+        dev.finish()
+        assert_close(y_new.read(np.float32), ref, TOL_F32, "noalloc fp32 at the size limit")
+    K, N = 1024, 3000
+    xb = O.bf16(O.uniform(K, 13))
+    Wh = O.f16(O.uniform(K * N, 14))
+    dx, dW = dev.array(xb, mg.BF16), dev.array(Wh, mg.F16, mg.LAYOUT_KN)
+    y_ref, y_new = dev.empty(N, mg.F16), dev.empty(N, mg.F16)
+    mg.dispatch_gemv(dev, None, dx, dW, y_ref, N, K).wait()
+    ref = O.f16_to_f32(y_ref.read(np.uint16))
+    for _ in range(2):
+        mg.dispatch_gemv_noalloc(dev, dx, dW, y_new, N, K)
+        dev.finish()
+        assert_close(O.f16_to_f32(y_new.read(np.uint16)), ref, TOL_16, "noalloc bf16 x, f16 W and y")
 
 
 def test_noalloc_rejects_sizes_beyond_its_array(dev):
