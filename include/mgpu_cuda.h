@@ -171,6 +171,37 @@ int mgpu_dispatch_gemv_noalloc(const mgpu_device* dev, mgpu_buf* x, mgpu_buf* W_
  * y[1,N] = x[1,K] * dequant(W)^T with W packed GGUF blocks [N][K/32] of `type`. */
 mgpu_event* mgpu_gemv_q(const mgpu_device* dev, mgpu_buf* x, mgpu_buf* W, mgpu_buf* y, int N, int K,
                         int type);
+/* New: the GEMVs of a decode step in one launch.  Replaces a run of dependent dispatch_gemv
+ * calls (src/models/moondream2.cpp:357-542 calls one per projection, waiting on each) when
+ * the weights are GGUF Q4_0 / Q8_0.  A link is one GEMV y[1,N] = x[1,K] * dequant(W)^T with the
+ * argument meaning of mgpu_gemv_q.  Its x is either a buffer that is ready when the chain
+ * runs, or the output of an earlier link: a view of that link's y (same type, K values inside
+ * its N), the chain's dataflow.  The chain gives the same results as running the links one
+ * after another with mgpu_gemv_q.  mgpu_gemv_chain_create checks the links once and keeps
+ * pointers to the buffers, which must outlive the chain: all links share one quant type;
+ * 1024 <= K <= 8192 with K a power of two and at most 192 links (MGPU_ERR_UNSUPPORTED
+ * otherwise: split the chain, or run those GEMVs with mgpu_gemv_q); every x aligned to 4
+ * elements; y ranges disjoint from each other, from every W and from every x that is not an
+ * earlier y; W not written while the chain runs.  It allocates a small stage table and a
+ * 64-byte counter per SM; mgpu_gemv_chain_run allocates nothing and can be captured in a
+ * graph.  Runs of one chain must not overlap on the GPU (one stream).  A run that hits a
+ * bounded-wait expiry reports MGPU_ERR_DEVICE_TIMEOUT and leaves the chain refusing to run:
+ * destroy and re-create it. */
+typedef struct mgpu_gemv_chain mgpu_gemv_chain;
+typedef struct mgpu_gemv_link {
+    mgpu_buf* x; /* [K] f32 / f16 / bf16, or a view of an earlier link's y */
+    mgpu_buf* W; /* GGUF Q4_0 / Q8_0 blocks [N][K/32] */
+    mgpu_buf* y; /* [N] f32 / f16 / bf16 */
+    int N;
+    int K;
+} mgpu_gemv_link;
+mgpu_gemv_chain* mgpu_gemv_chain_create(const mgpu_device* dev, const mgpu_gemv_link* links, int n_links);
+mgpu_event* mgpu_gemv_chain_run(mgpu_gemv_chain* chain);
+/* One run with per-link timing (synchronous): end_us[i] = microseconds from the run's start
+ * to the moment the last CTA finished link i (device %globaltimer, max over CTAs). */
+int mgpu_gemv_chain_run_timed(mgpu_gemv_chain* chain, double* end_us);
+int mgpu_gemv_chain_links(const mgpu_gemv_chain* chain);
+void mgpu_gemv_chain_destroy(mgpu_gemv_chain* chain);
 /* C[M,N] = A[M,K] * dequant(W)^T (+ bias[N] if non-NULL), W packed [N][K/32] blocks, A
  * fp16/bf16; the blocks are dequantised to A's type inside the GEMM's weight loads. */
 mgpu_event* mgpu_gemm_q(const mgpu_device* dev, mgpu_buf* A, mgpu_buf* W, mgpu_buf* C, int M, int N,

@@ -68,6 +68,11 @@ SIGNATURES = {
     "mgpu_dispatch_vision_proj": (_vp, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
     "mgpu_dispatch_gemv_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i]),
     "mgpu_gemv_q": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i]),
+    "mgpu_gemv_chain_create": (_vp, [_vp, _vp, _i]),
+    "mgpu_gemv_chain_run": (_vp, [_vp]),
+    "mgpu_gemv_chain_run_timed": (_i, [_vp, _vp]),
+    "mgpu_gemv_chain_links": (_i, [_vp]),
+    "mgpu_gemv_chain_destroy": (None, [_vp]),
     "mgpu_gemm_q": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "mgpu_gemm": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "mgpu_gemm_fused": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i, _vp]),
@@ -104,6 +109,12 @@ class TensorInfo(ctypes.Structure):
     """Binary-compatible with the reference's TensorInfo (src/models/gguf_loader.h:51-58)."""
     _fields_ = [("name", ctypes.c_char * 256), ("n_dims", ctypes.c_uint32), ("dims", ctypes.c_uint64 * 4),
                 ("type", ctypes.c_uint32), ("offset", ctypes.c_uint64), ("data_size", ctypes.c_size_t)]
+
+
+class GemvLink(ctypes.Structure):
+    """mgpu_gemv_link: one GEMV of a chain (x may be a view of an earlier link's y)."""
+    _fields_ = [("x", ctypes.c_void_p), ("W", ctypes.c_void_p), ("y", ctypes.c_void_p), ("N", ctypes.c_int),
+                ("K", ctypes.c_int)]
 
 
 _lib = None
@@ -388,6 +399,41 @@ def dispatch_gemv_noalloc(dev: Device, x: Buffer, W_img: Buffer, y: Buffer, N: i
 
 def gemv_q(dev: Device, x: Buffer, W: Buffer, y: Buffer, N: int, K: int, qtype: int) -> Event:
     return _ev(lib().mgpu_gemv_q(dev.h, x.h, W.h, y.h, N, K, qtype), "gemv_q")
+
+
+class GemvChain:
+    """mgpu_gemv_chain: a decode step's dependent GEMVs in one persistent launch.
+
+    links: (x, W, y, N, K) per GEMV in order; an x that is a view of an earlier link's y reads
+    that link's output (the chain's dataflow), any other x is read as it is when the chain runs.
+    The buffers must outlive the chain (this object keeps references to them)."""
+
+    def __init__(self, dev: Device, links):
+        self.dev = dev
+        self._keep = [(x, W, y) for x, W, y, _, _ in links]
+        arr = (GemvLink * len(links))(*[GemvLink(x.h, W.h, y.h, N, K) for x, W, y, N, K in links])
+        h = lib().mgpu_gemv_chain_create(dev.h, arr, len(links))
+        if not h:
+            _raise_last("gemv_chain_create")
+        self.h = h
+        self.n = len(links)
+
+    def run(self) -> Event:
+        return _ev(lib().mgpu_gemv_chain_run(self.h), "gemv_chain_run")
+
+    def run_timed(self) -> np.ndarray:
+        """One synchronous run; microseconds from the run's start to the end of each link."""
+        out = np.zeros(self.n, np.float64)
+        _check(lib().mgpu_gemv_chain_run_timed(self.h, out.ctypes.data), "gemv_chain_run_timed")
+        return out
+
+    def destroy(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.mgpu_gemv_chain_destroy(self.h)
+        self.h = None
+
+    def __del__(self):
+        self.destroy()
 
 
 def gemm_q(dev: Device, A: Buffer, W: Buffer, C: Buffer, M: int, N: int, K: int, qtype: int,

@@ -27,6 +27,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "qdot.cuh"
 
 using namespace mgpu_dev;
 
@@ -40,229 +41,6 @@ constexpr uint32_t kGemvSmemBudget = 100 * 1024;  // per CTA: two CTAs share an 
 // The MMA kernel's budget: two such CTAs plus their 1 KB reservations stay within an SM's
 // 228 KB, and a 16-row chunk of K = 8192 Q4_0 rows (74 KB) fits beside its activations.
 constexpr uint32_t kGemvMmaSmemBudget = 110 * 1024;
-
-template <int QT> struct QTraits;
-template <> struct QTraits<MGPU_Q4_0> {
-    static constexpr int kBlockBytes = 18;
-    static constexpr int kWords = 5;  // 20 aligned bytes cover an 18-byte block at offset 0 or 2
-};
-template <> struct QTraits<MGPU_Q8_0> {
-    static constexpr int kBlockBytes = 34;
-    static constexpr int kWords = 9;
-};
-
-// ---- integer inner product ---------------------------------------------------------
-// Each consumer thread owns one 32-element block column for the whole launch.  Its 32
-// activations are converted once to 23-bit fixed point relative to their own max
-// (x_i = X_i * 2^(e-22), |X_i| <= 2^22) and split into three byte planes
-// X = b2 * 2^16 + b1 * 2^8 + b0 (b0, b1 unsigned, b2 signed), packed four elements per
-// word in the order the quant bytes arrive.  A block's sum_k X_k q_k is then exact integer
-// arithmetic: one dp4a per four weights and byte plane, straight on the packed nibbles
-// (Q4_0: q & 0x0F0F0F0F, and (q & 0xF0F0F0F0) = 16 * the high nibbles) or int8 (Q8_0).
-__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
-    int d;
-    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
-    int d;
-    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
-    int d;
-    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
-    int d;
-    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-
-// The thread's activations in fixed point.  p[plane][w]: plane 0..2 = b0, b1, b2;
-// w = 0..7 = elements 4w..4w+3.  scale = 2^(e-22); xsum = sum_k X_k.
-struct XFixed {
-    uint32_t p[3][8];
-    float scale;
-    float xsum;
-};
-
-// The CTA converts all K activations once, cooperatively: thread t takes 4 consecutive
-// elements at a time, the 8 threads of a 32-element block agree on the block's exponent
-// with shuffles, and the packed byte planes go to shared memory:
-//   planes[p * (K/4) + w]  (w = word index = element / 4), bscale[b], bsum[b] per block b.
-// Consumer threads then read their own block's 24 words.  Costs one round trip to L2 plus a
-// handful of instructions per thread, instead of 32 loads and conversions per thread.
-// words = K / 4 is a multiple of 256 (K % 1024 == 0) and at most 2048 (K <= 8192), so each
-// thread converts ITERS = K / 1024 words; the count is a compile-time constant so that all
-// loads are issued before any is used and the activation vector costs one round trip.
-// (K of 3, 5, 6 or 7 x 1024 takes the runtime-bounded form: ITERS = 8, EXACT = false.)
-template <typename XT, int ITERS, bool EXACT>
-__device__ __forceinline__ void prepare_x_n(const XT* __restrict__ x, int K, uint32_t* planes, float* bscale,
-                                            float* bsum, int tid, int nthreads) {
-    constexpr int kMaxIter = ITERS;
-    const int words = K / 4;
-    const int iters = EXACT ? ITERS : words / nthreads;
-    float v[kMaxIter][4];
-#pragma unroll
-    for (int it = 0; it < kMaxIter; ++it) {
-        if (it < iters) {
-            const int w = it * nthreads + tid;
-            if constexpr (sizeof(XT) == 4) {
-                const float4 f = __ldg(reinterpret_cast<const float4*>(x) + w);
-                v[it][0] = f.x; v[it][1] = f.y; v[it][2] = f.z; v[it][3] = f.w;
-            } else {
-                const uint2 u = __ldg(reinterpret_cast<const uint2*>(x) + w);
-                const uint32_t uu[2] = {u.x, u.y};
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    XT lo, hi;
-                    uint16_t l16 = (uint16_t)(uu[j] & 0xFFFF), h16 = (uint16_t)(uu[j] >> 16);
-                    memcpy(&lo, &l16, 2);
-                    memcpy(&hi, &h16, 2);
-                    v[it][2 * j] = to_f32<XT>(lo);
-                    v[it][2 * j + 1] = to_f32<XT>(hi);
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int it = 0; it < kMaxIter; ++it) {
-        if (it < iters) {
-            const int w = it * nthreads + tid;
-            float amax = fmaxf(fmaxf(fabsf(v[it][0]), fabsf(v[it][1])), fmaxf(fabsf(v[it][2]), fabsf(v[it][3])));
-#pragma unroll
-            for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-            int e = 0;
-            frexpf(amax, &e);  // the block's |x| < 2^e
-            const float up = __int_as_float((127 + 22 - e) << 23);  // 2^(22-e); |e| < 100 for finite x
-            // X = round-to-nearest-even(v * 2^(22-e)), |X| <= 2^22: one fma against 1.5 * 2^23
-            // puts X + 2^23 + 2^22 in [2^23, 2^24] with a unit step, so its bits minus those of
-            // 1.5 * 2^23 are X (v * up is exact, so this equals __float2int_rn(v * up)).  The
-            // byte planes of the four elements are gathered with byte permutes.
-            uint32_t X[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) X[j] = (uint32_t)(__float_as_int(fmaf(v[it][j], up, 12582912.0f)) - 0x4B400000);
-            int sum = (int)(X[0] + X[1] + X[2] + X[3]);
-            const uint32_t t01 = prmt(X[0], X[1], 0x5140u), t23 = prmt(X[2], X[3], 0x5140u);
-            const uint32_t u01 = prmt(X[0], X[1], 0x0062u), u23 = prmt(X[2], X[3], 0x0062u);
-            const uint32_t b0 = prmt(t01, t23, 0x5410u);  // byte 0 of X[0..3]
-            const uint32_t b1 = prmt(t01, t23, 0x7632u);  // byte 1
-            const uint32_t b2 = prmt(u01, u23, 0x5410u);  // byte 2
-#pragma unroll
-            for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-            planes[w] = b0;
-            planes[words + w] = b1;
-            planes[2 * words + w] = b2;
-            if ((tid & 7) == 0) {
-                bscale[w >> 3] = __int_as_float((127 + e - 22) << 23);  // 2^(e-22)
-                bsum[w >> 3] = (float)sum;
-            }
-        }
-    }
-}
-
-template <typename XT>
-__device__ __forceinline__ void prepare_x(const XT* __restrict__ x, int K, uint32_t* planes, float* bscale,
-                                          float* bsum, int tid, int nthreads) {
-    switch (K >> 10) {
-        case 1: prepare_x_n<XT, 1, true>(x, K, planes, bscale, bsum, tid, nthreads); break;
-        case 2: prepare_x_n<XT, 2, true>(x, K, planes, bscale, bsum, tid, nthreads); break;
-        case 4: prepare_x_n<XT, 4, true>(x, K, planes, bscale, bsum, tid, nthreads); break;
-        case 8: prepare_x_n<XT, 8, true>(x, K, planes, bscale, bsum, tid, nthreads); break;
-        default: prepare_x_n<XT, 8, false>(x, K, planes, bscale, bsum, tid, nthreads); break;
-    }
-}
-
-__device__ __forceinline__ void load_xfixed(const uint32_t* planes, const float* bscale, const float* bsum,
-                                            int words, int col, XFixed& xf) {
-#pragma unroll
-    for (int p = 0; p < 3; ++p) {
-        const uint4* src = reinterpret_cast<const uint4*>(planes + p * words + col * 8);
-        const uint4 a = src[0], b = src[1];
-        xf.p[p][0] = a.x; xf.p[p][1] = a.y; xf.p[p][2] = a.z; xf.p[p][3] = a.w;
-        xf.p[p][4] = b.x; xf.p[p][5] = b.y; xf.p[p][6] = b.z; xf.p[p][7] = b.w;
-    }
-    xf.scale = bscale[col];
-    xf.xsum = bsum[col];
-}
-
-// One Q4_0 block against the thread's activations.  w = the 20 aligned bytes containing the
-// block; `sel` realigns the 16 quant bytes, `dsel` extracts the fp16 scale.  Element j < 16
-// is the low nibble of qs[j], element j + 16 the high nibble.
-// Returns d * sum_k x_k (q_k - 8).
-__device__ __forceinline__ float q4_0_block_dot(const uint32_t (&w)[5], uint32_t sel, uint32_t dsel,
-                                                const XFixed& xf) {
-    const float d = __half2float(__ushort_as_half((unsigned short)prmt(w[0], 0u, dsel)));
-    int lo0 = 0, lo1 = 0, lo2 = 0, hi0 = 0, hi1 = 0, hi2 = 0;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        const uint32_t q = prmt(w[m], w[m + 1], sel);
-        const uint32_t lo = q & 0x0F0F0F0Fu;  // elements 4m..4m+3
-        const uint32_t hi = q & 0xF0F0F0F0u;  // 16 x elements 16+4m..16+4m+3
-        lo0 = dp4a_uu(lo, xf.p[0][m], lo0);
-        lo1 = dp4a_uu(lo, xf.p[1][m], lo1);
-        lo2 = dp4a_us(lo, xf.p[2][m], lo2);
-        hi0 = dp4a_uu(hi, xf.p[0][4 + m], hi0);
-        hi1 = dp4a_uu(hi, xf.p[1][4 + m], hi1);
-        hi2 = dp4a_us(hi, xf.p[2][4 + m], hi2);
-    }
-    // 16 * sum X q per plane (exact int32), combined in fp32
-    const int t0 = lo0 * 16 + hi0, t1 = lo1 * 16 + hi1, t2 = lo2 * 16 + hi2;
-    const float s16 = fmaf((float)t2, 65536.0f, fmaf((float)t1, 256.0f, (float)t0));
-    // sum X (q - 8) = (s16 - 128 * xsum) / 16
-    return d * (xf.scale * 0.0625f) * fmaf(-128.0f, xf.xsum, s16);
-}
-
-// One Q8_0 block: 32 signed bytes, w = q * d.
-__device__ __forceinline__ float q8_0_block_dot(const uint32_t (&w)[9], uint32_t sel, uint32_t dsel,
-                                                const XFixed& xf) {
-    const float d = __half2float(__ushort_as_half((unsigned short)prmt(w[0], 0u, dsel)));
-    int a0 = 0, a1 = 0, a2 = 0;
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-        const uint32_t q = prmt(w[m], w[m + 1], sel);  // elements 4m..4m+3
-        a0 = dp4a_su(q, xf.p[0][m], a0);
-        a1 = dp4a_su(q, xf.p[1][m], a1);
-        a2 = dp4a_ss(q, xf.p[2][m], a2);
-    }
-    const float s = fmaf((float)a2, 65536.0f, fmaf((float)a1, 256.0f, (float)a0));
-    return d * xf.scale * s;
-}
-
-template <int QT, int NW>
-__device__ __forceinline__ float q_block_dot(const uint32_t (&w)[NW], uint32_t sel, uint32_t dsel,
-                                             const XFixed& xf) {
-    if constexpr (QT == MGPU_Q4_0) return q4_0_block_dot(w, sel, dsel, xf);
-    else return q8_0_block_dot(w, sel, dsel, xf);
-}
-
-// Transposing butterfly: v[0..R) per lane in, the 32-lane sum of row `row` out, where lanes
-// with lane % (32 / R) == 0 hold distinct rows.
-template <int R>
-__device__ __forceinline__ float warp_reduce_rows(float (&v)[R], int lane, int& row) {
-    constexpr int LOG = (R == 1) ? 0 : (R == 2) ? 1 : (R == 4) ? 2 : 3;
-    row = 0;
-#pragma unroll
-    for (int step = 0; step < LOG; ++step) {
-        const int h = R >> (step + 1);
-        const int off = 16 >> step;
-        const bool up = (lane & off) != 0;
-#pragma unroll
-        for (int k = 0; k < (R >> 1); ++k) {
-            if (k < h) {
-                const float send = up ? v[k] : v[k + h];
-                const float keep = up ? v[k + h] : v[k];
-                v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-            }
-        }
-        if (up) row += h;
-    }
-#pragma unroll
-    for (int off = 16 >> LOG; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
-    return v[0];
-}
 
 struct GemvQArgs {
     const uint8_t* W;

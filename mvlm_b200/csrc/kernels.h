@@ -45,6 +45,35 @@ cudaError_t gemv_kn_noalloc(const LaunchCtx& c, int wtype, const void* W, int64_
                             int ytype, void* y, int N, int K);
 size_t gemv_kn_noalloc_max_n();
 
+// ------------------------------------------------------- GEMV chain (chain.cu) ------
+// One GEMV of a chain, as the kernel reads it from device memory (64 bytes).
+struct ChainStage {
+    const uint8_t* W;    // GGUF Q4_0 / Q8_0 rows [N][row_bytes]
+    const void* x;       // input [K] of xtype: an external vector, or a view of stage dep's y
+    void* y;             // output [N] of ytype
+    int N, K;
+    uint32_t row_bytes;
+    int xtype, ytype;
+    int dep;             // the stage whose output x is (-1: x is ready when the chain starts)
+    int dep_off;         // x's first element within that output
+    int dep_n;           // that stage's N (its rows are split over the CTAs like every stage's)
+    int post;            // 1: a later stage reads this one's output (the CTAs post their flags)
+    int pad;
+};
+// K the chain kernel takes: 1024 .. 8192, K / 32 dividing its 512 consumer threads.
+bool chain_shape_ok(int K);
+// Links one chain may hold (its stage table is copied to shared memory).
+int chain_max_links();
+// Bytes of the per-CTA flags a chain owns (zeroed once; the kernel only counts them up).
+size_t chain_flag_bytes(int sm_count);
+// One cooperative launch (one CTA per SM) over the n stages (all of qtype) at `stages` (device
+// memory).  sync: 4 zeroed words owned by the chain (launch counter (u64), finish ticket,
+// poison); flags: chain_flag_bytes zeroed bytes owned by the chain.  times: null, or n + 1
+// words: per-stage end time (max over CTAs, %globaltimer ns; start at 0) and the launch's start
+// (min over CTAs; start at ~0).
+cudaError_t gemv_chain(const LaunchCtx& c, int qtype, const ChainStage* stages, int n, unsigned int* sync,
+                       unsigned long long* flags, unsigned long long* times);
+
 // ---------------------------------------------------------------- misc (misc.cu) ----
 cudaError_t dequant(const LaunchCtx& c, int qtype, const uint8_t* W, int otype, void* out, int64_t n);
 cudaError_t quantize(const LaunchCtx& c, int qtype, const float* src, uint8_t* dst, int64_t n);

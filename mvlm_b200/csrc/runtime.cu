@@ -718,6 +718,211 @@ mgpu_event* mgpu_gemv_q(const mgpu_device* d, mgpu_buf* x, mgpu_buf* W, mgpu_buf
     return mgpu_dispatch_gemv(d, nullptr, x, W, y, N, K);
 }
 
+// ------------------------------------------------------------------ GEMV chain -------
+struct mgpu_gemv_chain {
+    mgpu_device* dev;
+    int n;
+    int qtype;
+    mgpu_k::ChainStage* d_stages;   // the stage table the kernel reads
+    unsigned int* d_sync;           // launch counter (u64), finish ticket, poison
+    unsigned long long* d_flags;    // per-CTA counts of finished links
+    unsigned long long* d_times;    // n + 1 words for timed runs (allocated on first use)
+};
+
+namespace {
+
+struct Range {
+    const char* lo;
+    const char* hi;
+    bool overlaps(const Range& o) const { return lo < o.hi && o.lo < hi; }
+    bool contains(const Range& o) const { return lo <= o.lo && o.hi <= hi; }
+};
+
+Range range_of(const mgpu_buf* b, size_t bytes) {
+    const char* p = static_cast<const char*>(b->ptr);
+    return Range{p, p + bytes};
+}
+
+void free_chain(mgpu_gemv_chain* c) {
+    if (!c) return;
+    if (c->d_stages) cudaFree(c->d_stages);
+    if (c->d_sync) cudaFree(c->d_sync);
+    if (c->d_flags) cudaFree(c->d_flags);
+    if (c->d_times) cudaFree(c->d_times);
+    delete c;
+}
+
+}  // namespace
+
+mgpu_gemv_chain* mgpu_gemv_chain_create(const mgpu_device* cd, const mgpu_gemv_link* links, int n) {
+    API_ENTRY();
+    REQUIRE(cd && links && n > 0, "gemv_chain_create: null device / links or n_links=%d", n);
+    mgpu_device* d = const_cast<mgpu_device*>(cd);
+    if (n > mgpu_k::chain_max_links()) {
+        set_error(MGPU_ERR_UNSUPPORTED, "gemv_chain_create: %d links; a chain holds at most %d (split it)", n,
+                  mgpu_k::chain_max_links());
+        return nullptr;
+    }
+    const int qtype = links[0].W ? links[0].W->type : -1;
+    REQUIRE(is_quant_type(qtype), "gemv_chain_create: link 0: W must be GGUF Q4_0 or Q8_0");
+    std::vector<Range> yr(n), wr(n), xr(n);
+    std::vector<int> src(n, -1);
+    std::vector<size_t> src_off(n, 0);
+    for (int i = 0; i < n; ++i) {
+        const mgpu_gemv_link& L = links[i];
+        REQUIRE(L.x && L.W && L.y, "gemv_chain_create: link %d: null buffer", i);
+        REQUIRE(L.N > 0 && L.K > 0, "gemv_chain_create: link %d: N=%d K=%d", i, L.N, L.K);
+        REQUIRE(L.W->type == qtype, "gemv_chain_create: link %d: W type %d differs from link 0's %d", i, L.W->type,
+                qtype);
+        REQUIRE(L.W->layout == MGPU_LAYOUT_NK, "gemv_chain_create: link %d: W must be GGUF [N][K/32]", i);
+        const size_t rb = quant_row_bytes(qtype, L.K);
+        REQUIRE(L.K % 32 == 0 && ld_or(L.W, (int64_t)rb) == (int64_t)rb,
+                "gemv_chain_create: link %d: W rows must be dense GGUF blocks", i);
+        REQUIRE(L.W->bytes >= (size_t)L.N * rb, "gemv_chain_create: link %d: W holds fewer than N=%d rows", i, L.N);
+        REQUIRE(((uintptr_t)L.W->ptr & 15) == 0, "gemv_chain_create: link %d: W must be 16-byte aligned", i);
+        REQUIRE(is_float_type(L.x->type) && is_float_type(L.y->type),
+                "gemv_chain_create: link %d: x and y must be f32 / f16 / bf16", i);
+        REQUIRE(L.x->bytes >= (size_t)L.K * elem_size(L.x->type), "gemv_chain_create: link %d: x holds fewer than K=%d",
+                i, L.K);
+        REQUIRE(L.y->bytes >= (size_t)L.N * elem_size(L.y->type), "gemv_chain_create: link %d: y holds fewer than N=%d",
+                i, L.N);
+        if (!mgpu_k::chain_shape_ok(L.K)) {
+            set_error(MGPU_ERR_UNSUPPORTED, "gemv_chain_create: link %d: K=%d (the chain takes 1024 <= K <= 8192, "
+                      "K %% 1024 == 0); run it with mgpu_gemv_q", i, L.K);
+            return nullptr;
+        }
+        wr[i] = range_of(L.W, (size_t)L.N * rb);
+        yr[i] = range_of(L.y, (size_t)L.N * elem_size(L.y->type));
+        xr[i] = range_of(L.x, (size_t)L.K * elem_size(L.x->type));
+        // x: the output of the latest earlier link whose y it touches, or an external vector
+        for (int j = i - 1; j >= 0; --j) {
+            if (!yr[j].overlaps(xr[i])) continue;
+            REQUIRE(yr[j].contains(xr[i]) && links[j].y->type == L.x->type,
+                    "gemv_chain_create: link %d: x overlaps link %d's y without being a view of it of the same type",
+                    i, j);
+            const size_t off = (size_t)(xr[i].lo - yr[j].lo);
+            const size_t es = elem_size(L.x->type);
+            REQUIRE(off % es == 0, "gemv_chain_create: link %d: x starts inside an element of link %d's y", i, j);
+            src[i] = j;
+            src_off[i] = off / es;
+            break;
+        }
+        // x is read four elements at a time
+        REQUIRE(((uintptr_t)L.x->ptr % (4 * elem_size(L.x->type))) == 0,
+                "gemv_chain_create: link %d: x must be aligned to 4 elements", i);
+    }
+    // hazards the chain's overlapped execution would expose: outputs must not overlap each other,
+    // any weights or any external input
+    for (int i = 0; i < n; ++i) {
+        for (int j = 0; j < n; ++j) {
+            REQUIRE(!yr[i].overlaps(wr[j]), "gemv_chain_create: link %d's y overlaps link %d's W", i, j);
+            if (j != i) REQUIRE(!yr[i].overlaps(yr[j]), "gemv_chain_create: links %d and %d write overlapping y", i, j);
+            if (src[j] < 0)
+                REQUIRE(!yr[i].overlaps(xr[j]), "gemv_chain_create: link %d's y overlaps link %d's input x", i, j);
+        }
+    }
+    std::vector<int> post(n, 0);
+    for (int i = 0; i < n; ++i)
+        if (src[i] >= 0) post[src[i]] = 1;
+    DeviceGuard g(d->ordinal);
+    mgpu_gemv_chain* c = new mgpu_gemv_chain();
+    c->dev = d;
+    c->n = n;
+    c->qtype = qtype;
+    auto fail = [&](cudaError_t e, const char* what) -> mgpu_gemv_chain* {
+        cuda_ok(e, what);
+        free_chain(c);
+        return nullptr;
+    };
+    cudaError_t e = cudaMalloc(&c->d_stages, sizeof(mgpu_k::ChainStage) * n);
+    if (e != cudaSuccess) return fail(e, "gemv_chain_create: cudaMalloc(stage table)");
+    e = cudaMalloc(&c->d_sync, 64);
+    if (e != cudaSuccess) return fail(e, "gemv_chain_create: cudaMalloc(sync)");
+    const size_t flag_bytes = mgpu_k::chain_flag_bytes(d->sm_count);
+    e = cudaMalloc(&c->d_flags, flag_bytes);
+    if (e != cudaSuccess) return fail(e, "gemv_chain_create: cudaMalloc(flags)");
+    std::vector<mgpu_k::ChainStage> st(n);
+    for (int i = 0; i < n; ++i) {
+        const mgpu_gemv_link& L = links[i];
+        mgpu_k::ChainStage& s = st[i];
+        memset(&s, 0, sizeof(s));
+        s.W = static_cast<const uint8_t*>(L.W->ptr);
+        s.x = L.x->ptr;
+        s.y = L.y->ptr;
+        s.N = L.N;
+        s.K = L.K;
+        s.row_bytes = (uint32_t)quant_row_bytes(qtype, L.K);
+        s.xtype = L.x->type;
+        s.ytype = L.y->type;
+        s.dep = src[i];
+        s.dep_off = src[i] >= 0 ? (int)src_off[i] : 0;
+        s.dep_n = src[i] >= 0 ? links[src[i]].N : 0;
+        s.post = post[i];
+    }
+    e = cudaMemcpyAsync(c->d_stages, st.data(), sizeof(mgpu_k::ChainStage) * n, cudaMemcpyHostToDevice, d->stream);
+    if (e != cudaSuccess) return fail(e, "gemv_chain_create: stage table upload");
+    e = cudaMemsetAsync(c->d_sync, 0, 64, d->stream);
+    if (e != cudaSuccess) return fail(e, "gemv_chain_create: clear sync words");
+    e = cudaMemsetAsync(c->d_flags, 0, flag_bytes, d->stream);
+    if (e != cudaSuccess) return fail(e, "gemv_chain_create: clear flags");
+    e = cudaStreamSynchronize(d->stream);
+    if (e != cudaSuccess) return fail(e, "gemv_chain_create: synchronize");
+    return c;
+}
+
+mgpu_event* mgpu_gemv_chain_run(mgpu_gemv_chain* c) {
+    API_ENTRY();
+    REQUIRE(c, "gemv_chain_run: null chain");
+    mgpu_device* d = c->dev;
+    DeviceGuard g(d->ordinal);
+    mgpu_event* ev = event_begin(d);
+    if (!cuda_ok(mgpu_k::gemv_chain(ctx_of(d), c->qtype, c->d_stages, c->n, c->d_sync, c->d_flags, nullptr), "gemv_chain_run")) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(d, ev);
+}
+
+int mgpu_gemv_chain_run_timed(mgpu_gemv_chain* c, double* end_us) {
+    t_err = MGPU_OK;
+    if (!c || !end_us) {
+        set_error(MGPU_ERR_INVALID_ARG, "gemv_chain_run_timed: null argument");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    mgpu_device* d = c->dev;
+    if (d->capturing) {
+        set_error(MGPU_ERR_INVALID_ARG, "gemv_chain_run_timed: synchronous, not capturable");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(d->ordinal);
+    const size_t words = (size_t)c->n + 1;
+    if (!c->d_times && !cuda_ok(cudaMalloc(&c->d_times, words * 8), "gemv_chain_run_timed: cudaMalloc"))
+        return t_err;
+    if (!cuda_ok(cudaMemsetAsync(c->d_times, 0, (size_t)c->n * 8, d->stream), "gemv_chain_run_timed: clear") ||
+        !cuda_ok(cudaMemsetAsync(c->d_times + c->n, 0xFF, 8, d->stream), "gemv_chain_run_timed: clear"))
+        return t_err;
+    if (!cuda_ok(mgpu_k::gemv_chain(ctx_of(d), c->qtype, c->d_stages, c->n, c->d_sync, c->d_flags, c->d_times),
+                 "gemv_chain_run_timed"))
+        return t_err;
+    std::vector<unsigned long long> t(words);
+    if (!cuda_ok(cudaMemcpyAsync(t.data(), c->d_times, words * 8, cudaMemcpyDeviceToHost, d->stream),
+                 "gemv_chain_run_timed: read times") ||
+        !cuda_ok(cudaStreamSynchronize(d->stream), "gemv_chain_run_timed: synchronize"))
+        return t_err;
+    if (!check_status(d)) return t_err;
+    for (int i = 0; i < c->n; ++i) end_us[i] = t[i] >= t[c->n] ? (double)(t[i] - t[c->n]) * 1e-3 : 0.0;
+    return MGPU_OK;
+}
+
+int mgpu_gemv_chain_links(const mgpu_gemv_chain* c) { return c ? c->n : 0; }
+
+void mgpu_gemv_chain_destroy(mgpu_gemv_chain* c) {
+    if (!c) return;
+    DeviceGuard g(c->dev->ordinal);
+    cudaStreamSynchronize(c->dev->stream);
+    free_chain(c);
+}
+
 mgpu_event* mgpu_dispatch_patch_embed(const mgpu_device* cd, mgpu_program, mgpu_buf* image, mgpu_buf* proj_weight,
                                       mgpu_buf* proj_bias, mgpu_buf* patches, int C, int H, int W, int ph, int pw,
                                       int embed_dim) {
