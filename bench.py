@@ -50,6 +50,9 @@ LAYER_SHAPES = [("qkv", 2048, 6144), ("out", 2048, 2048), ("fc1", 2048, 8192), (
 HEAD = ("lm_head", 2048, 51200)
 PREFILL_SHAPES = [(761, 2048, 6144), (761, 2048, 2048), (761, 2048, 8192), (761, 8192, 2048)]  # (M, K, N)
 SEED = 0x4D564C4D
+DECODE_WORKLOAD = ("Q4_0 decode step, M=1: 24 layers x (qkv 2048x6144, out 2048x2048, fc1 2048x8192, fc2 8192x2048) "
+                   "+ lm_head 2048x51200, each GEMV reading the previous one's output (BASELINE config 1 shapes over "
+                   "the model's 24 layers)")
 
 
 def measured_peaks() -> dict:
@@ -151,6 +154,111 @@ def cpu_baseline(budget_s: float = 12.0) -> dict:
 # --------------------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------------------
+def qbytes(qt: int, K: int, N: int) -> int:
+    """Algorithmic bytes of one quantised GEMV: packed weights + fp32 x + fp32 y."""
+    return N * (K // 32) * (18 if qt == 2 else 34) + 4 * K + 4 * N
+
+
+STEP_BYTES_Q4 = sum(qbytes(2, K, N) for _, K, N in LAYER_SHAPES) * LAYERS + qbytes(2, HEAD[1], HEAD[2])
+
+
+def make_q(dev, mg, tmp, qt, K, N, seed):
+    """Seeded ~N(0, 0.02) weights [N][K], quantised to qt on the device."""
+    w = dev.create_buffer(N * (K // 32) * (18 if qt == mg.Q4_0 else 34), None, qt, mg.LAYOUT_NK, N, K)
+    dev.fill_normal(tmp, N * K, seed, 0.02)
+    dev.quantize(tmp, w, N * K, qt)
+    return w
+
+
+def head_seed(r: int) -> int:
+    return SEED + 999_999 + r
+
+
+def build_decode_step(dev, mg, tmp, qt, n_head, head_rank):
+    """The decode step's GEMVs with the dataflow of a real decode token: the first link reads the
+    token's hidden state x0, every later link reads (the first K values of) the previous link's
+    output, and the lm_head (this rank's n_head rows) reads the last layer's output.
+    Returns (links [(name, x, W, y, N, K)], x0)."""
+    x0 = dev.empty(HEAD[1], mg.F32)
+    dev.fill_normal(x0, HEAD[1], SEED + 5, 1.0)
+    links, prev = [], None
+    for l in range(LAYERS):
+        for j, (name, K, N) in enumerate(LAYER_SHAPES):
+            W = make_q(dev, mg, tmp, qt, K, N, SEED + 1000 * l + j + (0 if qt == mg.Q4_0 else 7_000_000))
+            y = dev.empty(N, mg.F32)
+            x = x0 if prev is None else prev.view(0, K * 4).set_format(mg.F32)
+            links.append((name, x, W, y, N, K))
+            prev = y
+    Wh = make_q(dev, mg, tmp, qt, HEAD[1], n_head, head_seed(head_rank) + (0 if qt == mg.Q4_0 else 7_000_000))
+    yh = dev.empty(n_head, mg.F32)
+    links.append((HEAD[0], prev.view(0, HEAD[1] * 4).set_format(mg.F32), Wh, yh, n_head, HEAD[1]))
+    return links, x0
+
+
+def enqueue_links(dev, mg, qt, links):
+    for _, x, W, y, N, K in links:
+        mg.gemv_q(dev, x, W, y, N, K, qt)
+
+
+def run_per_shape(dev, mg, torch, stream, peaks, qt, tmp) -> dict:
+    """Each Phi-1.5 decode shape as its own chain of dependent GEMVs (every launch reads the
+    previous launch's output, through PDL like the step), with enough links that a replay
+    streams about 2x the L2 of packed weights; GB/s = links x algorithmic bytes / device time.
+    fc2's input (K=8192) is a vector whose first 2048 values are the previous fc2's output."""
+    out = {}
+    bb = 18 if qt == mg.Q4_0 else 34
+    for name, K, N in LAYER_SHAPES + [HEAD]:
+        wbytes = N * (K // 32) * bb
+        L = max(4, -(-256_000_000 // wbytes))
+        links, prev = [], None
+        xs = dev.empty(K, mg.F32)
+        dev.fill_normal(xs, K, SEED + 77, 1.0)
+        for i in range(L):
+            W = make_q(dev, mg, tmp, qt, K, N, SEED + 50_000 + 31 * i + K + N)
+            if K <= N:
+                y = dev.empty(N, mg.F32)
+                x = xs if prev is None else prev.view(0, K * 4).set_format(mg.F32)
+                nxt = y
+            else:
+                # the next link's K-long input, whose first N values this link writes
+                xn = dev.empty(K, mg.F32)
+                dev.fill_normal(xn, K, SEED + 78 + i, 1.0)
+                y = xn.view(0, N * 4).set_format(mg.F32)
+                x = xs if prev is None else prev
+                nxt = xn
+            links.append((name, x, W, y, N, K))
+            prev = nxt
+        ms = time_graph(dev, torch, stream, lambda: enqueue_links(dev, mg, qt, links), 20)
+        gbs = L * qbytes(qt, K, N) / (ms * 1e-3) / 1e9
+        out[name] = {"K": K, "N": N, "links": L, "us_per_gemv": round(ms * 1e3 / L, 3), "gbs": round(gbs, 1),
+                     "frac": round(gbs / peaks["hbm_gbs"], 4)}
+        del links
+    return out
+
+
+def run_chain_kernel(dev, mg, torch, stream, peaks, qt, links, step_bytes) -> dict:
+    """The same decode step through mgpu_gemv_chain (one cooperative launch for all links)."""
+    chain = mg.GemvChain(dev, [(x, W, y, N, K) for _, x, W, y, N, K in links])
+    try:
+        ms = time_graph(dev, torch, stream, lambda: chain.run(), 20)
+        ends = chain.run_timed()
+        per = {}
+        prev = 0.0
+        for (name, _, _, _, N, K), t in zip(links, ends):
+            d = per.setdefault(name, [0.0, 0])
+            d[0] += t - prev
+            d[1] += qbytes(qt, K, N)
+            prev = t
+        gbs = step_bytes / (ms * 1e-3) / 1e9
+        return {"ms_per_step": round(ms, 5), "gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 4),
+                "launches_per_step": 1,
+                "per_shape_gbs": {k: round(v[1] / (v[0] * 1e-6) / 1e9, 1) for k, v in per.items()},
+                "basis": "one cooperative launch over the step's links; per-shape figures from one run with "
+                         "%globaltimer marks at each link's end (max over CTAs)"}
+    finally:
+        chain.destroy()
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch
 
@@ -170,73 +278,45 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     dev.set_stream(stream.cuda_stream)
     dev.set_event_mode(0)
     peaks = measured_peaks()
+    qt = mg.Q4_0
 
-    # ---------------- weights: generated and quantised on the device ----------------
-    from mvlm_b200.shard import column_shard, gather_columns
+    # ---------------- the decode step, weights generated and quantised on the device ----------------
+    from mvlm_b200.shard import column_shard, combine_argmax_device
     h0, h1 = column_shard(HEAD[2], world, rank)
     n_head = h1 - h0
-    head_rows = [column_shard(HEAD[2], world, r)[0] for r in range(world)] + [HEAD[2]]
-    max_el = max(max(K * N for _, K, N in LAYER_SHAPES), HEAD[1] * n_head)
-    tmp = dev.empty(max_el, mg.F32)
-
-    def make_q(K, N, seed):
-        w = dev.create_buffer(N * (K // 32) * 18, None, mg.Q4_0, mg.LAYOUT_NK, N, K)
-        dev.fill_normal(tmp, N * K, seed, 0.02)
-        dev.quantize(tmp, w, N * K, mg.Q4_0)
-        return w
-
-    layers = []
-    for l in range(LAYERS):
-        mats = []
-        for j, (name, K, N) in enumerate(LAYER_SHAPES):
-            W = make_q(K, N, SEED + 1000 * l + j)
-            x = dev.empty(K, mg.F32)
-            dev.fill_normal(x, K, SEED + 7 + 1000 * l + j, 1.0)
-            y = dev.empty(N, mg.F32)
-            mats.append((name, K, N, W, x, y))
-        layers.append(mats)
-    # lm_head shard: this rank's rows [head_rows[r], head_rows[r+1]) of W[51200][2048]
-    K_h = HEAD[1]
-    Wh = make_q(K_h, n_head, SEED + 999_999 + rank)
-    xh = dev.empty(K_h, mg.F32)
-    dev.fill_normal(xh, K_h, SEED + 5, 1.0)
-    y_full = torch.empty(HEAD[2], dtype=torch.float32, device="cuda")
-    y_shard_t = torch.empty(n_head, dtype=torch.float32, device="cuda")
-    yh = dev.wrap(y_shard_t.data_ptr(), n_head * 4, mg.F32)
-    del tmp
+    tmp = dev.empty(max(max(K * N for _, K, N in LAYER_SHAPES), HEAD[1] * HEAD[2]), mg.F32)
+    links, x0 = build_decode_step(dev, mg, tmp, qt, n_head, rank)
     dev.finish()
+    K_h = HEAD[1]
+    yh = links[-1][3]
+    hidden = links[-2][3]
+    # distinct bytes of one step: every layer once (replicated on N GPUs) + the whole lm_head
+    step_bytes = sum(qbytes(qt, K, N) for _, K, N in LAYER_SHAPES) * LAYERS + qbytes(qt, K_h, HEAD[2])
+    # the greedy token on N GPUs: each rank's argmax over its logit shard (8 bytes), all-gathered
+    arg_t = torch.zeros(2, dtype=torch.int32, device="cuda")
+    argbuf = dev.wrap(arg_t.data_ptr(), 8, mg.F32)
+    gath = torch.zeros(2 * world, dtype=torch.int32, device="cuda")
+    head_offsets = torch.tensor([column_shard(HEAD[2], world, r)[0] for r in range(world)], dtype=torch.int64,
+                                device="cuda")
 
-    step_bytes = sum(gemv_bytes(K, N) for _, K, N in LAYER_SHAPES) * LAYERS + gemv_bytes(K_h, HEAD[2])
-    launches_per_step = LAYERS * len(LAYER_SHAPES) + 1
+    def enqueue():
+        enqueue_links(dev, mg, qt, links)
+        if world > 1:
+            mg.argmax(dev, yh, n_head, argbuf)
 
-    # ---------------- capture one step ----------------
-    def enqueue_step():
-        for mats in layers:
-            for name, K, N, W, x, y in mats:
-                mg.gemv_q(dev, x, W, y, N, K, mg.Q4_0)
-        m0 = dev.record_event()
-        mg.gemv_q(dev, xh, Wh, yh, n_head, K_h, mg.Q4_0)
-        m1 = dev.record_event()
-        return m0, m1
-
-    enqueue_step()  # eager run first (validates arguments outside capture)
+    enqueue()  # eager run first (validates arguments outside capture)
     dev.finish()
     dev.capture_begin()
-    head0, head1 = enqueue_step()
+    enqueue()
     graph = dev.capture_end()
-
-    def gather_logits():
-        # one NCCL all-gather of the logit shards over NVLink (all_gather_into_tensor when the
-        # shards are equal, as for 51200 / {1,2,4,8})
-        if HEAD[2] % world == 0:
-            dist.all_gather_into_tensor(y_full, y_shard_t)
-        else:
-            y_full.copy_(gather_columns(y_shard_t, HEAD[2]))
+    launches_per_step = len(links) + (1 if world > 1 else 0)
 
     def step():
         graph.launch()
         if world > 1:
-            gather_logits()
+            dist.all_gather_into_tensor(gath, arg_t)
+            return combine_argmax_device(gath, head_offsets)
+        return None
 
     for _ in range(args.warmup):
         step()
@@ -253,87 +333,92 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for _ in range(args.steps):
-        step()
+        token = step()
     ev1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clocks = sampler.stop()
-    ms_total = ev0.elapsed_time(ev1)
-    # lm_head launch duration: marker events captured around it inside the graph, read after
-    # each of a few replays (the graph is the same one the timed loop replays)
-    head_samples = []
-    for _ in range(min(args.steps, 50)):
-        step()
-        torch.cuda.synchronize()
-        head_samples.append(head0.elapsed_ms(head1))
-    head_ms = statistics.mean(head_samples)
-
-    ms = ms_total / args.steps
+    ms = ev0.elapsed_time(ev1) / args.steps
     if world > 1:
-        t = torch.tensor([ms, head_ms], dtype=torch.float64, device="cuda")
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, head_ms = float(t[0]), float(t[1])
+        ms = float(t[0])
 
-    # ---------------- e2e through the C ABI with host buffers ----------------
-    y_full_buf = dev.wrap(y_full.data_ptr(), HEAD[2] * 4, mg.F32) if world > 1 else None
-    e2e = run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, dist, gather_logits, torch,
-                  stream, y_full_buf)
+    # ---------------- parity of the step's result ----------------
+    parity = {"ok": None, "skipped": "--ncu"}
+    e2e = None
+    if not args.ncu:
+        parity = check_decode_parity(dev, mg, torch, dist, world, rank, qt, tmp, links, n_head,
+                                     token if world > 1 else None)
+        # ---------------- e2e through the C ABI with host buffers ----------------
+        e2e = run_e2e(args, dev, mg, torch, stream, dist, world, qt, links, x0, argbuf, arg_t, gath, head_offsets,
+                      step_bytes)
 
-    # ---------------- prefill GEMMs (secondary metric) ----------------
-    prefill = run_prefill(dev, mg, torch, stream, peaks) if rank == 0 and not args.no_prefill else None
-    # ---------------- the other BASELINE configs (secondary, one GPU) ----------------
-    secondary = None
+    # ---------------- secondary measurements ----------------
+    graph = None
+    secondary = {}
+    if world == 1 and not args.no_secondary:
+        per_launch_logits = yh.read(np.float32)
+        secondary["chain_kernel"] = _guarded(run_chain_kernel, dev, mg, torch, stream, peaks, qt, links, step_bytes)
+        secondary["chain_kernel"]["logits_equal_per_launch"] = bool(np.array_equal(yh.read(np.float32),
+                                                                                  per_launch_logits))
+        secondary["per_shape"] = run_per_shape(dev, mg, torch, stream, peaks, qt, tmp)
+        secondary["q8_0_sweep"] = _guarded(run_q8_sweep, dev, mg, torch, stream, peaks, tmp)
+    del tmp
+    layers = [[(name, K, N, W, x, y) for name, x, W, y, N, K in links[4 * l:4 * l + 4]] for l in range(LAYERS)]
+    Wh = links[-1][2]
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill(dev, mg, torch, stream, peaks, world, dist, rank)
     if not args.no_secondary:
         if world == 1:
-            secondary = {"fp32_gemv": run_fp32_gemv(dev, mg, torch, stream, peaks),
-                         "batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head),
-                         # before SigLIP, whose seconds of dense MMAs can leave the clocks power-capped
-                         "fused_epilogues": _guarded(run_fused_epilogues, dev, mg, torch, stream, peaks),
-                         "siglip": run_siglip(dev, mg, torch, stream, peaks)}
+            secondary.update({"fp32_gemv": run_fp32_gemv(dev, mg, torch, stream, peaks),
+                              "batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h,
+                                                                   n_head),
+                              # before SigLIP, whose seconds of dense MMAs can leave the clocks power-capped
+                              "fused_epilogues": _guarded(run_fused_epilogues, dev, mg, torch, stream, peaks),
+                              "siglip": run_siglip(dev, mg, torch, stream, peaks)})
         else:
             # every rank takes part (collectives); rank 0 reports
-            secondary = {"batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head,
-                                                              world=world, dist=dist),
-                         "siglip": run_siglip(dev, mg, torch, stream, peaks, batches=(8, 64), world=world, dist=dist)}
-
-    graph = None
+            secondary.update({"batched_decode": run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h,
+                                                                   n_head, world=world, dist=dist),
+                              "siglip": run_siglip(dev, mg, torch, stream, peaks, batches=(8, 64), world=world,
+                                                   dist=dist)})
+    if "siglip" in secondary and "parity" in secondary["siglip"]:
+        parity["siglip_rel_err"] = secondary["siglip"]["parity"]["rel_err"]
+        parity["ok"] = parity["ok"] and secondary["siglip"]["parity"]["ok"]
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return None
 
-    head_bytes = gemv_bytes(K_h, n_head)
-    achieved = head_bytes / (head_ms * 1e-3) / 1e9
     value = step_bytes / (ms * 1e-3) / 1e9
+    traffic = profiled_traffic()
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "pct_of_peak": round(100.0 * value / peaks["hbm_gbs"], 1),
-        "data": "synthetic: weights ~N(0,0.02) seeded, quantised to GGUF Q4_0 on the device; x ~N(0,1) fp32",
-        "config": {"workload": "Q4_0 decode GEMV sweep, M=1: 24 layers x (qkv 2048x6144, out 2048x2048, "
-                               "fc1 2048x8192, fc2 8192x2048) + lm_head 2048x51200 (BASELINE config 1 shapes "
-                               "over the model's 24 layers)",
+        "data": "synthetic: weights ~N(0,0.02) seeded, quantised to GGUF Q4_0 on the device; x0 ~N(0,1) fp32",
+        "config": {"workload": DECODE_WORKLOAD,
                    "bytes_per_step": step_bytes, "launches_per_step": launches_per_step,
                    "l2": "inputs larger than L2: 738 MB of packed weights per step vs 126 MB L2",
-                   "parallelism": f"lm_head column-shard x{world} + NCCL all-gather; layers replicated"
-                   if world > 1 else "single GPU", "seed": SEED, "prng": "SplitMix64 + Box-Muller (device)"},
-        "roofline": {"bound": "hbm", "kernel": "gemv_q_stream", "launches_per_step": launches_per_step,
+                   "parallelism": f"lm_head column-shard x{world} + distributed argmax (8-byte all-gather); "
+                                  f"layers replicated" if world > 1 else "single GPU",
+                   "seed": SEED, "prng": "SplitMix64 + Box-Muller (device)"},
+        "roofline": {"bound": "hbm", "kernel": "gemv_q_stream", "launches_per_step": len(links),
                      "achieved": round(value, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(value / peaks["hbm_gbs"], 4), "traffic": None,
-                     "avg_launch_us": round(ms * 1e3 / launches_per_step, 3),
-                     "bytes_per_launch_avg": step_bytes // launches_per_step, "peak_source": peaks["source"],
-                     "basis": "every launch in the timed region is gemv_q_stream, back to back: average "
-                              "algorithmic bytes per launch / average launch duration (CUDA events)"},
-        "lm_head_launch": {"gbs": round(achieved, 1), "frac": round(achieved / peaks["hbm_gbs"], 4),
-                           "bytes": head_bytes, "ms": round(head_ms, 5),
-                           "basis": "marker events captured around the lm_head launch inside the graph",
-                           "dram_traffic_bytes": 59059360 if world == 1 else None,
-                           "dram_traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch, "
-                                                  "profiles/gemv_q_stream_q4_0_lm_head_2048x51200.md"},
+                     "frac": round(value / peaks["hbm_gbs"], 4), "traffic": traffic.get("bytes_per_step"),
+                     "traffic_source": traffic.get("source"),
+                     "avg_launch_us": round(ms * 1e3 / len(links), 3),
+                     "bytes_per_launch_avg": step_bytes // len(links), "peak_source": peaks["source"],
+                     "basis": "every GEMV of the step is a gemv_q_stream launch, back to back under programmatic "
+                              "dependent launch: algorithmic bytes of the step / device time of the step (CUDA "
+                              "events)"},
+        "parity": parity, "parity_ok": parity["ok"],
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
@@ -347,44 +432,81 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     return line
 
 
-def run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, dist, gather_logits, torch,
-            stream, y_full_buf=None) -> dict:
-    """The step through the public C ABI, from pinned host memory to pinned host memory, the way
-    an engine drives it: the step's 97 activation vectors live in one device arena (views from
-    mgpu_buf_view), so one mgpu_buf_write_async moves them all; the 97 mgpu_gemv_q dispatches
-    are captured once with mgpu_capture_begin/end and replayed with mgpu_graph_launch; one
-    mgpu_buf_read_async returns every layer output.  The logits: on one GPU they are in the same
-    arena; on N GPUs each rank's shard is all-gathered (NCCL over NVLink) and the full logits
-    are read back with a second mgpu_buf_read_async.  Device time of the whole loop, copies
-    included, by CUDA events on the stream."""
-    L = mg.lib()
-    shapes = [(K, N, W) for mats in layers for (_, K, N, W, _, _) in mats] + [(K_h, n_head, Wh)]
-    h2d = sum(K * 4 for K, _, _ in shapes)
-    y_shapes = shapes if world == 1 else shapes[:-1]  # N>1: the logit shard goes to yh, then all-gathered
-    y_bytes = sum(N * 4 for _, N, _ in y_shapes)
-    logit_bytes = 0 if world == 1 else HEAD[2] * 4
-    d2h = y_bytes + logit_bytes
-    x_arena = dev.create_buffer(h2d, None, mg.F32)
-    y_arena = dev.create_buffer(y_bytes, None, mg.F32)
-    xv, yv = [], []
-    xo = yo = 0
-    for K, N, _ in shapes:
-        xv.append(x_arena.view(xo, K * 4))
-        xo += K * 4
-    for _, N, _ in y_shapes:
-        yv.append(y_arena.view(yo, N * 4))
-        yo += N * 4
+def check_decode_parity(dev, mg, torch, dist, world, rank, qt, tmp, links, n_head, token) -> dict:
+    """The step's result against independent computations, after the timed region:
+    - the logits (on N GPUs all-gathered once) against the CPU oracle's lm_head (dequantise +
+      fp32 dot, the reference's quantised path) applied to the same final hidden state, within
+      the fp32 tolerance 1e-4 of the output's max-norm;
+    - on N GPUs also against one GPU's full lm_head (the shards' weights regenerated on rank 0),
+      and the distributed greedy token against the argmax of the gathered logits."""
+    import oracle as O
+    from mvlm_b200.shard import column_shard
+    yh, hidden = links[-1][3], links[-2][3]
+    K_h, N_h = HEAD[1], HEAD[2]
+    logits = torch.empty(N_h, dtype=torch.float32, device="cuda")
     if world > 1:
-        yv.append(yh)
+        from mvlm_b200.shard import gather_columns
+        shard = torch.from_numpy(yh.read(np.float32)).cuda()
+        logits = gather_columns(shard, N_h)
+    else:
+        logits.copy_(torch.from_numpy(yh.read(np.float32)).cuda())
+    out = {"tolerance": 1e-4}
+    if rank != 0:
+        return {"ok": True}
+    h = hidden.read(np.float32)[:K_h].copy()
+    got = logits.cpu().numpy()
+    # the whole lm_head's packed rows: this rank's, or every rank's regenerated from their seeds
+    if world == 1:
+        Wfull = links[-1][2].read(np.uint8)
+    else:
+        parts = []
+        for r in range(world):
+            a, b = column_shard(N_h, world, r)
+            w = make_q(dev, mg, tmp, qt, K_h, b - a, head_seed(r))
+            parts.append(w.read(np.uint8))
+        Wfull = np.concatenate(parts)
+        # one GPU's full lm_head from the same hidden state
+        dW = dev.array(Wfull, qt, mg.LAYOUT_NK)
+        dy = dev.empty(N_h, mg.F32)
+        mg.gemv_q(dev, dev.array(h, mg.F32), dW, dy, N_h, K_h, qt).wait()
+        one = dy.read(np.float32)
+        out["gathered_vs_one_gpu_rel_err"] = float(np.max(np.abs(got - one)) / np.max(np.abs(one)))
+        out["token"] = int(token.item())
+        out["token_is_argmax"] = out["token"] == int(np.argmax(got))
+    O.set_threads(len(os.sched_getaffinity(0)))
+    ref = O.gemm_q(h, Wfull, 1, N_h, K_h, qt, threads=True)
+    out["logits_vs_oracle_rel_err"] = float(np.max(np.abs(got - ref)) / np.max(np.abs(ref)))
+    ok = out["logits_vs_oracle_rel_err"] <= 1e-4
+    if world > 1:
+        ok = ok and out["gathered_vs_one_gpu_rel_err"] <= 1e-4 and out["token_is_argmax"]
+    out["ok"] = bool(ok)
+    return out
+
+
+def run_e2e(args, dev, mg, torch, stream, dist, world, qt, links, x0, argbuf, arg_t, gath, head_offsets,
+            step_bytes) -> dict:
+    """The step through the public C ABI, from pinned host memory to pinned host memory, as an
+    engine drives a decode token: mgpu_buf_write_async of the token's hidden state (8 KB), the
+    captured step (97 mgpu_gemv_q and the device argmax of the logits, mgpu_argmax) replayed with
+    mgpu_graph_launch, and one mgpu_buf_read_async of the 8-byte greedy result.  On N GPUs each
+    rank's argmax of its logit shard is all-gathered (NCCL, 8 bytes per rank) and combined on the
+    device.  Device time of the whole loop, copies included, by CUDA events on the stream."""
+    from mvlm_b200.shard import combine_argmax_device
+    L = mg.lib()
+    yh = links[-1][3]
+    n_head = links[-1][4]
+    h2d, d2h = HEAD[1] * 4, 8
+    tok_t = torch.zeros(2, dtype=torch.int32, device="cuda")
+    tok = dev.wrap(tok_t.data_ptr(), 8, mg.F32)
     hx = L.mgpu_host_alloc(h2d)
     hy = L.mgpu_host_alloc(d2h)
     try:
-        host_x = np.ctypeslib.as_array((np.ctypeslib.ctypes.c_float * (h2d // 4)).from_address(hx))
+        host_x = np.ctypeslib.as_array((ctypes_float() * (h2d // 4)).from_address(hx))
         host_x[:] = np.random.default_rng(SEED).standard_normal(h2d // 4).astype(np.float32)
 
         def enqueue():
-            for (K, N, W), x, y in zip(shapes, xv, yv):
-                mg.gemv_q(dev, x, W, y, N, K, mg.Q4_0)
+            enqueue_links(dev, mg, qt, links)
+            mg.argmax(dev, yh, n_head, argbuf)
 
         enqueue()  # eager pass: validates arguments outside the capture
         dev.finish()
@@ -393,12 +515,14 @@ def run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, d
         graph = dev.capture_end()
 
         def one():
-            mg._check(L.mgpu_buf_write_async(x_arena.h, 0, hx, h2d), "buf_write_async")
+            mg._check(L.mgpu_buf_write_async(x0.h, 0, hx, h2d), "buf_write_async")
             graph.launch()
-            mg._check(L.mgpu_buf_read_async(y_arena.h, 0, hy, y_bytes), "buf_read_async")
             if world > 1:
-                gather_logits()
-                mg._check(L.mgpu_buf_read_async(y_full_buf.h, 0, hy + y_bytes, logit_bytes), "buf_read_async")
+                dist.all_gather_into_tensor(gath, arg_t)
+                tok_t[0] = combine_argmax_device(gath, head_offsets).to(torch.int32)
+                mg._check(L.mgpu_buf_read_async(tok.h, 0, hy, d2h), "buf_read_async")
+            else:
+                mg._check(L.mgpu_buf_read_async(argbuf.h, 0, hy, d2h), "buf_read_async")
 
         steps = max(3, min(args.steps, 2000))
         for _ in range(3):
@@ -418,75 +542,165 @@ def run_e2e(args, dev, mg, layers, xh, Wh, yh, n_head, K_h, step_bytes, world, d
             ms = float(t[0])
         return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 5), "steps": steps,
-                "api": "mgpu_buf_write_async (all 97 inputs, one pinned buffer) + mgpu_graph_launch of the "
-                       "captured 97 mgpu_gemv_q + mgpu_buf_read_async (all outputs"
-                       + ("" if world == 1 else "; logits after an NCCL all-gather") + ")"}
+                "api": "mgpu_buf_write_async (the token's hidden state, pinned) + mgpu_graph_launch of the "
+                       "captured 97 mgpu_gemv_q + mgpu_argmax + mgpu_buf_read_async (the 8-byte greedy result"
+                       + ("" if world == 1 else "; rank argmaxes all-gathered with NCCL and combined on the device")
+                       + ")"}
     finally:
         L.mgpu_host_free(hx)
         L.mgpu_host_free(hy)
 
 
-def run_prefill(dev, mg, torch, stream, peaks) -> dict:
+def ctypes_float():
+    import ctypes
+    return ctypes.c_float
+
+
+def run_q8_sweep(dev, mg, torch, stream, peaks, tmp) -> dict:
+    """BASELINE config 1's Q8_0 half: the same decode step (24 layers + lm_head, each GEMV reading
+    the previous output) with the weights quantised to Q8_0, then each shape's dependent chain."""
+    qt = mg.Q8_0
+    links, _ = build_decode_step(dev, mg, tmp, qt, HEAD[2], 0)
+    step_bytes = sum(qbytes(qt, K, N) for _, K, N in LAYER_SHAPES) * LAYERS + qbytes(qt, HEAD[1], HEAD[2])
+    ms = time_graph(dev, torch, stream, lambda: enqueue_links(dev, mg, qt, links), 50)
+    del links
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    return {"bytes_per_step": step_bytes, "ms_per_step": round(ms, 5), "gbs": round(gbs, 1),
+            "frac": round(gbs / peaks["hbm_gbs"], 4),
+            "per_shape": run_per_shape(dev, mg, torch, stream, peaks, qt, tmp)}
+
+
+def profiled_traffic() -> dict:
+    """DRAM bytes per step of the decode step's kernels, from the committed ncu summary of the
+    same workload (profiles/gemv_q_stream_decode_step_dram.md: the `bytes per step` row)."""
+    path = os.path.join(ROOT, "profiles", "gemv_q_stream_decode_step_dram.md")
+    if not os.path.exists(path):
+        return {}
+    with open(path) as f:
+        for line in f:
+            if line.startswith("| bytes per step"):
+                cells = [c.strip() for c in line.strip().strip("|").split("|")]
+                return {"bytes_per_step": int(cells[1].replace(",", "")), "source": os.path.relpath(path, ROOT)}
+    return {}
+
+
+def run_prefill(dev, mg, torch, stream, peaks, world=1, dist=None, rank=0) -> dict:
     """tcgen05 GEMM on the Phi-1.5 prefill shapes: M=761, bf16 A, Q8_0 W (dequantised to bf16
     tiles inside the kernel), fp32 accumulate, bf16 C.  Rotates enough weight copies per shape
-    that each pass over them is about 2x the L2.
-    The kernels are timed as a captured graph of one launch per copy (at least 40), which is
-    what an engine replaying its prefill graph sees; `eager_tflops` is the same loop dispatched
-    call by call from Python, whose ~8 us of host time per call hides part of the kernel time."""
+    that each pass over them is about 2x the L2; the kernels are timed as a captured graph of
+    one launch per copy (at least 40), replayed.
+    On N GPUs fc1 (2048x8192) is column-sharded: each rank computes 8192/N output columns of
+    every token and the shards are all-gathered with NCCL over NVLink into the [761][8192]
+    activations (the gathered [rank][M][N/N] blocks are put in row order on the device); the
+    other three GEMMs run whole on every rank (replicas).  Time = max over ranks; TFLOP/s count
+    each GEMM's full 2MKN once."""
+    import oracle as O
+    from mvlm_b200.shard import column_shard
     out = {}
     tot_flop, tot_ms = 0.0, 0.0
-    tmp_el = max(K * N for _, K, N in PREFILL_SHAPES)
-    tmp = dev.empty(tmp_el, mg.F32)
+    tmp = dev.empty(max(K * N for _, K, N in PREFILL_SHAPES), mg.F32)
+    parity = {}
     for M, K, N in PREFILL_SHAPES:
-        wbytes = N * (K // 32) * 34
-        ncopy = max(4, -(-256_000_000 // wbytes))
+        sharded = world > 1 and (K, N) == (2048, 8192)
+        a, b = column_shard(N, world, rank) if sharded else (0, N)
+        n_loc = b - a
+        rb = (K // 32) * 34
+        wbytes = N * rb
+        ncopy = max(4, -(-256_000_000 // (n_loc * rb)))
         iters = max(40, ncopy)
         A = dev.empty(M * K, mg.BF16)
         dev.fill_normal(A, M * K, SEED + K, 1.0)
-        Ws = []
+        Ws, Wfull = [], []
         for c in range(ncopy):
             w = dev.create_buffer(wbytes, None, mg.Q8_0, mg.LAYOUT_NK, N, K)
             dev.fill_normal(tmp, N * K, SEED + N + 17 * c, 0.02)
             dev.quantize(tmp, w, N * K, mg.Q8_0)
-            Ws.append(w)
-        C = dev.empty(M * N, mg.BF16)
-        for w in Ws:
-            mg.gemm_q(dev, A, w, C, M, N, K, mg.Q8_0)
+            Wfull.append(w)
+            Ws.append(w.view(a * rb, n_loc * rb).set_format(mg.Q8_0, mg.LAYOUT_NK, n_loc, K) if sharded else w)
+        C_t = torch.empty(M * n_loc, dtype=torch.bfloat16, device="cuda")
+        C = dev.wrap(C_t.data_ptr(), M * n_loc * 2, mg.BF16)
+        for w in Ws:  # eager pass first: validates the arguments outside the capture
+            mg.gemm_q(dev, A, w, C, M, n_loc, K, mg.Q8_0)
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for i in range(iters):
-            mg.gemm_q(dev, A, Ws[i % ncopy], C, M, N, K, mg.Q8_0)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ms_eager = e0.elapsed_time(e1) / iters
         dev.capture_begin()
         for i in range(iters):
-            mg.gemm_q(dev, A, Ws[i % ncopy], C, M, N, K, mg.Q8_0)
+            mg.gemm_q(dev, A, Ws[i % ncopy], C, M, n_loc, K, mg.Q8_0)
         graph = dev.capture_end()
+        if sharded:
+            gath = torch.empty(world * M * n_loc, dtype=torch.bfloat16, device="cuda")
+            full = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+
+            def once():
+                graph.launch()
+                # every launch of the replay writes the same shard: one gather per replay, as a
+                # layer's forward pays one
+                dist.all_gather_into_tensor(gath, C_t)
+                full.copy_(gath.view(world, M, n_loc).permute(1, 0, 2).reshape(M, N))
+        else:
+            def once():
+                graph.launch()
         for _ in range(3):
-            graph.launch()
+            once()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         reps = 5
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(reps):
-            graph.launch()
+            once()
         e1.record(stream)
         torch.cuda.synchronize()
-        del graph
-        ms = e0.elapsed_time(e1) / (reps * iters)
+        ms_all = e0.elapsed_time(e1) / reps
+        if world > 1:
+            t = torch.tensor([ms_all], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_all = float(t[0])
+        ms = ms_all / iters
+        if sharded:
+            # the gather's share: time the GEMM graph alone too, the difference is the exchange
+            e0.record(stream)
+            for _ in range(reps):
+                graph.launch()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            gemm_ms = float(t[0]) / iters
+            gather_ms = ms_all - float(t[0])
+            ms = gemm_ms + gather_ms
         flop = 2.0 * M * K * N
-        out[f"{K}x{N}"] = {"tflops": round(flop / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2),
-                           "eager_tflops": round(flop / (ms_eager * 1e-3) / 1e12, 1), "weight_copies": ncopy}
-        del Ws, A, C
+        key = f"{K}x{N}"
+        out[key] = {"tflops": round(flop / (ms * 1e-3) / 1e12, 1), "us": round(ms * 1e3, 2),
+                    "weight_copies": ncopy}
+        if sharded:
+            out[key].update({"column_shard": f"{n_loc} of {N} columns per GPU", "gemm_us": round(gemm_ms * 1e3, 2),
+                             "all_gather_us": round(gather_ms * 1e3, 2)})
+        if (K, N) == (2048, 8192) and rank == 0:
+            # parity of the (gathered) fc1 output on a few tokens against the CPU oracle
+            rows = [0, 1, 380, 760]
+            got = (full.float().cpu().numpy() if sharded else
+                   C_t.float().cpu().numpy().reshape(M, N))[rows]
+            Ah = O.bf16_to_f32(A.read(np.uint16)).reshape(M, K)[rows]
+            ref = O.gemm_q(np.ascontiguousarray(Ah), Wfull[(iters - 1) % ncopy].read(np.uint8), len(rows), N, K,
+                           O.Q8_0, threads=True).reshape(len(rows), N)
+            err = float(np.max(np.abs(got - ref)) / np.max(np.abs(ref)))
+            parity = {"fc1_rows_checked": rows, "rel_err": err, "tolerance": 1e-2, "ok": err <= 1e-2}
+        graph = None
+        del Ws, Wfull, A, C, C_t
         tot_flop += flop
         tot_ms += ms
     agg = tot_flop / (tot_ms * 1e-3) / 1e12
-    return {"unit": "TFLOP/s", "M": 761, "weights": "Q8_0", "activations": "bf16", "shapes": out,
-            "aggregate_tflops": round(agg, 1), "frac_of_peak": round(agg / peaks["bf16_tflops"], 4),
-            "peak": peaks["bf16_tflops"], "peak_source": peaks["source"],
-            "timing": "CUDA events around 5 replays of a captured graph of one launch per weight copy; "
-                      "copies rotated so each pass reads ~256 MB of packed weights (2x L2)"}
+    res = {"unit": "TFLOP/s", "M": 761, "weights": "Q8_0", "activations": "bf16", "n_gpus": world, "shapes": out,
+           "aggregate_tflops": round(agg, 1), "frac_of_peak": round(agg / peaks["bf16_tflops"], 4),
+           "peak": peaks["bf16_tflops"], "peak_source": peaks["source"],
+           "parallelism": "single GPU" if world == 1 else
+           f"fc1 column-shard x{world} + NCCL all-gather; qkv / out / fc2 replicated",
+           "timing": "CUDA events around 5 replays of a captured graph of one launch per weight copy; "
+                     "copies rotated so each pass reads ~256 MB of packed weights (2x L2)"}
+    if parity:
+        res["parity"] = parity
+    return res
 
 
 def _guarded(fn, *args) -> dict:
@@ -625,6 +839,7 @@ def run_siglip(dev, mg, torch, stream, peaks, batches=(1, 8, 64), world=1, dist=
         Ws.append(w)
     del tmp
     out = {}
+    parity = {}
     for B in batches:
         if B % world:
             continue
@@ -646,10 +861,30 @@ def run_siglip(dev, mg, torch, stream, peaks, batches=(1, 8, 64), world=1, dist=
         tf = flop / (ms * 1e-3) / 1e12
         out[f"B{B}"] = {"M_per_gpu": M, "tflops": round(tf, 1), "frac": round(tf / (peaks["bf16_tflops"] * world), 4),
                         "ms": round(ms, 4), "gflop": round(flop / 1e9, 1)}
+        if B == max(batches):
+            # parity: C holds the last GEMM (projection 8192 -> 2048) of this GPU's images; a few
+            # of its rows against the CPU oracle, on every rank, worst error over the ranks
+            import oracle as O
+            K, N = shapes[-1]
+            rows = [0, 1, M // 2, M - 1]
+            Ah = O.f16_to_f32(A.read(np.uint16, M * K)).reshape(M, K)[rows]
+            Cg = O.f16_to_f32(C.read(np.uint16, M * N)).reshape(M, N)[rows]
+            ref = O.gemm_nk(np.ascontiguousarray(Ah), Ws[-1].read(np.uint16), mg.F16, len(rows), N, K).reshape(
+                len(rows), N)
+            err = float(np.max(np.abs(Cg - ref)) / np.max(np.abs(ref)))
+            if world > 1:
+                t = torch.tensor([err], dtype=torch.float64, device="cuda")
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                err = float(t[0])
+            parity = {"batch": B, "rows_checked_per_gpu": rows, "gemm": f"{K}x{N}", "rel_err": err,
+                      "tolerance": 1e-2, "ok": err <= 1e-2}
         del A, C
-    return {"unit": "TFLOP/s", "dtype": "f16", "gemms": "layer qkv/out/fc1/fc2 + projection 2304x8192, 8192x2048",
-            "peak": peaks["bf16_tflops"], "peak_source": peaks["source"], "batches": out,
-            "parallelism": "single GPU" if world == 1 else f"batch-shard x{world} (B/{world} images per GPU)"}
+    res = {"unit": "TFLOP/s", "dtype": "f16", "gemms": "layer qkv/out/fc1/fc2 + projection 2304x8192, 8192x2048",
+           "peak": peaks["bf16_tflops"], "peak_source": peaks["source"], "batches": out,
+           "parallelism": "single GPU" if world == 1 else f"batch-shard x{world} (B/{world} images per GPU)"}
+    if parity:
+        res["parity"] = parity
+    return res
 
 
 def run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head, seqs=(8, 32, 128), world=1,
@@ -754,7 +989,7 @@ def run_reference(args, rank: int, world: int) -> dict | None:
     return {"metric": METRIC, "value": b["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32", "impl": "reference", "data": "synthetic (seeded, host)",
-            "config": {"workload": "Q4_0 decode GEMV sweep (one layer + lm_head sample), M=1, host cores"},
+            "config": {"workload": DECODE_WORKLOAD, "bytes_per_step": STEP_BYTES_Q4},
             "cpu_baseline": {"value": b["value"], "unit": "GB/s", "cores": b["cores"], "kind": "port",
                              "sample": b["sample"]},
             "e2e": {"value": b["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -772,8 +1007,14 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the fp32 GEMV, batched-decode and SigLIP sections")
+    ap.add_argument("--ncu", action="store_true",
+                    help="capture mode for ncu: only the decode step (3 timed steps), no e2e, parity or other "
+                         "sections, so that a launch list or a capture holds the step's kernels alone")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.ncu:
+        args.steps = min(args.steps, 3)
+        args.no_secondary = args.no_prefill = args.no_cpu_baseline = True
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

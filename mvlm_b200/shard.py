@@ -74,6 +74,20 @@ def combine_argmax(pairs: list[tuple[int, float]], n: int, world: int) -> int:
     return best_i
 
 
+def combine_argmax_device(slots, offsets):
+    """combine_argmax on the device, with no host round trip: `slots` holds the ranks'
+    all-gathered (index, fp32 value bits) int32 pairs in rank order, `offsets` (int64) each
+    rank's first global column.  torch.argmax returns the first maximum, i.e. the lowest rank
+    among equal values.  Returns a 0-dim int64 tensor."""
+    import torch
+
+    pairs = slots.view(-1, 2)
+    vals = pairs[:, 1].contiguous().view(torch.float32)
+    best = torch.argmax(vals)
+    idx = pairs[:, 0].to(torch.int64) + offsets
+    return torch.where(vals[best] > -1e30, idx[best], torch.zeros_like(idx[best]))
+
+
 def distributed_argmax(local_pair, n: int, group=None) -> int:
     """All-gather each rank's 8-byte (index, value) argmax of its lm_head shard (instead of its
     logits: 8 bytes per rank rather than 4 * n / world) and combine them.  `local_pair` is a

@@ -77,7 +77,7 @@ def _argmax_worker(rank, world, port, q):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         import oracle as O
-        from mvlm_b200.shard import distributed_argmax
+        from mvlm_b200.shard import combine_argmax_device, distributed_argmax
         N = 101
         ok = True
         for case in range(3):
@@ -91,8 +91,14 @@ def _argmax_worker(rank, world, port, q):
             i, v = O.argmax_logits(logits[a:b].view(np.uint32), O.F32)
             pair = torch.tensor([i, 0], dtype=torch.int32)
             pair[1] = torch.tensor([v], dtype=torch.float32).view(torch.int32)[0]
+            want = O.argmax_logits(logits.view(np.uint32), O.F32)[0]
             got = distributed_argmax(pair, N)
-            ok &= got == O.argmax_logits(logits.view(np.uint32), O.F32)[0]
+            ok &= got == want
+            # the device-side combine the timed decode step uses (no host round trip)
+            slots = torch.empty(2 * world, dtype=torch.int32)
+            dist.all_gather_into_tensor(slots, pair)
+            offsets = torch.tensor([column_shard(N, world, r)[0] for r in range(world)], dtype=torch.int64)
+            ok &= int(combine_argmax_device(slots, offsets)) == want
         q.put((rank, bool(ok)))
     finally:
         dist.destroy_process_group()
