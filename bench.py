@@ -281,7 +281,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     qt = mg.Q4_0
 
     # ---------------- the decode step, weights generated and quantised on the device ----------------
-    from mvlm_b200.shard import column_shard, combine_argmax_device
+    from mvlm_b200.shard import column_shard
     h0, h1 = column_shard(HEAD[2], world, rank)
     n_head = h1 - h0
     tmp = dev.empty(max(max(K * N for _, K, N in LAYER_SHAPES), HEAD[1] * HEAD[2]), mg.F32)
@@ -293,11 +293,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     # distinct bytes of one step: every layer once (replicated on N GPUs) + the whole lm_head
     step_bytes = sum(qbytes(qt, K, N) for _, K, N in LAYER_SHAPES) * LAYERS + qbytes(qt, K_h, HEAD[2])
     # the greedy token on N GPUs: each rank's argmax over its logit shard (8 bytes), all-gathered
+    # with NCCL, then combined on the device by mgpu_argmax_combine
     arg_t = torch.zeros(2, dtype=torch.int32, device="cuda")
     argbuf = dev.wrap(arg_t.data_ptr(), 8, mg.F32)
     gath = torch.zeros(2 * world, dtype=torch.int32, device="cuda")
-    head_offsets = torch.tensor([column_shard(HEAD[2], world, r)[0] for r in range(world)], dtype=torch.int64,
-                                device="cuda")
+    gathbuf = dev.wrap(gath.data_ptr(), 8 * world, mg.F32)
+    tok_t = torch.zeros(2, dtype=torch.int32, device="cuda")
+    tokbuf = dev.wrap(tok_t.data_ptr(), 8, mg.F32)
 
     def enqueue():
         enqueue_links(dev, mg, qt, links)
@@ -309,13 +311,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     dev.capture_begin()
     enqueue()
     graph = dev.capture_end()
-    launches_per_step = len(links) + (1 if world > 1 else 0)
+    launches_per_step = len(links) + (2 if world > 1 else 0)
 
     def step():
         graph.launch()
         if world > 1:
             dist.all_gather_into_tensor(gath, arg_t)
-            return combine_argmax_device(gath, head_offsets)
+            mg.argmax_combine(dev, gathbuf, world, HEAD[2], tokbuf)
+            return tok_t
         return None
 
     for _ in range(args.warmup):
@@ -353,8 +356,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         parity = check_decode_parity(dev, mg, torch, dist, world, rank, qt, tmp, links, n_head,
                                      token if world > 1 else None)
         # ---------------- e2e through the C ABI with host buffers ----------------
-        e2e = run_e2e(args, dev, mg, torch, stream, dist, world, qt, links, x0, argbuf, arg_t, gath, head_offsets,
-                      step_bytes)
+        e2e = run_e2e(args, dev, mg, torch, stream, dist, world, qt, links, x0, argbuf, arg_t, gath, gathbuf,
+                      tokbuf, step_bytes)
 
     # ---------------- secondary measurements ----------------
     graph = None
@@ -471,7 +474,7 @@ def check_decode_parity(dev, mg, torch, dist, world, rank, qt, tmp, links, n_hea
         mg.gemv_q(dev, dev.array(h, mg.F32), dW, dy, N_h, K_h, qt).wait()
         one = dy.read(np.float32)
         out["gathered_vs_one_gpu_rel_err"] = float(np.max(np.abs(got - one)) / np.max(np.abs(one)))
-        out["token"] = int(token.item())
+        out["token"] = int(token[0].item())
         out["token_is_argmax"] = out["token"] == int(np.argmax(got))
     O.set_threads(len(os.sched_getaffinity(0)))
     ref = O.gemm_q(h, Wfull, 1, N_h, K_h, qt, threads=True)
@@ -483,7 +486,7 @@ def check_decode_parity(dev, mg, torch, dist, world, rank, qt, tmp, links, n_hea
     return out
 
 
-def run_e2e(args, dev, mg, torch, stream, dist, world, qt, links, x0, argbuf, arg_t, gath, head_offsets,
+def run_e2e(args, dev, mg, torch, stream, dist, world, qt, links, x0, argbuf, arg_t, gath, gathbuf, tokbuf,
             step_bytes) -> dict:
     """The step through the public C ABI, from pinned host memory to pinned host memory, as an
     engine drives a decode token: mgpu_buf_write_async of the token's hidden state (8 KB), the
@@ -491,13 +494,10 @@ def run_e2e(args, dev, mg, torch, stream, dist, world, qt, links, x0, argbuf, ar
     mgpu_graph_launch, and one mgpu_buf_read_async of the 8-byte greedy result.  On N GPUs each
     rank's argmax of its logit shard is all-gathered (NCCL, 8 bytes per rank) and combined on the
     device.  Device time of the whole loop, copies included, by CUDA events on the stream."""
-    from mvlm_b200.shard import combine_argmax_device
     L = mg.lib()
     yh = links[-1][3]
     n_head = links[-1][4]
     h2d, d2h = HEAD[1] * 4, 8
-    tok_t = torch.zeros(2, dtype=torch.int32, device="cuda")
-    tok = dev.wrap(tok_t.data_ptr(), 8, mg.F32)
     hx = L.mgpu_host_alloc(h2d)
     hy = L.mgpu_host_alloc(d2h)
     try:
@@ -519,8 +519,8 @@ def run_e2e(args, dev, mg, torch, stream, dist, world, qt, links, x0, argbuf, ar
             graph.launch()
             if world > 1:
                 dist.all_gather_into_tensor(gath, arg_t)
-                tok_t[0] = combine_argmax_device(gath, head_offsets).to(torch.int32)
-                mg._check(L.mgpu_buf_read_async(tok.h, 0, hy, d2h), "buf_read_async")
+                mg.argmax_combine(dev, gathbuf, world, HEAD[2], tokbuf)
+                mg._check(L.mgpu_buf_read_async(tokbuf.h, 0, hy, d2h), "buf_read_async")
             else:
                 mg._check(L.mgpu_buf_read_async(argbuf.h, 0, hy, d2h), "buf_read_async")
 
@@ -544,7 +544,7 @@ def run_e2e(args, dev, mg, torch, stream, dist, world, qt, links, x0, argbuf, ar
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 5), "steps": steps,
                 "api": "mgpu_buf_write_async (the token's hidden state, pinned) + mgpu_graph_launch of the "
                        "captured 97 mgpu_gemv_q + mgpu_argmax + mgpu_buf_read_async (the 8-byte greedy result"
-                       + ("" if world == 1 else "; rank argmaxes all-gathered with NCCL and combined on the device")
+                       + ("" if world == 1 else "; rank argmaxes all-gathered with NCCL, mgpu_argmax_combine")
                        + ")"}
     finally:
         L.mgpu_host_free(hx)
@@ -664,10 +664,24 @@ def run_prefill(dev, mg, torch, stream, peaks, world=1, dist=None, rank=0) -> di
                 graph.launch()
             e1.record(stream)
             torch.cuda.synchronize()
-            t = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device="cuda")
+            g_ms = e0.elapsed_time(e1) / reps
+            # and the two halves of the exchange on their own: the NCCL all-gather, the re-layout
+            e0.record(stream)
+            for _ in range(reps):
+                dist.all_gather_into_tensor(gath, C_t)
+            e1.record(stream)
+            e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e2.record(stream)
+            for _ in range(reps):
+                full.copy_(gath.view(world, M, n_loc).permute(1, 0, 2).reshape(M, N))
+            e3.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([g_ms, e0.elapsed_time(e1) / reps, e2.elapsed_time(e3) / reps], dtype=torch.float64,
+                             device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             gemm_ms = float(t[0]) / iters
             gather_ms = ms_all - float(t[0])
+            nccl_ms, relayout_ms = float(t[1]), float(t[2])
             ms = gemm_ms + gather_ms
         flop = 2.0 * M * K * N
         key = f"{K}x{N}"
@@ -675,7 +689,9 @@ def run_prefill(dev, mg, torch, stream, peaks, world=1, dist=None, rank=0) -> di
                     "weight_copies": ncopy}
         if sharded:
             out[key].update({"column_shard": f"{n_loc} of {N} columns per GPU", "gemm_us": round(gemm_ms * 1e3, 2),
-                             "all_gather_us": round(gather_ms * 1e3, 2)})
+                             "exchange_us": round(gather_ms * 1e3, 2), "nccl_all_gather_us": round(nccl_ms * 1e3, 2),
+                             "relayout_us": round(relayout_ms * 1e3, 2),
+                             "all_gather_bytes": world * M * n_loc * 2})
         if (K, N) == (2048, 8192) and rank == 0:
             # parity of the (gathered) fc1 output on a few tokens against the CPU oracle
             rows = [0, 1, 380, 760]

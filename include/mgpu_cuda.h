@@ -252,6 +252,13 @@ mgpu_event* mgpu_dequant(const mgpu_device* dev, mgpu_buf* W, mgpu_buf* out, int
 mgpu_event* mgpu_argmax(const mgpu_device* dev, mgpu_buf* logits, int n, mgpu_buf* out);
 /* argmax_logits itself: waits for the stream and returns the index, or -1 on error. */
 int mgpu_argmax_logits(const mgpu_device* dev, mgpu_buf* logits, int vocab_size);
+/* New (the reference decodes on one device): the greedy token of logits column-sharded over
+ * n_ranks GPUs, from the ranks' mgpu_argmax results gathered in rank order (`pairs`: n_ranks x
+ * {int32 index within the shard, fp32 value}; rank r owns columns [r*(n/R) + min(r, n%R), ..)
+ * of the n_total, the first n % R ranks one more).  `out` (>= 8 bytes) receives the global
+ * index and its value: the larger value wins and equal values go to the lower rank, so the
+ * result is argmax_logits' first maximum over the whole row.  One thread, one launch. */
+mgpu_event* mgpu_argmax_combine(const mgpu_device* dev, mgpu_buf* pairs, int n_ranks, int n_total, mgpu_buf* out);
 
 /* ---------------------------------------------------------------- events ---------- */
 int mgpu_wait_event(mgpu_event* ev);                 /* clWaitForEvents(1, &ev) */

@@ -80,6 +80,7 @@ SIGNATURES = {
     "mgpu_dequant": (_vp, [_vp, _vp, _vp, _i64, _i]),
     "mgpu_argmax": (_vp, [_vp, _vp, _i, _vp]),
     "mgpu_argmax_logits": (_i, [_vp, _vp, _i]),
+    "mgpu_argmax_combine": (_vp, [_vp, _vp, _i, _i, _vp]),
     "mgpu_wait_event": (_i, [_vp]),
     "mgpu_release_event": (None, [_vp]),
     "mgpu_profile_end": (_d, [_vp]),
@@ -464,6 +465,12 @@ def dequant(dev: Device, W: Buffer, out: Buffer, n: int, qtype: int) -> Event:
 def argmax(dev: Device, logits: Buffer, n: int, out: Buffer) -> Event:
     """out (8 bytes) <- {int32 index, fp32 value}: the reference's argmax_logits on the device."""
     return _ev(lib().mgpu_argmax(dev.h, logits.h, n, out.h), "argmax")
+
+
+def argmax_combine(dev: Device, pairs: Buffer, n_ranks: int, n_total: int, out: Buffer) -> Event:
+    """out (8 bytes) <- the global {index, value} from the ranks' gathered mgpu_argmax pairs of a
+    row column-sharded over n_ranks GPUs (the reference's first maximum over the whole row)."""
+    return _ev(lib().mgpu_argmax_combine(dev.h, pairs.h, n_ranks, n_total, out.h), "argmax_combine")
 
 
 def argmax_logits(dev: Device, logits: Buffer, vocab_size: int) -> int:

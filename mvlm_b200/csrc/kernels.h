@@ -84,6 +84,8 @@ cudaError_t convert(const LaunchCtx& c, int itype, const void* in, int otype, vo
 cudaError_t selftest_bounded_wait(const LaunchCtx& c, uint64_t limit_ns);
 // out[0] = argmax index, out[1] = the value (fp32 bits), reference argmax semantics; n >= 1.
 cudaError_t argmax(const LaunchCtx& c, int type, const void* logits, int n, int* out);
+// The global first maximum of a row column-sharded over n_ranks, from the ranks' argmax pairs.
+cudaError_t argmax_combine(const LaunchCtx& c, const int* pairs, int n_ranks, int n_total, int* out);
 // patches[p][k] (k < kpad, zero for k >= C*ph*pw) from image [C][H][W]; same element type
 cudaError_t im2col(const LaunchCtx& c, int type, const void* img, void* patches, int C, int H, int W, int ph,
                    int pw, int kpad);

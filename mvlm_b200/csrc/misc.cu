@@ -164,6 +164,26 @@ __device__ __forceinline__ float argmax_value(int type, const void* x, int64_t i
     return __uint_as_float(b);
 }
 
+// The ranks' (index, value) argmax pairs of a column-sharded row, in rank order, into the
+// global first maximum: rank r's columns start at r * (n / R) + min(r, n % R); a strictly
+// larger value wins, so equal values keep the lower rank's (smaller) index; nothing above
+// -1e30 leaves index 0, as argmax_kernel starts.
+__global__ void argmax_combine_kernel(const int* __restrict__ pairs, int n_ranks, int n_total, int* out) {
+    if (threadIdx.x != 0) return;
+    const int base = n_total / n_ranks, extra = n_total % n_ranks;
+    float best = -1e30f;
+    int bi = 0;
+    for (int r = 0; r < n_ranks; ++r) {
+        const float v = __int_as_float(pairs[2 * r + 1]);
+        if (v > best) {
+            best = v;
+            bi = r * base + min(r, extra) + pairs[2 * r];
+        }
+    }
+    out[0] = bi;
+    out[1] = __float_as_int(best);
+}
+
 // One CTA: the first index whose value is greater than every earlier one, starting from
 // (-1e30, index 0) as the reference does; out[0] = index, out[1] = its value (fp32 bits).
 // Each thread scans a strided subsequence in index order keeping its first maximum; the
@@ -261,6 +281,11 @@ cudaError_t convert(const LaunchCtx& c, int itype, const void* in, int otype, vo
 
 cudaError_t argmax(const LaunchCtx& c, int type, const void* logits, int n, int* out) {
     argmax_kernel<<<1, 1024, 0, c.stream>>>(type, logits, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t argmax_combine(const LaunchCtx& c, const int* pairs, int n_ranks, int n_total, int* out) {
+    argmax_combine_kernel<<<1, 32, 0, c.stream>>>(pairs, n_ranks, n_total, out);
     return cudaGetLastError();
 }
 

@@ -1008,6 +1008,22 @@ mgpu_event* mgpu_argmax(const mgpu_device* cd, mgpu_buf* logits, int n, mgpu_buf
     return event_end(d, ev);
 }
 
+mgpu_event* mgpu_argmax_combine(const mgpu_device* cd, mgpu_buf* pairs, int n_ranks, int n_total, mgpu_buf* out) {
+    API_ENTRY();
+    REQUIRE(cd && pairs && out && n_ranks > 0 && n_total >= n_ranks, "mgpu_argmax_combine: bad arguments");
+    REQUIRE(pairs->bytes >= (size_t)n_ranks * 8, "mgpu_argmax_combine: pairs holds fewer than %d pairs", n_ranks);
+    REQUIRE(out->bytes >= 8, "mgpu_argmax_combine: out needs 8 bytes");
+    mgpu_device* d = const_cast<mgpu_device*>(cd);
+    DeviceGuard g(d->ordinal);
+    mgpu_event* ev = event_begin(d);
+    if (!cuda_ok(mgpu_k::argmax_combine(ctx_of(d), (const int*)pairs->ptr, n_ranks, n_total, (int*)out->ptr),
+                 "mgpu_argmax_combine")) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(d, ev);
+}
+
 // The reference's argmax_logits(device, logits, vocab_size): the index, or -1 on error.  Waits
 // for the device stream; the result goes through bytes 64..71 of the device's status block.
 int mgpu_argmax_logits(const mgpu_device* cd, mgpu_buf* logits, int vocab_size) {

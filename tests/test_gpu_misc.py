@@ -108,3 +108,30 @@ def test_argmax_logits_matches_reference_scan(dev, t):
     raw2 = raw.copy()
     raw2[9] = {mg.F16: 0x7E00, mg.BF16: 0x7FC0, mg.F32: 0x7FC00000}[t]
     assert mg.argmax_logits(dev, dev.array(raw2, t), n) == O.argmax_logits(raw2, t)[0] == 9
+
+
+@pytest.mark.parametrize("ranks", [2, 3, 8])
+def test_argmax_combine_column_shards(dev, ranks):
+    # the lm_head's logits column-sharded over `ranks` GPUs (emulated here on one): each shard's
+    # mgpu_argmax, the pairs in rank order, then mgpu_argmax_combine, against the reference's
+    # scan of the whole row; with a maximum tied across shards, and with nothing above -1e30
+    from mvlm_b200.shard import column_shard
+    n = 51203
+    for case in range(3):
+        x = O.normal(n, 300 + case, 3.0)
+        if case == 1:
+            x[[n - 5, 17]] = 40.0  # tied in the last and first shards: index 17 wins
+        if case == 2:
+            x[:] = -np.inf
+        raw = x.view(np.uint32).copy()
+        want_i, want_v = O.argmax_logits(raw, mg.F32)
+        logits = dev.array(raw, mg.F32)
+        pairs = dev.empty(2 * ranks, mg.F32)
+        for r in range(ranks):
+            a, b = column_shard(n, ranks, r)
+            mg.argmax(dev, logits.view(4 * a, 4 * (b - a)).set_format(mg.F32), b - a, pairs.view(8 * r, 8))
+        out = dev.empty(2, mg.F32)
+        mg.argmax_combine(dev, pairs, ranks, n, out).wait()
+        got = out.read(np.int32)
+        assert got[0] == want_i, (case, got[0], want_i)
+        assert np.float32(got[1:2].view(np.float32)[0]) == np.float32(want_v)
