@@ -171,6 +171,20 @@ int mgpu_dispatch_gemv_noalloc(const mgpu_device* dev, mgpu_buf* x, mgpu_buf* W_
  * y[1,N] = x[1,K] * dequant(W)^T with W packed GGUF blocks [N][K/32] of `type`. */
 mgpu_event* mgpu_gemv_q(const mgpu_device* dev, mgpu_buf* x, mgpu_buf* W, mgpu_buf* y, int N, int K,
                         int type);
+/* dispatch_rms_norm (src/engine/compute.h:38-40, compute.cpp:156-184 launching
+ * layernorm.cl:41-146): output[r] = input[r] * rsqrt(mean(input[r]^2) + eps) * weight for
+ * num_rows rows of hidden_size values, fp32 arithmetic.  input / output fp16 (the reference's
+ * types), bf16 or fp32, both of one type; weight fp16 / bf16 / fp32.  Returns the event. */
+mgpu_event* mgpu_dispatch_rms_norm(const mgpu_device* dev, mgpu_program program, mgpu_buf* input, mgpu_buf* output,
+                                   mgpu_buf* weight, int num_rows, int hidden_size, float eps);
+/* New: the RMSNorm in front of a decode projection fused into the quantised GEMV:
+ * y = x' * dequant(W)^T with x' = RMSNorm(x) computed as mgpu_dispatch_rms_norm does and rounded
+ * to x's type, which is what the reference's rms_norm writes and its next dispatch_gemv reads
+ * (moondream2.cpp:359-367, :455-463).  One launch, the norm in the GEMV's activation prologue,
+ * for 1024 <= K <= 8192 with K a power of two; other shapes normalise into the device's scratch
+ * and then run the GEMV (two launches; run those once before a graph capture). */
+mgpu_event* mgpu_gemv_q_rmsnorm(const mgpu_device* dev, mgpu_buf* x, mgpu_buf* norm_weight, float eps, mgpu_buf* W,
+                                mgpu_buf* y, int N, int K, int type);
 /* New: the GEMVs of a decode step in one launch.  Replaces a run of dependent dispatch_gemv
  * calls (src/models/moondream2.cpp:357-542 calls one per projection, waiting on each) when
  * the weights are GGUF Q4_0 / Q8_0.  A link is one GEMV y[1,N] = x[1,K] * dequant(W)^T with the

@@ -68,6 +68,8 @@ SIGNATURES = {
     "mgpu_dispatch_vision_proj": (_vp, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i]),
     "mgpu_dispatch_gemv_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i]),
     "mgpu_gemv_q": (_vp, [_vp, _vp, _vp, _vp, _i, _i, _i]),
+    "mgpu_dispatch_rms_norm": (_vp, [_vp, _vp, _vp, _vp, _vp, _i, _i, _f]),
+    "mgpu_gemv_q_rmsnorm": (_vp, [_vp, _vp, _vp, _f, _vp, _vp, _i, _i, _i]),
     "mgpu_gemv_chain_create": (_vp, [_vp, _vp, _i]),
     "mgpu_gemv_chain_run": (_vp, [_vp]),
     "mgpu_gemv_chain_run_timed": (_i, [_vp, _vp]),
@@ -396,6 +398,18 @@ def dispatch_gemv_noalloc(dev: Device, x: Buffer, W_img: Buffer, y: Buffer, N: i
     """mgpu_dispatch_gemv_noalloc: the [K][N] GEMV with its scratch in a fixed device array of
     the library (no allocation; N <= 262144; calls that overlap on the GPU race)."""
     _check(lib().mgpu_dispatch_gemv_noalloc(dev.h, x.h, W_img.h, y.h, N, K), "dispatch_gemv_noalloc")
+
+
+def dispatch_rms_norm(dev: Device, program, input: Buffer, output: Buffer, weight: Buffer, num_rows: int,
+                      hidden_size: int, eps: float) -> Event:
+    return _ev(lib().mgpu_dispatch_rms_norm(dev.h, None, input.h, output.h, weight.h, num_rows, hidden_size, eps),
+               "dispatch_rms_norm")
+
+
+def gemv_q_rmsnorm(dev: Device, x: Buffer, norm_weight: Buffer, eps: float, W: Buffer, y: Buffer, N: int, K: int,
+                   qtype: int) -> Event:
+    """y = RMSNorm(x) . dequant(W)^T with the norm in the GEMV's prologue (mgpu_gemv_q_rmsnorm)."""
+    return _ev(lib().mgpu_gemv_q_rmsnorm(dev.h, x.h, norm_weight.h, eps, W.h, y.h, N, K, qtype), "gemv_q_rmsnorm")
 
 
 def gemv_q(dev: Device, x: Buffer, W: Buffer, y: Buffer, N: int, K: int, qtype: int) -> Event:

@@ -42,6 +42,13 @@ constexpr uint32_t kGemvSmemBudget = 100 * 1024;  // per CTA: two CTAs share an 
 // 228 KB, and a 16-row chunk of K = 8192 Q4_0 rows (74 KB) fits beside its activations.
 constexpr uint32_t kGemvMmaSmemBudget = 110 * 1024;
 
+// RMSNorm applied to x by gemv_q_stream's prologue (gemv_q_norm).
+struct GemvNorm {
+    const void* gamma;
+    int gtype;
+    float eps;
+};
+
 struct GemvQArgs {
     const uint8_t* W;
     const void* x;
@@ -53,6 +60,9 @@ struct GemvQArgs {
     int stages;            // ring depth, 2..kGemvMaxStages
     int chunks_per_flush;  // chunks whose row partials are buffered before one reduction
     int* status;
+    const void* gamma;     // RMSNorm weight [K] of gtype applied to x first, or null
+    int gtype;
+    float eps;
 };
 
 template <int QT, int RPT, typename XT, typename YT>
@@ -129,7 +139,11 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     uint32_t* planes = reinterpret_cast<uint32_t*>(smem + (size_t)a.stages * a.stage_stride);
     float* bscale = reinterpret_cast<float*>(planes + 3 * (K / 4));
     float* bsum = bscale + nb;
-    prepare_x<XT>(reinterpret_cast<const XT*>(a.x), K, planes, bscale, bsum, tid, kConsumerThreads);
+    if (a.gamma)
+        prepare_x_norm<XT>(reinterpret_cast<const XT*>(a.x), a.gamma, a.gtype, a.eps, K, planes, bscale, bsum,
+                           bsum + nb, tid, kConsumerThreads);  // (the row partials' space, not in use yet)
+    else
+        prepare_x<XT>(reinterpret_cast<const XT*>(a.x), K, planes, bscale, bsum, tid, kConsumerThreads);
     named_barrier_sync(1, kConsumerThreads);
     const int col = tid % nb;  // block column owned by this thread for the whole launch
     XFixed xf;
@@ -718,13 +732,15 @@ struct GemvQLaunch {
     template <typename XT, typename YT>
     struct F {
         static cudaError_t run(const mgpu_k::LaunchCtx& c, const uint8_t* W, const void* x, void* y, int N,
-                               int K) {
+                               int K, const GemvNorm* norm) {
             constexpr int BB = QTraits<QT>::kBlockBytes;
             const int nb = K / 32;
             const size_t row_bytes = (size_t)nb * BB;
             const bool fast = (nb % 32 == 0) && nb <= 256 && (row_bytes % 16 == 0) &&
                               ((reinterpret_cast<uintptr_t>(W) & 15) == 0) &&
                               ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+            // the RMSNorm prologue is in the streaming dp4a kernel only
+            if (norm && !(fast && (kConsumerThreads % nb) == 0)) return cudaErrorNotSupported;
             if (!fast) {
                 const int blocks = (N * 32 + 255) / 256;
                 gemv_q_generic<QT, XT, YT><<<blocks, 256, 0, c.stream>>>(W, (const XT*)x, (YT*)y, N, nb, row_bytes);
@@ -813,6 +829,9 @@ struct GemvQLaunch {
             a.stages = stages;
             a.chunks_per_flush = (int)(part_floats(rpt) / ((size_t)RP * rpt * wpr));
             a.status = c.status;
+            a.gamma = norm ? norm->gamma : nullptr;
+            a.gtype = norm ? norm->gtype : 0;
+            a.eps = norm ? norm->eps : 0.0f;
             const size_t smem = (size_t)a.stages * a.stage_stride + x_bytes + 4 * part_floats(rpt);
             switch (rpt) {
                 case 8: return launch<8, XT, YT>(c, a, G, smem);
@@ -1023,10 +1042,23 @@ namespace mgpu_k {
 cudaError_t gemv_q(const LaunchCtx& c, int qtype, const uint8_t* W, int xtype, const void* x, int ytype,
                    void* y, int N, int K) {
     if (N <= 0) return cudaSuccess;
+    const GemvNorm* none = nullptr;
     if (qtype == MGPU_Q4_0)
-        return dispatch_xy<GemvQLaunch<MGPU_Q4_0>::F>(xtype, ytype, c, W, x, y, N, K);
+        return dispatch_xy<GemvQLaunch<MGPU_Q4_0>::F>(xtype, ytype, c, W, x, y, N, K, none);
     if (qtype == MGPU_Q8_0)
-        return dispatch_xy<GemvQLaunch<MGPU_Q8_0>::F>(xtype, ytype, c, W, x, y, N, K);
+        return dispatch_xy<GemvQLaunch<MGPU_Q8_0>::F>(xtype, ytype, c, W, x, y, N, K, none);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t gemv_q_norm(const LaunchCtx& c, int qtype, const uint8_t* W, int xtype, const void* x, int gtype,
+                        const void* gamma, float eps, int ytype, void* y, int N, int K) {
+    if (N <= 0) return cudaSuccess;
+    GemvNorm nrm{gamma, gtype, eps};
+    const GemvNorm* p = &nrm;
+    if (qtype == MGPU_Q4_0)
+        return dispatch_xy<GemvQLaunch<MGPU_Q4_0>::F>(xtype, ytype, c, W, x, y, N, K, p);
+    if (qtype == MGPU_Q8_0)
+        return dispatch_xy<GemvQLaunch<MGPU_Q8_0>::F>(xtype, ytype, c, W, x, y, N, K, p);
     return cudaErrorInvalidValue;
 }
 

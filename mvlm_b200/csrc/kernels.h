@@ -44,6 +44,11 @@ size_t gemv_kn_scratch_bytes(int N, int K, int sm_count, int* splits_out);
 cudaError_t gemv_kn_noalloc(const LaunchCtx& c, int wtype, const void* W, int64_t ldw, int xtype, const void* x,
                             int ytype, void* y, int N, int K);
 size_t gemv_kn_noalloc_max_n();
+// gemv_q with x replaced by RMSNorm(x) = x * rsqrt(mean(x^2) + eps) * gamma (rounded to x's type)
+// in the kernel's prologue.  cudaErrorNotSupported (nothing launched) for shapes the streaming
+// kernel does not take; the caller then normalises first (rms_norm) and runs gemv_q.
+cudaError_t gemv_q_norm(const LaunchCtx& c, int qtype, const uint8_t* W, int xtype, const void* x, int gtype,
+                        const void* gamma, float eps, int ytype, void* y, int N, int K);
 
 // ------------------------------------------------------- GEMV chain (chain.cu) ------
 // One GEMV of a chain, as the kernel reads it from device memory (64 bytes).
@@ -84,6 +89,9 @@ cudaError_t convert(const LaunchCtx& c, int itype, const void* in, int otype, vo
 cudaError_t selftest_bounded_wait(const LaunchCtx& c, uint64_t limit_ns);
 // out[0] = argmax index, out[1] = the value (fp32 bits), reference argmax semantics; n >= 1.
 cudaError_t argmax(const LaunchCtx& c, int type, const void* logits, int n, int* out);
+// out[r][:] = RMSNorm(in[r][:]) for rows r < rows of H values (in / out of `type`, w of wtype).
+cudaError_t rms_norm(const LaunchCtx& c, int type, const void* in, void* out, int wtype, const void* w, int rows,
+                     int H, float eps);
 // The global first maximum of a row column-sharded over n_ranks, from the ranks' argmax pairs.
 cudaError_t argmax_combine(const LaunchCtx& c, const int* pairs, int n_ranks, int n_total, int* out);
 // patches[p][k] (k < kpad, zero for k >= C*ph*pw) from image [C][H][W]; same element type

@@ -142,6 +142,94 @@ __device__ __forceinline__ void prepare_x_n(const XT* __restrict__ x, int K, uin
         if (it < iters) convert_x_word(v[it], it * nthreads + tid, words, planes, bscale, bsum, (tid & 7) == 0);
 }
 
+// Four consecutive values of a float-typed vector (f32 / f16 / bf16) at word w, as fp32.
+template <typename T>
+__device__ __forceinline__ void load_word4(const T* __restrict__ p, int w, float (&v)[4]) {
+    if constexpr (sizeof(T) == 4) {
+        const float4 f = __ldg(reinterpret_cast<const float4*>(p) + w);
+        v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    } else {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(p) + w);
+        const uint32_t uu[2] = {u.x, u.y};
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            T lo, hi;
+            uint16_t l16 = (uint16_t)(uu[j] & 0xFFFF), h16 = (uint16_t)(uu[j] >> 16);
+            memcpy(&lo, &l16, 2);
+            memcpy(&hi, &h16, 2);
+            v[2 * j] = to_f32<T>(lo);
+            v[2 * j + 1] = to_f32<T>(hi);
+        }
+    }
+}
+__device__ __forceinline__ void load_word4_typed(int type, const void* p, int w, float (&v)[4]) {
+    if (type == MGPU_F32) load_word4(reinterpret_cast<const float*>(p), w, v);
+    else if (type == MGPU_F16) load_word4(reinterpret_cast<const __half*>(p), w, v);
+    else load_word4(reinterpret_cast<const __nv_bfloat16*>(p), w, v);
+}
+
+// RMSNorm's scale rsqrt(mean(x^2) + eps) (src/kernels/layernorm.cl:41-146), K values held by
+// `nthreads` threads (a multiple of 32) as 4-element words it * nthreads + tid, from each
+// thread's partial sum of squares `ss` (its words in order, fmaf per value): a xor butterfly in
+// each warp, then the warps' sums added in warp order through red[nthreads / 32], shared with
+// named barrier 1.  The standalone kernel and the GEMV prologue both call this with 256 threads,
+// so their normalised vectors have the same bits.
+__device__ __forceinline__ float rms_scale(float ss, float* red, int tid, int nthreads, int K, float eps) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    named_barrier_sync(1, nthreads);
+    float total = 0.0f;
+    for (int w = 0; w < nthreads / 32; ++w) total += red[w];
+    return rsqrtf(total / (float)K + eps);
+}
+
+// prepare_x with the RMSNorm of x in front: x_k * rsqrt(mean(x^2) + eps) * gamma_k, rounded to
+// x's own type, as the reference's rms_norm writes its output in the input's type before the
+// projection reads it; then the fixed-point conversion.  red: nthreads / 32 floats of scratch.
+template <typename XT, int ITERS, bool EXACT>
+__device__ __forceinline__ void prepare_x_norm_n(const XT* __restrict__ x, const void* gamma, int gtype, float eps,
+                                                 int K, uint32_t* planes, float* bscale, float* bsum, float* red,
+                                                 int tid, int nthreads) {
+    constexpr int kMaxIter = ITERS;
+    const int words = K / 4;
+    const int iters = EXACT ? ITERS : words / nthreads;
+    float v[kMaxIter][4];
+    float ss = 0.0f;
+#pragma unroll
+    for (int it = 0; it < kMaxIter; ++it)
+        if (it < iters) load_word4(x, it * nthreads + tid, v[it]);
+#pragma unroll
+    for (int it = 0; it < kMaxIter; ++it)
+        if (it < iters)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ss = fmaf(v[it][j], v[it][j], ss);
+    const float r = rms_scale(ss, red, tid, nthreads, K, eps);
+#pragma unroll
+    for (int it = 0; it < kMaxIter; ++it) {
+        if (it < iters) {
+            float g[4];
+            load_word4_typed(gtype, gamma, it * nthreads + tid, g);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[it][j] = to_f32<XT>(from_f32<XT>(v[it][j] * r * g[j]));
+            convert_x_word(v[it], it * nthreads + tid, words, planes, bscale, bsum, (tid & 7) == 0);
+        }
+    }
+}
+
+template <typename XT>
+__device__ __forceinline__ void prepare_x_norm(const XT* __restrict__ x, const void* gamma, int gtype, float eps,
+                                               int K, uint32_t* planes, float* bscale, float* bsum, float* red,
+                                               int tid, int nthreads) {
+    switch (K >> 10) {
+        case 1: prepare_x_norm_n<XT, 1, true>(x, gamma, gtype, eps, K, planes, bscale, bsum, red, tid, nthreads); break;
+        case 2: prepare_x_norm_n<XT, 2, true>(x, gamma, gtype, eps, K, planes, bscale, bsum, red, tid, nthreads); break;
+        case 4: prepare_x_norm_n<XT, 4, true>(x, gamma, gtype, eps, K, planes, bscale, bsum, red, tid, nthreads); break;
+        case 8: prepare_x_norm_n<XT, 8, true>(x, gamma, gtype, eps, K, planes, bscale, bsum, red, tid, nthreads); break;
+        default: prepare_x_norm_n<XT, 8, false>(x, gamma, gtype, eps, K, planes, bscale, bsum, red, tid, nthreads); break;
+    }
+}
+
 template <typename XT>
 __device__ __forceinline__ void prepare_x(const XT* __restrict__ x, int K, uint32_t* planes, float* bscale,
                                           float* bsum, int tid, int nthreads) {

@@ -718,6 +718,67 @@ mgpu_event* mgpu_gemv_q(const mgpu_device* d, mgpu_buf* x, mgpu_buf* W, mgpu_buf
     return mgpu_dispatch_gemv(d, nullptr, x, W, y, N, K);
 }
 
+mgpu_event* mgpu_dispatch_rms_norm(const mgpu_device* cd, mgpu_program, mgpu_buf* input, mgpu_buf* output,
+                                   mgpu_buf* weight, int num_rows, int hidden_size, float eps) {
+    API_ENTRY();
+    REQUIRE(cd && input && output && weight, "dispatch_rms_norm: null argument");
+    REQUIRE(num_rows > 0 && hidden_size > 0, "dispatch_rms_norm: num_rows=%d hidden_size=%d", num_rows, hidden_size);
+    REQUIRE(is_float_type(input->type) && output->type == input->type,
+            "dispatch_rms_norm: input and output must be f16 / bf16 / f32 of one type");
+    REQUIRE(is_float_type(weight->type) && weight->bytes >= (size_t)hidden_size * elem_size(weight->type),
+            "dispatch_rms_norm: weight must hold hidden_size float values");
+    const size_t bytes = (size_t)num_rows * hidden_size * elem_size(input->type);
+    REQUIRE(input->bytes >= bytes && output->bytes >= bytes, "dispatch_rms_norm: buffers smaller than rows x hidden");
+    mgpu_device* d = const_cast<mgpu_device*>(cd);
+    DeviceGuard g(d->ordinal);
+    mgpu_event* ev = event_begin(d);
+    if (!cuda_ok(mgpu_k::rms_norm(ctx_of(d), input->type, input->ptr, output->ptr, weight->type, weight->ptr, num_rows,
+                                  hidden_size, eps), "dispatch_rms_norm")) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(d, ev);
+}
+
+mgpu_event* mgpu_gemv_q_rmsnorm(const mgpu_device* cd, mgpu_buf* x, mgpu_buf* gamma, float eps, mgpu_buf* W,
+                                mgpu_buf* y, int N, int K, int type) {
+    API_ENTRY();
+    REQUIRE(cd && x && gamma && W && y, "gemv_q_rmsnorm: null argument");
+    REQUIRE(N > 0 && K > 0 && K % 32 == 0, "gemv_q_rmsnorm: N=%d K=%d", N, K);
+    REQUIRE(is_quant_type(type) && (W->type == type || W->type == MGPU_F16), "gemv_q_rmsnorm: W must be Q4_0 / Q8_0");
+    REQUIRE(is_float_type(x->type) && is_float_type(y->type), "gemv_q_rmsnorm: x and y must be f32 / f16 / bf16");
+    REQUIRE(is_float_type(gamma->type) && gamma->bytes >= (size_t)K * elem_size(gamma->type),
+            "gemv_q_rmsnorm: norm_weight must hold K float values");
+    REQUIRE(x->bytes >= (size_t)K * elem_size(x->type), "gemv_q_rmsnorm: x holds fewer than K=%d values", K);
+    REQUIRE(y->bytes >= (size_t)N * elem_size(y->type), "gemv_q_rmsnorm: y holds fewer than N=%d values", N);
+    const size_t rb = quant_row_bytes(type, K);
+    REQUIRE(W->bytes >= (size_t)N * rb, "gemv_q_rmsnorm: W holds fewer than N=%d rows", N);
+    W->type = type;
+    W->layout = MGPU_LAYOUT_NK;
+    mgpu_device* d = const_cast<mgpu_device*>(cd);
+    DeviceGuard g(d->ordinal);
+    mgpu_event* ev = event_begin(d);
+    cudaError_t e = mgpu_k::gemv_q_norm(ctx_of(d), type, (const uint8_t*)W->ptr, x->type, x->ptr, gamma->type,
+                                        gamma->ptr, eps, y->type, y->ptr, N, K);
+    if (e == cudaErrorNotSupported) {
+        // normalise into the scratch arena, then the plain GEMV (stream-ordered)
+        const size_t xb = ((size_t)K * elem_size(x->type) + 255) & ~(size_t)255;
+        if (!ensure_workspace(d, kScratchOffset + xb)) {
+            if (ev) d->event_pool.push_back(ev);
+            return nullptr;
+        }
+        void* xn = (char*)d->workspace + kScratchOffset;
+        e = mgpu_k::rms_norm(ctx_of(d), x->type, x->ptr, xn, gamma->type, gamma->ptr, 1, K, eps);
+        if (e == cudaSuccess)
+            e = mgpu_k::gemv_q(ctx_of(d), type, (const uint8_t*)W->ptr, x->type, xn, y->type, y->ptr, N, K);
+    }
+    if (!cuda_ok(e, "gemv_q_rmsnorm")) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(d, ev);
+}
+
 // ------------------------------------------------------------------ GEMV chain -------
 struct mgpu_gemv_chain {
     mgpu_device* dev;

@@ -66,6 +66,7 @@ def lib():
         L.ora_activate.restype = ctypes.c_float
         L.ora_activate_n.argtypes = [vp, sz, i32]
         L.ora_silu_gate_n.argtypes = [vp, vp, vp, sz]
+        L.ora_rms_norm.argtypes = [vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_float]
         for n in ("ora_f32_to_f16_n", "ora_f16_to_f32_n", "ora_f32_to_bf16_n", "ora_bf16_to_f32_n"):
             getattr(L, n).argtypes = [vp, vp, sz]
         L.ora_type_size.argtypes = [i32]
@@ -258,6 +259,14 @@ def unfused_epilogue(acc, bias, act: int, resid, M: int, N: int, ctype: int):
     if resid is not None:
         c = round_to(c + np.ascontiguousarray(resid, np.float32).reshape(M * N), ctype)
     return c
+
+
+def rms_norm(x, w, rows: int, hidden: int, eps: float, otype: int):
+    """layernorm.cl's rms_norm on fp32 values (x already in its storage type), rounded to otype."""
+    out = np.empty(rows * hidden, np.float32)
+    lib().ora_rms_norm(_p(np.ascontiguousarray(x, np.float32)), _p(np.ascontiguousarray(w, np.float32)), _p(out),
+                       rows, hidden, float(eps))
+    return round_to(out, otype)
 
 
 def unfused_silu_gate(gate_acc, up, ctype: int):

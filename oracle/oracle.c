@@ -316,6 +316,20 @@ void ora_activate_n(float* x, size_t n, int act) {
     for (size_t i = 0; i < n; ++i) x[i] = ora_activate(x[i], act);
 }
 
+/* rms_norm (src/kernels/layernorm.cl:41-146), one row as its work-group computes it: the sum of
+ * squares in fp32 with fma, rms_scale = rsqrt(sum / hidden + eps) (native_rsqrt taken as
+ * 1 / sqrt), then val * rms_scale * w in fp32 in that order; the caller rounds to the output
+ * type (the kernel stores half). */
+void ora_rms_norm(const float* x, const float* w, float* out, int rows, int hidden, float eps) {
+    for (int r = 0; r < rows; ++r) {
+        const float* xr = x + (size_t)r * hidden;
+        float ss = 0.0f;
+        for (int i = 0; i < hidden; ++i) ss = fmaf(xr[i], xr[i], ss);
+        const float scale = 1.0f / sqrtf(ss / (float)hidden + eps);
+        for (int i = 0; i < hidden; ++i) out[(size_t)r * hidden + i] = xr[i] * scale * w[i];
+    }
+}
+
 /* silu_gate_multiply (activations.cl:219-265), scalar tail: gf * (1 / (1 + exp(-gf))) * uf. */
 void ora_silu_gate_n(const float* gate, const float* up, float* out, size_t n) {
     for (size_t i = 0; i < n; ++i) {

@@ -88,4 +88,5 @@ void ora_set_threads(int n);
 #ifdef __cplusplus
 }
 #endif
+void ora_rms_norm(const float* x, const float* w, float* out, int rows, int hidden, float eps);
 #endif

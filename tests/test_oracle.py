@@ -218,3 +218,15 @@ def test_silu_gate_restatement():
     u = np.float32([2.0, 5.0, -1.0, 0.5])
     want = O.round_to(O.activate(g, 2) * u, 1)
     assert np.allclose(O.unfused_silu_gate(g, u, 1), want, rtol=1e-3, atol=0)
+
+
+def test_rms_norm_restatement_matches_float64():
+    # layernorm.cl's rms_norm: x * rsqrt(mean(x^2) + eps) * w, fp32 arithmetic; checked against
+    # the same formula in float64 (fp32 output, so only fp32 rounding separates them)
+    rows, H, eps = 3, 1000, 1e-5
+    x = O.normal(rows * H, 8, 2.0)
+    w = O.normal(H, 9, 0.5)
+    got = O.rms_norm(x, w, rows, H, eps, O.F32).reshape(rows, H)
+    xd = x.astype(np.float64).reshape(rows, H)
+    ref = xd / np.sqrt(np.mean(xd * xd, axis=1, keepdims=True) + eps) * w.astype(np.float64)
+    assert np.max(np.abs(got - ref)) <= 1e-5 * np.max(np.abs(ref))
