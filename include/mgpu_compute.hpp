@@ -9,8 +9,10 @@
 //   if (ev) { clWaitForEvents(1, &ev); clReleaseEvent(ev); }
 //
 // cl_mem / cl_event / cl_program are aliases of the C ABI handles; the OpenCL helper calls
-// those call sites use on them (clWaitForEvents, clReleaseEvent, clReleaseMemObject,
-// clFinish) are provided as inline shims.  Header-only.
+// those call sites use on them (clWaitForEvents, clReleaseEvent, clReleaseMemObject) are
+// provided as inline shims.  Header-only: for code written against this header.  To build the
+// reference's own engine headers and model code unchanged, use include/cl_compat/CL/cl.h with
+// mvlm_b200/engine/engine_cuda.cpp instead (DeviceInfo keeps its OpenCL fields there).
 #pragma once
 
 #include <cstddef>

@@ -116,6 +116,9 @@ int mgpu_buf_read(const mgpu_buf* buf, size_t offset, void* dst, size_t bytes);
  * should be pinned (mgpu_host_alloc) for the copy to be asynchronous. */
 int mgpu_buf_write_async(mgpu_buf* buf, size_t offset, const void* src, size_t bytes);
 int mgpu_buf_read_async(const mgpu_buf* buf, size_t offset, void* dst, size_t bytes);
+/* Stream-ordered device-to-device copy between two buffers of one device
+ * (clEnqueueCopyBuffer, used by kv_cache_append, src/models/moondream2.cpp:302-314). */
+int mgpu_buf_copy_async(mgpu_buf* dst, size_t dst_offset, const mgpu_buf* src, size_t src_offset, size_t bytes);
 void* mgpu_host_alloc(size_t bytes);
 void mgpu_host_free(void* p);
 void mgpu_release_buffer(mgpu_buf* buf);

@@ -56,6 +56,7 @@ SIGNATURES = {
     "mgpu_buf_read": (_i, [_vp, _sz, _vp, _sz]),
     "mgpu_buf_write_async": (_i, [_vp, _sz, _vp, _sz]),
     "mgpu_buf_read_async": (_i, [_vp, _sz, _vp, _sz]),
+    "mgpu_buf_copy_async": (_i, [_vp, _sz, _vp, _sz, _sz]),
     "mgpu_host_alloc": (_vp, [_sz]),
     "mgpu_host_free": (None, [_vp]),
     "mgpu_release_buffer": (None, [_vp]),

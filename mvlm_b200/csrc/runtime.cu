@@ -554,6 +554,19 @@ int mgpu_buf_read_async(const mgpu_buf* b, size_t off, void* dst, size_t bytes) 
     return MGPU_OK;
 }
 
+int mgpu_buf_copy_async(mgpu_buf* dst, size_t dst_offset, const mgpu_buf* src, size_t src_offset, size_t bytes) {
+    if (!dst || !src || src->dev != dst->dev || dst_offset + bytes > dst->bytes || src_offset + bytes > src->bytes) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_buf_copy_async: bad arguments");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    if (bytes == 0) return MGPU_OK;
+    DeviceGuard g(dst->dev->ordinal);
+    if (!cuda_ok(cudaMemcpyAsync((char*)dst->ptr + dst_offset, (const char*)src->ptr + src_offset, bytes,
+                                 cudaMemcpyDeviceToDevice, dst->dev->stream), "mgpu_buf_copy_async"))
+        return t_err;
+    return MGPU_OK;
+}
+
 void* mgpu_host_alloc(size_t bytes) {
     void* p = nullptr;
     if (!cuda_ok(cudaMallocHost(&p, bytes), "cudaMallocHost")) return nullptr;

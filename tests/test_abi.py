@@ -102,3 +102,20 @@ def test_no_device_is_an_error_not_a_crash():
     assert code != mg.OK and msg
     with pytest.raises(mg.MgpuError):
         mg.Device(0)
+
+
+def test_engine_dropin_harness_links():
+    # oracle/_ref/libref_dropin.so: the reference's moondream2_forward (extracted unmodified from
+    # src/models/moondream2.cpp) compiled with the reference's headers over include/cl_compat and
+    # linked to libmgpu through mvlm_b200/engine/engine_cuda.cpp; the GPU run is
+    # tests/test_gpu_dropin.py
+    ref = os.path.join(ROOT, "oracle", "_ref")
+    lib_path = os.path.join(ref, "libref_dropin.so")
+    if not os.path.exists(lib_path):
+        pytest.skip("built only where the reference checkout is present")
+    with open(os.path.join(ref, "moondream2_forward.inc")) as f:
+        text = f.read()
+    assert "cl_mem moondream2_forward(Moondream2Model* model" in text and "kv_cache_append" in text
+    mg.lib()  # libmgpu first, as the harness links it
+    L = ctypes.CDLL(lib_path)
+    assert hasattr(L, "dropin_forward_decode")
