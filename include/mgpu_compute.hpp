@@ -2,8 +2,8 @@
 //
 // Same namespace, function names, argument order and return conventions as the reference's
 // src/engine/compute.h:16-33, :101-105, :128-131, memory.h:16-19, device.h:58 and
-// profiler.h:16, so that call sites such as moondream2_forward (src/models/moondream2.cpp:
-// 370-540) and moondream2_encode_vision (:791-918) compile unchanged against it:
+// profiler.h:16, so that its dispatch call sites (the GEMV / GEMM calls of moondream2_forward,
+// src/models/moondream2.cpp:370-540, and of moondream2_encode_vision, :791-918) read the same:
 //
 //   cl_event ev = dispatch_gemv(device, model->gemm_program, x, lw->q_proj_weight, y, N, K);
 //   if (ev) { clWaitForEvents(1, &ev); clReleaseEvent(ev); }
