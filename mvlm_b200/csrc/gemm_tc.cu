@@ -1110,9 +1110,17 @@ size_t gemm_split_bytes(const LaunchCtx& c, const GemmOperand& A, const GemmOper
     return p.splits > 1 && p.csplit == 1 ? (size_t)p.splits * M * N * sizeof(float) : 0;
 }
 
-bool make_tensor_map_u16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,
-                         int box_rows) {
-    return make_map_plain(m, ptr, rows, cols, ld, box_cols, box_rows);
+bool make_tensor_map_u16_3d(CUtensorMap* m, const void* ptr, const int64_t dims[3], const int64_t strides[2],
+                            const int box[3]) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    cuuint64_t d[3] = {(cuuint64_t)dims[0], (cuuint64_t)dims[1], (cuuint64_t)dims[2]};
+    cuuint64_t st[2] = {(cuuint64_t)strides[0], (cuuint64_t)strides[1]};
+    cuuint32_t b[3] = {(cuuint32_t)box[0], (cuuint32_t)box[1], (cuuint32_t)box[2]};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(ptr), d, st, b, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,

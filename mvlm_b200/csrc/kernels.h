@@ -129,10 +129,10 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
 bool skinny_ok(const GemmOperand& A, const GemmOperand& B, int M, int N, int K);
 cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
                            const void* bias, int bias_type, int M, int N, int K, const Epilogue& epi = Epilogue());
-// A 2-D TMA map over 16-bit units without swizzle: `rows` x `cols`, row pitch `ld` units, box
-// {box_cols, box_rows} (gemm_tc.cu).
-bool make_tensor_map_u16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols,
-                         int box_rows);
+// A 3-D TMA map over 16-bit units without swizzle: extents dims[0] (contiguous), dims[1],
+// dims[2]; byte strides of dims 1 and 2 (multiples of 16, in any order); box {box[0..2]}.
+bool make_tensor_map_u16_3d(CUtensorMap* m, const void* ptr, const int64_t dims[3], const int64_t strides[2],
+                            const int box[3]);
 // Why a GEMM request cannot run (nullptr when it can).
 const char* gemm_check(const GemmOperand& A, const GemmOperand& B, const GemmOperand& C, int M, int N, int K);
 

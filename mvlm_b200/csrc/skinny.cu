@@ -5,25 +5,32 @@
 // The shape is the decode GEMV's with a few activation rows, so the kernel is built like it:
 // each CTA owns an even share of W's rows and streams them once from HBM, while the weight
 // decode happens in registers straight into tensor-core fragments.
-//   * A producer thread stages, per 256-k slice, the CTA's packed rows (a 2-D TMA box over the
-//     rows' 16-bit units: 144 bytes = 8 blocks per row) and the activation rows of that slice
-//     (two 2-D TMA boxes of 136 x S elements: each row lands at a 272-byte pitch, which puts a
-//     fragment's 8 rows on distinct banks; rows past S and columns past K read as zeros).
-//     Three TMA instructions per stage: one small bulk copy per activation row was measured to
-//     cost ~50 ns of issue each, which serialised the ring.  Weights are never written by the
-//     preceding kernel, so the first slices stream before griddepcontrol.wait; activations
-//     after it.
-//   * A stage holds 1, 2 or 4 such 256-k sub-slices, so that each warp has several independent
-//     blocks to decode per stage (one block per stage left a warp with a single serial chain).
-//   * Eight consumer warps: warp w takes 16-row group (w % RG) and a contiguous run of the
-//     stage's blocks (the 8/RG warps of a row group split K).  Every warp consumes every
-//     stage, in order, so a warp's parity wait on a slot is never more than one phase ahead.  A lane turns its two quant
-//     bytes per row and block into bf16 / fp16 pairs: nibble | 0x4300 (bf16 128 + q) or
-//     | 0x6400 (fp16 1024 + q), minus 136 / 1032 gives q - 8 exactly, times the block's d.
-//     Those are the A fragments of mma.sync.m16n8k16 (weights as M = 16 rows), the staged
-//     activations the B fragments (sequences as N = 8 per tile), fp32 accumulation over all K.
-//   * After the last slice of a row chunk the warps' partial sums meet in shared memory and
-//     the CTA writes C (+ bias) for its rows.
+//   * A producer thread stages the CTA's rows in 256-k slices (8 blocks = 144 bytes per row),
+//     a stage holding 1..8 consecutive slices, with two TMA instructions per stage: one 3-D
+//     box of the packed rows, viewed as [slice][row][72 16-bit units], so that each slice's
+//     rows land at a 144-byte pitch (a fragment's 8 rows on distinct banks), and one 3-D box
+//     of the activations, viewed as [128-element chunk][sequence][element] with 136-element
+//     boxes, so that each sequence's chunk lands at a 272-byte pitch (rows past S, rows past N
+//     and the 8 elements past a chunk read as zeros).  TMA issue costs ~50-75 ns per
+//     instruction from the one producer thread; with one box per slice and operand it was the
+//     bound of the K = 8192 shapes.  Weights are never written by the preceding kernel, so the
+//     first stages' weights stream before griddepcontrol.wait; activations after it.
+//   * A stage holds as many slices as give each warp up to 8 (row group, block) units (4 with
+//     16 sequences), so that it has several independent chains per stage.
+//   * Eight consumer warps split K: warp w takes block w of every 256-k sub-slice, for all the
+//     chunk's 16-row groups, so the activation fragments it loads for a block serve every row
+//     group.  The MMA is mma.sync.m16n8k16 with the weights as M (16 rows) and the sequences
+//     as N (8 per tile), fp32 accumulation.  Its 16 k positions are taken in a permuted order
+//     (k 2t, 2t+1 <-> block elements 4t, 4t+2; k 2t+8, 2t+9 <-> 4t+1, 4t+3; the second k16 step
+//     the same + 16): the sum over k does not depend on the order, and in this one lane t's A
+//     fragments are the nibbles of quant word t (bytes 4t..4t+3, which hold elements 4t..4t+3
+//     low and 16+4t..19+4t high) in place, one mask-and-or per register:
+//     nibble | 0x4300 (bf16 128 + q) or | 0x6400 (fp16 1024 + q), minus 136 / 1032 = q - 8
+//     exactly.  The B fragments are the matching pairs of staged activations (one byte permute
+//     per register).  A block's two MMAs start from zero, so their result is the exact
+//     sum of (q - 8) x over the block, which is scaled by the block's fp16 d in fp32.
+//   * After the last slice of a row chunk the warps' partial sums meet in shared memory, are
+//     added in warp order (deterministic), and the CTA writes C (+ bias, epilogue) for its rows.
 // (Larger batches are tensor-bound enough for the tcgen05 GEMM, which takes them.)
 #include <cuda.h>
 
@@ -53,9 +60,9 @@ struct SkinnyArgs {
     mgpu_k::Epilogue epi;  // activation / residual after the bias
     int S, N, K;
     int stages;
-    uint32_t sub_bytes;    // one sub-slice: TR x 144 weight bytes, then 2 x 8 NT x 272 activation bytes
-    uint32_t stage_bytes;  // subs x sub_bytes, rounded up to 1 KB
-    uint32_t x_offset;     // offset of the activation rows inside a sub-slice
+    uint32_t stage_bytes;  // weights [SUBS][TR][144 B], then activations [2 SUBS][8 NT][272 B], 1 KB aligned
+    uint32_t x_offset;     // offset of the activations inside a stage (128-byte aligned)
+    uint32_t tx_bytes;     // bytes the two copies of a stage deliver
     int* status;
 };
 
@@ -69,18 +76,15 @@ template <> struct Magic<__half> {
     static constexpr float kSub = 1032.0f;
 };
 
-template <typename T>
-__device__ __forceinline__ uint32_t sub_mul2(uint32_t v, uint32_t sub2, uint32_t d2) {
+// (q - 8) of the two 4-bit fields at bit SH of each 16-bit half of w, as a T pair (exact).
+template <typename T, int SH>
+__device__ __forceinline__ uint32_t nib_pair(uint32_t w, uint32_t sub2) {
+    const uint32_t v = ((w >> SH) & 0x000F000Fu) | Magic<T>::kOr;
     uint32_t r;
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        asm("{\n .reg .b32 t;\n sub.rn.bf16x2 t, %1, %2;\n mul.rn.bf16x2 %0, t, %3;\n}\n"
-            : "=r"(r)
-            : "r"(v), "r"(sub2), "r"(d2));
-    } else {
-        asm("{\n .reg .b32 t;\n sub.rn.f16x2 t, %1, %2;\n mul.rn.f16x2 %0, t, %3;\n}\n"
-            : "=r"(r)
-            : "r"(v), "r"(sub2), "r"(d2));
-    }
+    if constexpr (std::is_same<T, __nv_bfloat16>::value)
+        asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(sub2));
+    else
+        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(sub2));
     return r;
 }
 
@@ -127,12 +131,11 @@ __device__ __forceinline__ void store_value(void* C, int type, size_t idx, float
 // NT = 8-sequence tiles per CTA (S per CTA <= 8 NT); RG = 16-row groups per chunk; SUBS =
 // 256-k sub-slices per stage.
 template <int NT, int RG, int SUBS, typename T>
-__global__ void __launch_bounds__(kSkThreads, 1)
+__global__ void __launch_bounds__(kSkThreads, 2)
     gemm_q4_skinny(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, SkinnyArgs a) {
     constexpr int TR = 16 * RG;         // rows per chunk
-    constexpr int WPG = 8 / RG;         // warps per row group (split K)
-    constexpr int BPW = RG * SUBS;      // blocks of a stage per warp
     constexpr int SP = 8 * NT;          // sequences per CTA
+    constexpr int RP = TR + 4;          // partial-sum row pitch: a warp's 32 writes on distinct banks
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     __shared__ __align__(8) uint64_t full_bar[kSkMaxStages];
@@ -151,7 +154,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     const int nchunks = (r1 - r0 + TR - 1) / TR;
     const int nslices = a.K / (kSkSlice * SUBS);  // stages per chunk
     const int total = nchunks * nslices;
-    float* red = reinterpret_cast<float*>(smem + (size_t)a.stages * a.stage_bytes);  // [WPG][TR][SP]
+    float* red = reinterpret_cast<float*>(smem + (size_t)a.stages * a.stage_bytes);  // [8 warps][SP][RP]
 
     if (tid == 0) {
         for (int s = 0; s < a.stages; ++s) {
@@ -170,21 +173,16 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         if (lane == 0) {
             prefetch_tensormap(&tmW);
             prefetch_tensormap(&tmX);
-            const uint32_t bytes = (uint32_t)SUBS * a.sub_bytes;
+            const uint32_t bytes = a.tx_bytes;
+            // one copy per stage for each operand: W's box is [SUBS slices][TR rows][72 units],
+            // the activations' [2 SUBS chunks of 128][8 NT sequences][136 elements]
             auto w_load = [&](int it, int s) {
                 const int c = it / nslices, ks = it % nslices;
-                for (int u = 0; u < SUBS; ++u)
-                    tma_load_2d(smem + (size_t)s * a.stage_bytes + (size_t)u * a.sub_bytes, &tmW,
-                                (ks * SUBS + u) * (kSkWRowBytes / 2), r0 + c * TR, &full_bar[s]);
+                tma_load_3d(smem + (size_t)s * a.stage_bytes, &tmW, 0, r0 + c * TR, ks * SUBS, &full_bar[s]);
             };
             auto x_load = [&](int it, int s) {
                 const int ks = it % nslices;
-                for (int u = 0; u < SUBS; ++u) {
-                    uint8_t* xdst = smem + (size_t)s * a.stage_bytes + (size_t)u * a.sub_bytes + a.x_offset;
-                    const int k0 = (ks * SUBS + u) * kSkSlice;
-                    tma_load_2d(xdst, &tmX, k0, seq0, &full_bar[s]);
-                    tma_load_2d(xdst + SP * kSkXPitch, &tmX, k0 + 128, seq0, &full_bar[s]);
-                }
+                tma_load_3d(smem + (size_t)s * a.stage_bytes + a.x_offset, &tmX, 0, seq0, 2 * ks * SUBS, &full_bar[s]);
             };
             // weights of the first stages before the dependency wait, activations after it
             const int pre = min(a.stages, total);
@@ -215,60 +213,78 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         return;
     }
 
-    // ---- consumers ----
+    // ---- consumers: warp w takes block w of every sub-slice, for every row group ----
     const int g = lane >> 2, t = lane & 3;
-    const int rg = warp % RG, kw = warp / RG;
+    const int bw = warp;                  // block within a sub-slice (0..7)
+    const bool even_block = (bw & 1) == 0;  // quants at 2 mod 4: realign with a byte permute
     const uint32_t sub2 = pack_pair<T>(Magic<T>::kSub);
+    // this lane's activation words inside a sub-slice: chunk bw / 4, sequence 8j + g, elements
+    // 32 (bw % 4) + 4t .. + 3 (and + 16)
+    const uint32_t x_lane = a.x_offset + (uint32_t)(bw >> 2) * (SP * kSkXPitch) + (uint32_t)g * kSkXPitch +
+                            (uint32_t)(bw & 3) * 64 + 8u * t;
+    // this lane's weight bytes inside a sub-slice: row g of a group, block bw (even: the aligned
+    // word at 4t before the quant word; odd: the quant word t itself)
+    const uint32_t w_lane = (uint32_t)g * kSkWRowBytes + (uint32_t)bw * 18 + (even_block ? 4u * t : 2u + 4u * t);
+    const uint32_t d_lane = (uint32_t)g * kSkWRowBytes + (uint32_t)bw * 18;
     int s = 0;
     uint32_t ph = 0;
     for (int c = 0; c < nchunks; ++c) {
-        float acc[NT][4];
+        float acc[RG][NT][4];
 #pragma unroll
-        for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+        for (int r = 0; r < RG; ++r)
+#pragma unroll
+            for (int j = 0; j < NT; ++j) acc[r][j][0] = acc[r][j][1] = acc[r][j][2] = acc[r][j][3] = 0.0f;
         for (int ks = 0; ks < nslices; ++ks) {
             if (!mbar_wait(&full_bar[s], ph, a.status)) return;
             const uint8_t* stg = smem + (size_t)s * a.stage_bytes;
 #pragma unroll
-            for (int bi = 0; bi < BPW; ++bi) {
-                const int bb = kw * BPW + bi;  // block within the stage
-                const uint8_t* wst = stg + (size_t)(bb >> 3) * a.sub_bytes;  // its sub-slice
-                const uint8_t* xst = wst + a.x_offset;
-                const int b = bb & 7;                                         // block within the sub-slice
-                const uint8_t* rowg = wst + (size_t)(rg * 16 + g) * kSkWRowBytes;
-                const uint8_t* rowg8 = rowg + 8 * kSkWRowBytes;
-                // quant bytes 2t, 2t+1 (elements 2t, 2t+1 and 16+2t, 17+2t) and 8+2t, 9+2t
-                const uint8_t* qg = rowg + b * 18 + 2;
-                const uint8_t* qg8 = rowg8 + b * 18 + 2;
-                const uint32_t wg = (uint32_t)*reinterpret_cast<const uint16_t*>(qg + 2 * t) |
-                                    ((uint32_t)*reinterpret_cast<const uint16_t*>(qg + 8 + 2 * t) << 16);
-                const uint32_t wg8 = (uint32_t)*reinterpret_cast<const uint16_t*>(qg8 + 2 * t) |
-                                     ((uint32_t)*reinterpret_cast<const uint16_t*>(qg8 + 8 + 2 * t) << 16);
-                const uint32_t dg2 = pack_pair<T>(__half2float(*reinterpret_cast<const __half*>(rowg + b * 18)));
-                const uint32_t dg82 = pack_pair<T>(__half2float(*reinterpret_cast<const __half*>(rowg8 + b * 18)));
-                // bytes [q(2t), q(2t+1), q(8+2t), q(9+2t)]: low nibbles are elements of the first
-                // k16 step, high nibbles of the second
-                const uint32_t lo = wg & 0x0F0F0F0Fu, hi = (wg >> 4) & 0x0F0F0F0Fu;
-                const uint32_t lo8 = wg8 & 0x0F0F0F0Fu, hi8 = (wg8 >> 4) & 0x0F0F0F0Fu;
-                uint32_t a1[4], a2[4];
-                a1[0] = sub_mul2<T>(prmt(lo, 0u, 0x4140u) | Magic<T>::kOr, sub2, dg2);    // row g, k 2t..
-                a1[1] = sub_mul2<T>(prmt(lo8, 0u, 0x4140u) | Magic<T>::kOr, sub2, dg82);  // row g+8
-                a1[2] = sub_mul2<T>(prmt(lo, 0u, 0x4342u) | Magic<T>::kOr, sub2, dg2);    // row g, k 8+2t..
-                a1[3] = sub_mul2<T>(prmt(lo8, 0u, 0x4342u) | Magic<T>::kOr, sub2, dg82);
-                a2[0] = sub_mul2<T>(prmt(hi, 0u, 0x4140u) | Magic<T>::kOr, sub2, dg2);
-                a2[1] = sub_mul2<T>(prmt(hi8, 0u, 0x4140u) | Magic<T>::kOr, sub2, dg82);
-                a2[2] = sub_mul2<T>(prmt(hi, 0u, 0x4342u) | Magic<T>::kOr, sub2, dg2);
-                a2[3] = sub_mul2<T>(prmt(hi8, 0u, 0x4342u) | Magic<T>::kOr, sub2, dg82);
+            for (int u = 0; u < SUBS; ++u) {
+                const uint8_t* wst = stg + (size_t)u * (TR * kSkWRowBytes);
+                const uint8_t* xst = stg + (size_t)u * (2 * SP * kSkXPitch);
+                // B fragments of block bw for every 8-sequence tile: k 2t, 2t+1 = elements
+                // (4t, 4t+2), k 2t+8, 2t+9 = (4t+1, 4t+3); then the same + 16
+                uint32_t bf[NT][4];
 #pragma unroll
                 for (int j = 0; j < NT; ++j) {
-                    // block b's 32 activations: box b / 4, elements 32 (b % 4) .. + 31
-                    const uint8_t* xr = xst + (size_t)(b >> 2) * (SP * kSkXPitch) + (size_t)(8 * j + g) * kSkXPitch +
-                                        (size_t)(b & 3) * 64 + 4 * t;
-                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xr);
-                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(xr + 16);
-                    const uint32_t b2 = *reinterpret_cast<const uint32_t*>(xr + 32);
-                    const uint32_t b3 = *reinterpret_cast<const uint32_t*>(xr + 48);
-                    mma16816<T>(acc[j], a1, b0, b1);
-                    mma16816<T>(acc[j], a2, b2, b3);
+                    const uint8_t* xr = xst + x_lane + (size_t)(8 * j) * kSkXPitch;
+                    const uint2 lo = *reinterpret_cast<const uint2*>(xr);
+                    const uint2 hi = *reinterpret_cast<const uint2*>(xr + 32);
+                    bf[j][0] = prmt(lo.x, lo.y, 0x5410u);
+                    bf[j][1] = prmt(lo.x, lo.y, 0x7632u);
+                    bf[j][2] = prmt(hi.x, hi.y, 0x5410u);
+                    bf[j][3] = prmt(hi.x, hi.y, 0x7632u);
+                }
+#pragma unroll
+                for (int r = 0; r < RG; ++r) {
+                    const uint8_t* rw = wst + (size_t)(r * 16) * kSkWRowBytes;
+                    uint32_t wg, wg8;
+                    if (even_block) {
+                        const uint32_t* p = reinterpret_cast<const uint32_t*>(rw + w_lane);
+                        const uint32_t* p8 = reinterpret_cast<const uint32_t*>(rw + w_lane + 8 * kSkWRowBytes);
+                        wg = prmt(p[0], p[1], 0x5432u);
+                        wg8 = prmt(p8[0], p8[1], 0x5432u);
+                    } else {
+                        wg = *reinterpret_cast<const uint32_t*>(rw + w_lane);
+                        wg8 = *reinterpret_cast<const uint32_t*>(rw + w_lane + 8 * kSkWRowBytes);
+                    }
+                    const float dg = __half2float(*reinterpret_cast<const __half*>(rw + d_lane));
+                    const float dg8 = __half2float(*reinterpret_cast<const __half*>(rw + d_lane + 8 * kSkWRowBytes));
+                    // A: rows g / g+8; first k16 step the low nibbles (elements 4t, 4t+2 at bit 0,
+                    // 4t+1, 4t+3 at bit 8), second the high nibbles (bits 4 and 12)
+                    const uint32_t a0[4] = {nib_pair<T, 0>(wg, sub2), nib_pair<T, 0>(wg8, sub2),
+                                            nib_pair<T, 8>(wg, sub2), nib_pair<T, 8>(wg8, sub2)};
+                    const uint32_t a1[4] = {nib_pair<T, 4>(wg, sub2), nib_pair<T, 4>(wg8, sub2),
+                                            nib_pair<T, 12>(wg, sub2), nib_pair<T, 12>(wg8, sub2)};
+#pragma unroll
+                    for (int j = 0; j < NT; ++j) {
+                        float d4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        mma16816<T>(d4, a0, bf[j][0], bf[j][1]);
+                        mma16816<T>(d4, a1, bf[j][2], bf[j][3]);
+                        acc[r][j][0] = fmaf(dg, d4[0], acc[r][j][0]);
+                        acc[r][j][1] = fmaf(dg, d4[1], acc[r][j][1]);
+                        acc[r][j][2] = fmaf(dg8, d4[2], acc[r][j][2]);
+                        acc[r][j][3] = fmaf(dg8, d4[3], acc[r][j][3]);
+                    }
                 }
             }
             __syncwarp();
@@ -278,33 +294,39 @@ __global__ void __launch_bounds__(kSkThreads, 1)
                 ph ^= 1u;
             }
         }
-        // partial sums of this warp: rows g, g+8 of its group, sequences 8j + 2t, 8j + 2t + 1
+        // partial sums of this warp: rows 16r + g, 16r + g + 8, sequences 8j + 2t, 8j + 2t + 1
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-            float* rp = red + ((size_t)kw * TR + rg * 16 + g) * SP + 8 * j + 2 * t;
-            rp[0] = acc[j][0];
-            rp[1] = acc[j][1];
-            rp[8 * SP] = acc[j][2];
-            rp[8 * SP + 1] = acc[j][3];
-        }
+        for (int r = 0; r < RG; ++r)
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                float* rp = red + ((size_t)warp * SP + 8 * j + 2 * t) * RP + r * 16 + g;
+                rp[0] = acc[r][j][0];
+                rp[RP] = acc[r][j][1];
+                rp[8] = acc[r][j][2];
+                rp[RP + 8] = acc[r][j][3];
+            }
         __syncwarp();
         if (lane == 0) mbar_arrive(&red_bar);
         if (!mbar_wait(&red_bar, (uint32_t)c & 1u, a.status)) return;
         const int row0 = r0 + c * TR;
         const int nrows = min(TR, r1 - row0);
         const bool fused = epilogue_active(a.epi);
-        for (int i = tid; i < nrows * ns; i += 256) {
-            const int sq = i / nrows, r = i % nrows;  // consecutive threads: consecutive rows
+        for (int i = tid; i < ns * TR; i += 256) {
+            const int sq = i / TR, r = i % TR;  // consecutive threads: consecutive rows
+            if (r >= nrows) continue;
             float v = 0.0f;
 #pragma unroll
-            for (int w = 0; w < WPG; ++w) v += red[((size_t)w * TR + r) * SP + sq];
+            for (int w = 0; w < 8; ++w) v += red[((size_t)w * SP + sq) * RP + r];
             if (a.bias) v += bias_value(a.bias, a.bias_type, row0 + r);
             if (fused) v = epilogue_finish(a.epi, seq0 + sq, row0 + r, v);
             store_value(a.C, a.c_type, (size_t)(seq0 + sq) * a.ldc + row0 + r, v);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&done_bar);
-        if (!mbar_wait(&done_bar, (uint32_t)c & 1u, a.status)) return;
+        if (c + 1 < nchunks) {
+            // the next chunk's partials overwrite these
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&done_bar);
+            if (!mbar_wait(&done_bar, (uint32_t)c & 1u, a.status)) return;
+        }
     }
 }
 
@@ -339,13 +361,26 @@ cudaError_t launch_skinny(const mgpu_k::LaunchCtx& c, const CUtensorMap& tm, con
 template <int NT, typename T>
 cudaError_t dispatch_rg(const mgpu_k::LaunchCtx& c, int rg, int subs, const CUtensorMap& tm, const CUtensorMap& tx,
                         const SkinnyArgs& a, dim3 grid, size_t smem) {
-    // (row groups, sub-slices): at most 4 blocks per warp per stage
-    if (rg == 4) return launch_skinny<NT, 4, 1, T>(c, tm, tx, a, grid, smem);
-    if (rg == 2) return subs == 2 ? launch_skinny<NT, 2, 2, T>(c, tm, tx, a, grid, smem)
-                                  : launch_skinny<NT, 2, 1, T>(c, tm, tx, a, grid, smem);
-    return subs == 4 ? launch_skinny<NT, 1, 4, T>(c, tm, tx, a, grid, smem)
-         : subs == 2 ? launch_skinny<NT, 1, 2, T>(c, tm, tx, a, grid, smem)
-                     : launch_skinny<NT, 1, 1, T>(c, tm, tx, a, grid, smem);
+    // (row groups, sub-slices): at most 8 (row group, block) units per warp per stage with one
+    // 8-sequence tile, 4 with two (the register budget of two CTAs per SM)
+    switch (rg) {
+        case 4: return launch_skinny<NT, 4, 1, T>(c, tm, tx, a, grid, smem);
+        case 3:
+            if constexpr (NT == 1)
+                if (subs == 2) return launch_skinny<NT, 3, 2, T>(c, tm, tx, a, grid, smem);
+            return launch_skinny<NT, 3, 1, T>(c, tm, tx, a, grid, smem);
+        case 2:
+            if constexpr (NT == 1)
+                if (subs == 4) return launch_skinny<NT, 2, 4, T>(c, tm, tx, a, grid, smem);
+            return subs == 2 ? launch_skinny<NT, 2, 2, T>(c, tm, tx, a, grid, smem)
+                             : launch_skinny<NT, 2, 1, T>(c, tm, tx, a, grid, smem);
+        default:
+            if constexpr (NT == 1)
+                if (subs == 8) return launch_skinny<NT, 1, 8, T>(c, tm, tx, a, grid, smem);
+            return subs == 4 ? launch_skinny<NT, 1, 4, T>(c, tm, tx, a, grid, smem)
+                 : subs == 2 ? launch_skinny<NT, 1, 2, T>(c, tm, tx, a, grid, smem)
+                             : launch_skinny<NT, 1, 1, T>(c, tm, tx, a, grid, smem);
+    }
 }
 
 }  // namespace
@@ -362,36 +397,64 @@ bool skinny_ok(const GemmOperand& A, const GemmOperand& B, int M, int N, int K) 
 cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B, const GemmOperand& C,
                            const void* bias, int bias_type, int M, int N, int K, const Epilogue& epi) {
     if (!skinny_ok(A, B, M, N, K)) return cudaErrorInvalidValue;
-    const int NT = M <= 8 ? 1 : M <= 16 ? 2 : 4;
+    // up to 16 sequences per CTA; more take further CTAs over the same rows (grid.y), whose
+    // second read of the packed rows is served by L2
+    const int NT = M <= 8 ? 1 : 2;
     const int SP = 8 * NT;
     // CTAs over the rows: one per SM, fewer when a CTA would get fewer than 16 rows
     const int G = max(1, min(c.sm_count, (N + 15) / 16));
     const int rows_per_cta = (N + G - 1) / G;
-    // chunk: all of the CTA's rows when they fit in 64 (so each activation slice is staged once
-    // per CTA), else 64-row chunks
-    int RG = 1;
-    while (RG < 4 && 16 * RG < rows_per_cta) RG <<= 1;
+    auto xoff_of = [&](int rg, int u) { return ((size_t)u * 16 * rg * kSkWRowBytes + 127) / 128 * 128; };
+    auto red_of = [&](int rg) { return (size_t)8 * SP * (16 * rg + 4) * sizeof(float); };
+    auto stage_of = [&](int rg, int u) {
+        return (xoff_of(rg, u) + (size_t)2 * u * SP * kSkXPitch + 1023) / 1024 * 1024;
+    };
+    // rows per chunk (16 RG): the choice with the fewest padded rows, counting each chunk's
+    // reduction as 8 rows of work, among those where the partial sums and two stages fit
+    int RG = 0;
+    long best = 0;
+    for (int rg = 1; rg <= 4; ++rg) {
+        if (2 * stage_of(rg, 1) + red_of(rg) + 1024 > kSkSmemBudget) continue;
+        const long chunks = (rows_per_cta + 16 * rg - 1) / (16 * rg);
+        const long cost = chunks * 16 * rg + 8 * chunks;
+        if (RG == 0 || cost <= best) {
+            RG = rg;
+            best = cost;
+        }
+    }
+    if (RG == 0) return cudaErrorInvalidValue;
     const int TR = 16 * RG;
-    const uint32_t x_offset = (uint32_t)((TR * kSkWRowBytes + 127) / 128 * 128);
-    const uint32_t sub_bytes = x_offset + 2 * SP * kSkXPitch;  // a multiple of 128
-    const size_t red_bytes = (size_t)(8 / RG) * TR * SP * sizeof(float);
-    // sub-slices per stage: up to 4 blocks per warp, dividing K / 256, with at least 2 stages
-    int subs = 4 / RG;
-    auto stage_of = [&](int u) { return ((size_t)u * sub_bytes + 1023) / 1024 * 1024; };
-    while (subs > 1 && ((K / kSkSlice) % subs != 0 || 2 * stage_of(subs) + red_bytes + 1024 > kSkSmemBudget))
+    const size_t red_bytes = red_of(RG);
+    // sub-slices per stage: up to 8 (row group, block) units per warp (4 with two tiles),
+    // dividing K / 256, with at least 2 stages
+    const int max_units = NT == 1 ? 8 : 4;
+    int subs = RG == 4 ? 1 : RG == 3 ? max_units / 4 : max_units / RG;
+    while (subs > 1 && ((K / kSkSlice) % subs != 0 || 2 * stage_of(RG, subs) + red_bytes + 1024 > kSkSmemBudget))
         subs >>= 1;
-    const uint32_t stage_bytes = (uint32_t)stage_of(subs);
+    const uint32_t stage_bytes = (uint32_t)stage_of(RG, subs);
+    const uint32_t x_offset = (uint32_t)xoff_of(RG, subs);
     const int stages = (int)std::min<size_t>(kSkMaxStages, (kSkSmemBudget - 1024 - red_bytes) / stage_bytes);
     if (stages < 2) return cudaErrorInvalidValue;
     const size_t smem = 1024 + (size_t)stages * stage_bytes + red_bytes;
 
     CUtensorMap tm;
-    // W as a 2-D array of 16-bit units: rows N, row pitch K/32 * 18 bytes; box = one 256-k slice
-    // (72 units) x TR rows
-    if (!make_tensor_map_u16(&tm, B.ptr, N, B.ld / 2, B.ld / 2, kSkWRowBytes / 2, TR)) return cudaErrorInvalidValue;
-    // A as a 2-D array of 16-bit elements: M rows, K columns, pitch lda; box 136 x 8 NT
+    // W as [K/256 slices][N rows][72 units]: unit pitch 2 bytes, row pitch K/32 * 18 bytes, slice
+    // pitch 144 bytes; box {72, TR, subs}, rows past N read as zeros
+    {
+        const int64_t dims[3] = {kSkWRowBytes / 2, N, K / kSkSlice};
+        const int64_t strides[2] = {B.ld, kSkWRowBytes};
+        const int box[3] = {kSkWRowBytes / 2, TR, subs};
+        if (!make_tensor_map_u16_3d(&tm, B.ptr, dims, strides, box)) return cudaErrorInvalidValue;
+    }
+    // A as [K/128 chunks][M rows][128 elements]: box {136, 8 NT, 2 subs}, whose 8 columns past a
+    // chunk and rows past M read as zeros; each activation row lands at a 272-byte pitch
     CUtensorMap tx;
-    if (!make_tensor_map_u16(&tx, A.ptr, M, K, A.ld, kSkXBox, SP)) return cudaErrorInvalidValue;
+    {
+        const int64_t dims[3] = {128, M, K / 128};
+        const int64_t strides[2] = {A.ld * 2, 256};
+        const int box[3] = {kSkXBox, SP, 2 * subs};
+        if (!make_tensor_map_u16_3d(&tx, A.ptr, dims, strides, box)) return cudaErrorInvalidValue;
+    }
     SkinnyArgs a;
     a.A = A.ptr;
     a.lda = A.ld;
@@ -405,17 +468,17 @@ cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmO
     a.N = N;
     a.K = K;
     a.stages = stages;
-    a.sub_bytes = sub_bytes;
+    a.tx_bytes = (uint32_t)(subs * TR * kSkWRowBytes + 2 * subs * SP * kSkXPitch);
     a.stage_bytes = stage_bytes;
     a.x_offset = x_offset;
     a.status = c.status;
     const dim3 grid(G, (M + SP - 1) / SP);
     const bool bf16 = A.type == MGPU_BF16;
-    switch (NT) {
-        case 1: return bf16 ? dispatch_rg<1, __nv_bfloat16>(c, RG, subs, tm, tx, a, grid, smem) : dispatch_rg<1, __half>(c, RG, subs, tm, tx, a, grid, smem);
-        case 2: return bf16 ? dispatch_rg<2, __nv_bfloat16>(c, RG, subs, tm, tx, a, grid, smem) : dispatch_rg<2, __half>(c, RG, subs, tm, tx, a, grid, smem);
-        default: return bf16 ? dispatch_rg<4, __nv_bfloat16>(c, RG, subs, tm, tx, a, grid, smem) : dispatch_rg<4, __half>(c, RG, subs, tm, tx, a, grid, smem);
-    }
+    if (NT == 1)
+        return bf16 ? dispatch_rg<1, __nv_bfloat16>(c, RG, subs, tm, tx, a, grid, smem)
+                    : dispatch_rg<1, __half>(c, RG, subs, tm, tx, a, grid, smem);
+    return bf16 ? dispatch_rg<2, __nv_bfloat16>(c, RG, subs, tm, tx, a, grid, smem)
+                : dispatch_rg<2, __half>(c, RG, subs, tm, tx, a, grid, smem);
 }
 
 }  // namespace mgpu_k

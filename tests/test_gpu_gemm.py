@@ -6,7 +6,7 @@ import pytest
 
 import mvlm_b200 as mg
 import oracle as O
-from tests.numerics import TOL_16, assert_close
+from tests.numerics import TOL_16, TOL_F32, assert_close
 
 pytestmark = pytest.mark.gpu
 
@@ -156,9 +156,13 @@ def test_gemm_rejects_bad_arguments(dev):
 
 @pytest.mark.parametrize("at", [mg.BF16, mg.F16])
 @pytest.mark.parametrize("M,N,K", [(1, 100, 256), (3, 2048, 2048), (8, 6144, 2048), (13, 1000, 512),
+                                   (8, 2048, 8192), (16, 8192, 2048), (24, 1000, 1024), (5, 51200, 2048),
                                    (40, 2048, 8192), (128, 4096, 2048), (32, 51200, 2048)])
 def test_skinny_q4_batched_decode(dev, at, M, N, K):
-    # batched decode: M sequences against GGUF Q4_0 weights (the streaming skinny kernel)
+    # batched decode: M sequences against GGUF Q4_0 weights (the streaming skinny kernel).
+    # Its MMAs take the exact (q - 8) and the 16-bit activations and scale each block's sum by d
+    # in fp32, so an fp32 output stays within the fp32 tolerance (M <= 32; larger M takes the
+    # tcgen05 GEMM, whose B tiles are (q - 8) d rounded to 16 bits)
     A = O.normal(M * K, 3 * M + K, 1.0)
     A16 = O.bf16(A) if at == mg.BF16 else O.f16(A)
     A32 = O.bf16_to_f32(A16) if at == mg.BF16 else O.f16_to_f32(A16)
@@ -171,4 +175,5 @@ def test_skinny_q4_batched_decode(dev, at, M, N, K):
                   bias=dev.array(bias, mg.F32)).wait()
         C = dC.read(mg.NP_DTYPE[ct])
         C = O.bf16_to_f32(C) if ct == mg.BF16 else O.f16_to_f32(C) if ct == mg.F16 else C
-        assert_close(C, ref.reshape(-1), TOL_16, f"skinny {M}x{N}x{K} a{at} c{ct}")
+        tol = TOL_F32 if ct == mg.F32 and M <= 32 else TOL_16
+        assert_close(C, ref.reshape(-1), tol, f"skinny {M}x{N}x{K} a{at} c{ct}")
