@@ -267,6 +267,11 @@ mgpu_event* mgpu_dequant(const mgpu_device* dev, mgpu_buf* W, mgpu_buf* out, int
  * fields).  Computed on the device by one CTA; `out` (>= 8 bytes) receives the int32 index and
  * the fp32 value, so shards of column-sharded logits combine by (larger value, smaller index). */
 mgpu_event* mgpu_argmax(const mgpu_device* dev, mgpu_buf* logits, int n, mgpu_buf* out);
+/* New: mgpu_argmax for a batch of `rows` rows of n logits, row r starting at element r * ld
+ * (ld >= n), e.g. each sequence of a batched decode against one lm_head column shard.  `out`
+ * (>= 8 * rows bytes) receives the rows' {int32 index, fp32 value} pairs in row order.  One CTA
+ * per row, one launch. */
+mgpu_event* mgpu_argmax_rows(const mgpu_device* dev, mgpu_buf* logits, int rows, int n, int64_t ld, mgpu_buf* out);
 /* argmax_logits itself: waits for the stream and returns the index, or -1 on error. */
 int mgpu_argmax_logits(const mgpu_device* dev, mgpu_buf* logits, int vocab_size);
 /* New (the reference decodes on one device): the greedy token of logits column-sharded over

@@ -83,6 +83,7 @@ SIGNATURES = {
     "mgpu_dequant": (_vp, [_vp, _vp, _vp, _i64, _i]),
     "mgpu_argmax": (_vp, [_vp, _vp, _i, _vp]),
     "mgpu_argmax_logits": (_i, [_vp, _vp, _i]),
+    "mgpu_argmax_rows": (_vp, [_vp, _vp, _i, _i, _i64, _vp]),
     "mgpu_argmax_combine": (_vp, [_vp, _vp, _i, _i, _vp]),
     "mgpu_wait_event": (_i, [_vp]),
     "mgpu_release_event": (None, [_vp]),
@@ -480,6 +481,12 @@ def dequant(dev: Device, W: Buffer, out: Buffer, n: int, qtype: int) -> Event:
 def argmax(dev: Device, logits: Buffer, n: int, out: Buffer) -> Event:
     """out (8 bytes) <- {int32 index, fp32 value}: the reference's argmax_logits on the device."""
     return _ev(lib().mgpu_argmax(dev.h, logits.h, n, out.h), "argmax")
+
+
+def argmax_rows(dev: Device, logits: Buffer, rows: int, n: int, ld: int, out: Buffer) -> Event:
+    """out (8 bytes per row) <- mgpu_argmax of each of `rows` rows of n logits, row r at element
+    r * ld: one launch for a batch of sequences."""
+    return _ev(lib().mgpu_argmax_rows(dev.h, logits.h, rows, n, ld, out.h), "argmax_rows")
 
 
 def argmax_combine(dev: Device, pairs: Buffer, n_ranks: int, n_total: int, out: Buffer) -> Event:

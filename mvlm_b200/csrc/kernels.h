@@ -89,6 +89,8 @@ cudaError_t convert(const LaunchCtx& c, int itype, const void* in, int otype, vo
 cudaError_t selftest_bounded_wait(const LaunchCtx& c, uint64_t limit_ns);
 // out[0] = argmax index, out[1] = the value (fp32 bits), reference argmax semantics; n >= 1.
 cudaError_t argmax(const LaunchCtx& c, int type, const void* logits, int n, int* out);
+// The same for `rows` rows of n values, row r at element r * ld: pair r at out[2r], out[2r+1].
+cudaError_t argmax_rows(const LaunchCtx& c, int type, const void* logits, int rows, int n, int64_t ld, int* out);
 // out[r][:] = RMSNorm(in[r][:]) for rows r < rows of H values (in / out of `type`, w of wtype).
 cudaError_t rms_norm(const LaunchCtx& c, int type, const void* in, void* out, int wtype, const void* w, int rows,
                      int H, float eps);

@@ -229,13 +229,17 @@ __global__ void argmax_combine_kernel(const int* __restrict__ pairs, int n_ranks
 // (-1e30, index 0) as the reference does; out[0] = index, out[1] = its value (fp32 bits).
 // Each thread scans a strided subsequence in index order keeping its first maximum; the
 // pairs then combine by larger value, then smaller index, which gives the same index.
-__global__ void __launch_bounds__(1024) argmax_kernel(int type, const void* __restrict__ x, int n, int* out) {
+// One CTA per row (row r of the batch at element r * ld); its pair at out[2r].
+__global__ void __launch_bounds__(1024) argmax_kernel(int type, const void* __restrict__ x, int n, int64_t ld,
+                                                      int* out) {
     __shared__ float sv[32];
     __shared__ int si[32];
+    const int64_t base = (int64_t)blockIdx.x * ld;
+    out += 2 * blockIdx.x;
     float best = -1e30f;
     int bi = 0x7FFFFFFF;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = argmax_value(type, x, i);
+        const float v = argmax_value(type, x, base + i);
         if (v > best) {
             best = v;
             bi = i;
@@ -321,7 +325,11 @@ cudaError_t convert(const LaunchCtx& c, int itype, const void* in, int otype, vo
 }
 
 cudaError_t argmax(const LaunchCtx& c, int type, const void* logits, int n, int* out) {
-    argmax_kernel<<<1, 1024, 0, c.stream>>>(type, logits, n, out);
+    return argmax_rows(c, type, logits, 1, n, n, out);
+}
+
+cudaError_t argmax_rows(const LaunchCtx& c, int type, const void* logits, int rows, int n, int64_t ld, int* out) {
+    argmax_kernel<<<rows, 1024, 0, c.stream>>>(type, logits, n, ld, out);
     return cudaGetLastError();
 }
 

@@ -1082,6 +1082,24 @@ mgpu_event* mgpu_argmax(const mgpu_device* cd, mgpu_buf* logits, int n, mgpu_buf
     return event_end(d, ev);
 }
 
+mgpu_event* mgpu_argmax_rows(const mgpu_device* cd, mgpu_buf* logits, int rows, int n, int64_t ld, mgpu_buf* out) {
+    API_ENTRY();
+    REQUIRE(cd && logits && out && rows > 0 && n > 0 && ld >= n, "mgpu_argmax_rows: bad arguments");
+    REQUIRE(is_float_type(logits->type), "mgpu_argmax_rows: logits must be f32/f16/bf16");
+    REQUIRE(logits->bytes >= ((size_t)(rows - 1) * ld + n) * elem_size(logits->type),
+            "mgpu_argmax_rows: logits too small");
+    REQUIRE(out->bytes >= (size_t)rows * 8, "mgpu_argmax_rows: out needs 8 bytes per row");
+    mgpu_device* d = const_cast<mgpu_device*>(cd);
+    DeviceGuard g(d->ordinal);
+    mgpu_event* ev = event_begin(d);
+    if (!cuda_ok(mgpu_k::argmax_rows(ctx_of(d), logits->type, logits->ptr, rows, n, ld, (int*)out->ptr),
+                 "mgpu_argmax_rows")) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(d, ev);
+}
+
 mgpu_event* mgpu_argmax_combine(const mgpu_device* cd, mgpu_buf* pairs, int n_ranks, int n_total, mgpu_buf* out) {
     API_ENTRY();
     REQUIRE(cd && pairs && out && n_ranks > 0 && n_total >= n_ranks, "mgpu_argmax_combine: bad arguments");

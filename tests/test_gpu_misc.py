@@ -135,3 +135,21 @@ def test_argmax_combine_column_shards(dev, ranks):
         got = out.read(np.int32)
         assert got[0] == want_i, (case, got[0], want_i)
         assert np.float32(got[1:2].view(np.float32)[0]) == np.float32(want_v)
+
+
+@pytest.mark.parametrize("rows,n,ld", [(1, 51200, 51200), (8, 6400, 6400), (5, 1000, 1029)])
+def test_argmax_rows_matches_per_row_scan(dev, rows, n, ld):
+    # a batch of sequences' logits against one lm_head shard: each row's pair equals the
+    # reference scan of that row; rows at a pitch ld >= n (padding never read), a tie in row 0
+    x = O.normal(rows * ld, 500 + rows, 3.0).reshape(rows, ld)
+    x[:, n:] = 1e6  # beyond each row's n values: must not win
+    x[0, [n // 3, n - 1]] = 50.0
+    raw = x.reshape(-1).view(np.uint32).copy()
+    out = dev.empty(2 * rows, mg.F32)
+    mg.argmax_rows(dev, dev.array(raw, mg.F32), rows, n, ld, out).wait()
+    got = out.read(np.int32).reshape(rows, 2)
+    for r in range(rows):
+        want_i, want_v = O.argmax_logits(raw[r * ld:r * ld + n].copy(), mg.F32)
+        assert got[r, 0] == want_i, (r, got[r, 0], want_i)
+        assert np.float32(got[r, 1:2].view(np.float32)[0]) == np.float32(want_v)
+    assert got[0, 0] == n // 3
