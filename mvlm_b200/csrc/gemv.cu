@@ -771,12 +771,17 @@ struct GemvQLaunch {
             const int per_sm = N > c.sm_count * kBigRows ? kGemvCtasPerSm : 1;
             const int G = max(1, min(c.sm_count * per_sm, (N + RP - 1) / RP));
             const int rows_per_cta = (N + G - 1) / G;
-            // Rows per thread (8, 4, 2, 1) and ring depth (2..8 stages).  Layer-sized GEMVs: a
-            // ring that holds all of the CTA's rows, so the weights stream in before
-            // griddepcontrol.wait returns; among those, the widest chunk (more independent rows
-            // per thread) that computes at most 25 % padding rows.  GEMVs too large to prefetch
-            // whole (the lm_head) stream through a 4-stage ring of the widest chunk that fits.
-            // Row partials of up to kPartFloats are buffered between flushes.
+            // Rows per thread (8, 4, 2, 1) and ring depth (2..8 stages).  Eight rows per thread
+            // whenever two stages of them fit: a decode chain then launches one function for
+            // every shape, and a dependent launch of a different function was measured to cost
+            // ~1.4 us more than one of the same function (a 97-GEMV Phi-1.5 step with 4 rows per
+            // thread for qkv / out and 8 for fc1 / fc2 / lm_head took 455.8 us, with 8 for all
+            // 385.8 us; per-shape chains of one function were equally fast either way).  The
+            // ring then holds all of a layer-sized GEMV's rows, so its weights stream in before
+            // griddepcontrol.wait returns.  Otherwise: a ring that holds all of the CTA's rows
+            // with the widest chunk that computes at most 25 % padding rows; then, for GEMVs too
+            // large to prefetch whole, a 4-stage ring of the widest chunk that fits.  Row
+            // partials of up to kPartFloats are buffered between flushes.
             constexpr int kPartFloats = 4096;
             const int wpr = nb / 32;
             const size_t x_bytes = (size_t)3 * (K / 4) * 4 + (size_t)2 * nb * 4;
@@ -792,6 +797,10 @@ struct GemvQLaunch {
                 return max(2, min(cap, min(chunks_of(r), (int)((kGemvSmemBudget - fixed) / stride(r)))));
             };
             int rpt = 0, stages = 0;
+            if (const int d8 = depth(8, kGemvMaxStages)) {
+                rpt = 8;
+                stages = d8;
+            }
             for (int r = 8; r >= 1 && !rpt; r >>= 1) {
                 const int d = depth(r, kGemvMaxStages);
                 const int waste = chunks_of(r) * RP * r - rows_per_cta;

@@ -172,11 +172,17 @@ mgpu_event* event_end(mgpu_device* d, mgpu_event* ev) {
     return ev;
 }
 
+// Called after the work it reports on has completed (an event or the stream was waited for).
+// The read is a device-to-pageable copy, which returns only once it has landed; it does not
+// wait for work queued on the device's stream after that point.  Every upload and fill of the
+// library, by contrast, goes on the device's stream: the stream is non-blocking, so an
+// operation on the legacy default stream (plain cudaMemcpy / cudaMemset) would not be ordered
+// with its kernels.
 bool check_status(mgpu_device* d) {
     int st = 0;
     if (!cuda_ok(cudaMemcpy(&st, d->d_status, sizeof(int), cudaMemcpyDeviceToHost), "read status")) return false;
     if (st != 0) {
-        cudaMemset(d->d_status, 0, sizeof(int));
+        cudaMemsetAsync(d->d_status, 0, sizeof(int), d->stream);
         set_error(st, "a kernel's bounded wait expired (device status %d); its output is invalid", st);
         return false;
     }
@@ -368,7 +374,8 @@ mgpu_device* mgpu_init_device(int ordinal) {
     d->saved_event_mode = 2;
     if (!cuda_ok(cudaStreamCreateWithFlags(&d->own_stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
         !cuda_ok(cudaMalloc(&d->d_status, 256), "cudaMalloc(status)") ||
-        !cuda_ok(cudaMemset(d->d_status, 0, 256), "cudaMemset(status)")) {
+        !cuda_ok(cudaMemsetAsync(d->d_status, 0, 256, d->own_stream), "cudaMemsetAsync(status)") ||
+        !cuda_ok(cudaStreamSynchronize(d->own_stream), "cudaStreamSynchronize")) {
         delete d;
         return nullptr;
     }
@@ -446,7 +453,12 @@ mgpu_buf* mgpu_create_buffer(mgpu_device* d, size_t bytes, const void* host_src)
     // Allocation rounded up to 256 bytes so that 16-byte vector / bulk reads of the last
     // row never leave the allocation.
     if (!cuda_ok(cudaMalloc(&p, (bytes + 255) & ~(size_t)255), "cudaMalloc")) return nullptr;
-    if (host_src && !cuda_ok(cudaMemcpy(p, host_src, bytes, cudaMemcpyHostToDevice), "cudaMemcpy")) {
+    // On the device's stream, then waited for: a plain cudaMemcpy from pageable memory may
+    // return before its last DMA lands, and it runs on the legacy default stream, which the
+    // device's non-blocking stream does not wait for (a kernel launched next could read the
+    // upload's tail before it arrived).
+    if (host_src && (!cuda_ok(cudaMemcpyAsync(p, host_src, bytes, cudaMemcpyHostToDevice, d->stream), "upload") ||
+                     !cuda_ok(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize"))) {
         cudaFree(p);
         return nullptr;
     }
@@ -460,10 +472,11 @@ mgpu_buf* mgpu_create_weight_image(mgpu_device* d, int rows, int cols, const uin
     mgpu_buf* b = mgpu_create_buffer(d, (size_t)rows * ld * 2, nullptr);
     if (!b) return nullptr;
     DeviceGuard g(d->ordinal);
-    if (!cuda_ok(cudaMemset(b->ptr, 0, b->bytes), "cudaMemset") ||
-        (data && !cuda_ok(cudaMemcpy2D(b->ptr, ld * 2, data, (size_t)cols * 2, (size_t)cols * 2, rows,
-                                       cudaMemcpyHostToDevice),
-                          "cudaMemcpy2D"))) {
+    if (!cuda_ok(cudaMemsetAsync(b->ptr, 0, b->bytes, d->stream), "cudaMemsetAsync") ||
+        (data && !cuda_ok(cudaMemcpy2DAsync(b->ptr, ld * 2, data, (size_t)cols * 2, (size_t)cols * 2, rows,
+                                            cudaMemcpyHostToDevice, d->stream),
+                          "cudaMemcpy2DAsync")) ||
+        !cuda_ok(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize")) {
         mgpu_release_buffer(b);
         return nullptr;
     }
