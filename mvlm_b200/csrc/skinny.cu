@@ -63,6 +63,7 @@ struct SkinnyArgs {
     uint32_t stage_bytes;  // weights [SUBS][TR][144 B], then activations [2 SUBS][8 NT][272 B], 1 KB aligned
     uint32_t x_offset;     // offset of the activations inside a stage (128-byte aligned)
     uint32_t tx_bytes;     // bytes the two copies of a stage deliver
+    int shape;             // which (row groups, sub-slices) body runs (SkinnyShape)
     int* status;
 };
 
@@ -128,11 +129,10 @@ __device__ __forceinline__ void store_value(void* C, int type, size_t idx, float
     else reinterpret_cast<__nv_bfloat16*>(C)[idx] = __float2bfloat16_rn(v);
 }
 
-// NT = 8-sequence tiles per CTA (S per CTA <= 8 NT); RG = 16-row groups per chunk; SUBS =
-// 256-k sub-slices per stage.
+// The kernel's body for NT = 8-sequence tiles per CTA (S per CTA <= 8 NT), RG = 16-row groups
+// per chunk, SUBS = 256-k sub-slices per stage.
 template <int NT, int RG, int SUBS, typename T>
-__global__ void __launch_bounds__(kSkThreads, 2)
-    gemm_q4_skinny(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, SkinnyArgs a) {
+__device__ __forceinline__ void skinny_body(const CUtensorMap& tmW, const CUtensorMap& tmX, const SkinnyArgs& a) {
     constexpr int TR = 16 * RG;         // rows per chunk
     constexpr int SP = 8 * NT;          // sequences per CTA
     constexpr int RP = TR + 4;          // partial-sum row pitch: a warp's 32 writes on distinct banks
@@ -330,10 +330,41 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     }
 }
 
-template <int NT, int RG, int SUBS, typename T>
+// The (row groups, sub-slices) pairs the planner uses.  One kernel function per (NT, T) holds
+// them all and picks one at run time: a decode step's GEMMs of different shapes then launch the
+// same function, and a dependent launch of a different function was measured ~1.4 us slower
+// than one of the same function (the M = 1 decode step: 455 -> 388 us with one function).
+enum SkinnyShape : int { kRg1S1, kRg1S2, kRg1S4, kRg1S8, kRg2S1, kRg2S2, kRg2S4, kRg3S1, kRg3S2, kRg4S1 };
+
+template <int NT, typename T>
+__global__ void __launch_bounds__(kSkThreads, 2)
+    gemm_q4_skinny(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, SkinnyArgs a) {
+    switch (a.shape) {
+        case kRg4S1: skinny_body<NT, 4, 1, T>(tmW, tmX, a); break;
+        case kRg3S1: skinny_body<NT, 3, 1, T>(tmW, tmX, a); break;
+        case kRg2S1: skinny_body<NT, 2, 1, T>(tmW, tmX, a); break;
+        case kRg2S2: skinny_body<NT, 2, 2, T>(tmW, tmX, a); break;
+        case kRg1S1: skinny_body<NT, 1, 1, T>(tmW, tmX, a); break;
+        case kRg1S2: skinny_body<NT, 1, 2, T>(tmW, tmX, a); break;
+        case kRg1S4: skinny_body<NT, 1, 4, T>(tmW, tmX, a); break;
+        default:
+            // with one 8-sequence tile only (the registers of two CTAs per SM)
+            if constexpr (NT == 1) {
+                switch (a.shape) {
+                    case kRg3S2: skinny_body<NT, 3, 2, T>(tmW, tmX, a); break;
+                    case kRg2S4: skinny_body<NT, 2, 4, T>(tmW, tmX, a); break;
+                    case kRg1S8: skinny_body<NT, 1, 8, T>(tmW, tmX, a); break;
+                    default: break;
+                }
+            }
+            break;
+    }
+}
+
+template <int NT, typename T>
 cudaError_t launch_skinny(const mgpu_k::LaunchCtx& c, const CUtensorMap& tm, const CUtensorMap& tx,
                           const SkinnyArgs& a, dim3 grid, size_t smem) {
-    auto kern = gemm_q4_skinny<NT, RG, SUBS, T>;
+    auto kern = gemm_q4_skinny<NT, T>;
     static thread_local uint64_t configured = 0;  // one bit per device ordinal
     int ordinal = 0;
     cudaGetDevice(&ordinal);
@@ -358,28 +389,13 @@ cudaError_t launch_skinny(const mgpu_k::LaunchCtx& c, const CUtensorMap& tm, con
     return cudaLaunchKernelEx(&cfg, kern, tm, tx, a);
 }
 
-template <int NT, typename T>
-cudaError_t dispatch_rg(const mgpu_k::LaunchCtx& c, int rg, int subs, const CUtensorMap& tm, const CUtensorMap& tx,
-                        const SkinnyArgs& a, dim3 grid, size_t smem) {
-    // (row groups, sub-slices): at most 8 (row group, block) units per warp per stage with one
-    // 8-sequence tile, 4 with two (the register budget of two CTAs per SM)
+// The shape id of a planner choice.
+int skinny_shape(int NT, int rg, int subs) {
     switch (rg) {
-        case 4: return launch_skinny<NT, 4, 1, T>(c, tm, tx, a, grid, smem);
-        case 3:
-            if constexpr (NT == 1)
-                if (subs == 2) return launch_skinny<NT, 3, 2, T>(c, tm, tx, a, grid, smem);
-            return launch_skinny<NT, 3, 1, T>(c, tm, tx, a, grid, smem);
-        case 2:
-            if constexpr (NT == 1)
-                if (subs == 4) return launch_skinny<NT, 2, 4, T>(c, tm, tx, a, grid, smem);
-            return subs == 2 ? launch_skinny<NT, 2, 2, T>(c, tm, tx, a, grid, smem)
-                             : launch_skinny<NT, 2, 1, T>(c, tm, tx, a, grid, smem);
-        default:
-            if constexpr (NT == 1)
-                if (subs == 8) return launch_skinny<NT, 1, 8, T>(c, tm, tx, a, grid, smem);
-            return subs == 4 ? launch_skinny<NT, 1, 4, T>(c, tm, tx, a, grid, smem)
-                 : subs == 2 ? launch_skinny<NT, 1, 2, T>(c, tm, tx, a, grid, smem)
-                             : launch_skinny<NT, 1, 1, T>(c, tm, tx, a, grid, smem);
+        case 4: return kRg4S1;
+        case 3: return NT == 1 && subs == 2 ? kRg3S2 : kRg3S1;
+        case 2: return NT == 1 && subs == 4 ? kRg2S4 : subs == 2 ? kRg2S2 : kRg2S1;
+        default: return NT == 1 && subs == 8 ? kRg1S8 : subs == 4 ? kRg1S4 : subs == 2 ? kRg1S2 : kRg1S1;
     }
 }
 
@@ -401,8 +417,11 @@ cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmO
     // second read of the packed rows is served by L2
     const int NT = M <= 8 ? 1 : 2;
     const int SP = 8 * NT;
-    // CTAs over the rows: one per SM, fewer when a CTA would get fewer than 16 rows
-    const int G = max(1, min(c.sm_count, (N + 15) / 16));
+    // CTAs over the rows: one per SM, fewer when a CTA would get fewer than 8 rows.  Layer
+    // shapes then all launch one CTA per SM: consecutive launches of a decode step whose grid
+    // sizes differ (148 and 128 CTAs at N = 2048 with 16-row shares) were measured ~1 us slower
+    // each (S = 8 step: 751 -> 575 us with 148 CTAs for every shape).
+    const int G = max(1, min(c.sm_count, (N + 7) / 8));
     const int rows_per_cta = (N + G - 1) / G;
     auto xoff_of = [&](int rg, int u) { return ((size_t)u * 16 * rg * kSkWRowBytes + 127) / 128 * 128; };
     auto red_of = [&](int rg) { return (size_t)8 * SP * (16 * rg + 4) * sizeof(float); };
@@ -474,11 +493,12 @@ cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmO
     a.status = c.status;
     const dim3 grid(G, (M + SP - 1) / SP);
     const bool bf16 = A.type == MGPU_BF16;
+    a.shape = skinny_shape(NT, RG, subs);
     if (NT == 1)
-        return bf16 ? dispatch_rg<1, __nv_bfloat16>(c, RG, subs, tm, tx, a, grid, smem)
-                    : dispatch_rg<1, __half>(c, RG, subs, tm, tx, a, grid, smem);
-    return bf16 ? dispatch_rg<2, __nv_bfloat16>(c, RG, subs, tm, tx, a, grid, smem)
-                : dispatch_rg<2, __half>(c, RG, subs, tm, tx, a, grid, smem);
+        return bf16 ? launch_skinny<1, __nv_bfloat16>(c, tm, tx, a, grid, smem)
+                    : launch_skinny<1, __half>(c, tm, tx, a, grid, smem);
+    return bf16 ? launch_skinny<2, __nv_bfloat16>(c, tm, tx, a, grid, smem)
+                : launch_skinny<2, __half>(c, tm, tx, a, grid, smem);
 }
 
 }  // namespace mgpu_k
