@@ -1115,6 +1115,26 @@ def run_batched_decode(dev, mg, torch, stream, peaks, layers, Wh, K_h, n_head, s
 # reference arm: the reference's quantised path as its CPU restatement (the reference has no
 # Q4_0 kernel of its own and no runnable OpenCL here), on the host cores
 # --------------------------------------------------------------------------------------
+def ncu_case_batched(args) -> dict:
+    """Capture case for ncu: four back-to-back batched-decode GEMMs (S = 8 sequences against the
+    qkv weights, Q4_0, bf16 activations and output), nothing else timed."""
+    import torch
+
+    import mvlm_b200 as mg
+    dev = mg.Device(0)
+    S, K, N = 8, 2048, 6144
+    tmp = dev.empty(K * N, mg.F32)
+    W = make_q(dev, mg, tmp, mg.Q4_0, K, N, SEED + 41)
+    A = dev.empty(S * K, mg.BF16)
+    dev.fill_normal(A, S * K, SEED + 42, 1.0)
+    C = dev.empty(S * N, mg.BF16)
+    for _ in range(4):
+        mg.gemm_q(dev, A, W, C, S, N, K, mg.Q4_0)
+    dev.finish()
+    torch.cuda.synchronize()
+    return {"ncu_case": args.ncu_case, "launches": 4, "S": S, "K": K, "N": N}
+
+
 def run_reference(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
@@ -1144,6 +1164,9 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the fp32 GEMV, batched-decode and SigLIP sections")
+    ap.add_argument("--ncu-case", choices=["decode", "batched_s8_qkv"], default="decode",
+                    help="with --ncu: the decode step (default), or four launches of the batched-decode GEMM "
+                         "(S=8, qkv 2048x6144, Q4_0, bf16) for a capture of that kernel")
     ap.add_argument("--ncu", action="store_true",
                     help="capture mode for ncu: only the decode step (3 timed steps), no e2e, parity or other "
                          "sections, so that a launch list or a capture holds the step's kernels alone")
@@ -1157,6 +1180,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         line = run_reference(args, rank, world)
+    elif args.ncu and args.ncu_case != "decode":
+        line = ncu_case_batched(args)
     else:
         line = run_ours(args, rank, world, local_rank)
     if line is not None and rank == 0:

@@ -951,11 +951,7 @@ struct GemvQLaunch {
             attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
             attr[0].val.programmaticStreamSerializationAllowed = 1;
             cfg.attrs = attr;
-#ifdef MGPU_GEMV_NO_PDL
-            cfg.numAttrs = 0;
-#else
             cfg.numAttrs = 1;
-#endif
             return cudaLaunchKernelEx(&cfg, kern, a);
         }
         template <int RPT, typename XT2, typename YT2>
@@ -986,11 +982,7 @@ struct GemvQLaunch {
             attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
             attr[0].val.programmaticStreamSerializationAllowed = 1;
             cfg.attrs = attr;
-#ifdef MGPU_GEMV_NO_PDL
-            cfg.numAttrs = 0;
-#else
             cfg.numAttrs = 1;
-#endif
             return cudaLaunchKernelEx(&cfg, kern, a);
         }
     };
