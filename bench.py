@@ -371,6 +371,29 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
     layer_bytes = sum(qbytes(qt, K, N) for _, K, N in LAYER_SHAPES) * LAYERS
     step_bytes = world * layer_bytes + qbytes(qt, K_h, N_h)
 
+    # ---- where a step's time goes (untimed steps, CUDA events between the phases, mean of
+    # each phase over the steps, max over ranks) ----
+    phases = ["layers", "hidden_all_gather", "head_convert_gemm_argmax", "pairs_all_to_all", "combine"]
+    reps = 20
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(len(phases) + 1)] for _ in range(reps)]
+    for ev in marks:
+        ev[0].record(stream)
+        g_layers.launch()
+        ev[1].record(stream)
+        dist.all_gather_into_tensor(Hall_t, hid_t)
+        ev[2].record(stream)
+        g_head.launch()
+        ev[3].record(stream)
+        dist.all_to_all_single(recv_t, pairs_t)
+        ev[4].record(stream)
+        mg.argmax_combine(dev, recv, world, N_h, tok)
+        ev[5].record(stream)
+    torch.cuda.synchronize()
+    per = torch.tensor([sum(ev[i].elapsed_time(ev[i + 1]) for ev in marks) / reps * 1e3 for i in range(len(phases))],
+                       dtype=torch.float64, device="cuda")
+    dist.all_reduce(per, op=dist.ReduceOp.MAX)
+    breakdown = {name: round(float(v), 2) for name, v in zip(phases, per.tolist())}
+
     # ---- parity, after the timed region: every sequence's full logits (the ranks' shards
     # gathered on rank 0) against the oracle's lm_head on the same bf16 hidden state, within the
     # fp32 tolerance; every rank's token against the argmax of its sequence's full row ----
@@ -442,7 +465,8 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
                   "mgpu_gemm_q (lm_head shard, M = N) and mgpu_argmax_rows + NCCL all-to-all of the pairs + "
                   "mgpu_argmax_combine + mgpu_buf_read_async (its 8-byte greedy result)"}
     return {"ms": ms, "step_bytes": step_bytes, "layer_bytes": layer_bytes, "n_head": n_head, "parity": parity,
-            "e2e": e2e, "clocks": clocks, "launches_per_step": len(links) + 4, "links": links, "Wh": Wh}
+            "e2e": e2e, "clocks": clocks, "launches_per_step": len(links) + 4, "links": links, "Wh": Wh,
+            "breakdown_us": breakdown}
 
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
@@ -476,6 +500,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                                                multi["clocks"])
         links, Wh, n_head = multi["links"], multi["Wh"], multi["n_head"]
         launches_per_step = multi["launches_per_step"]
+        secondary_multi = {"step_breakdown_us": multi["breakdown_us"]}
     else:
         n_head = HEAD[2]
         links, x0 = build_decode_step(dev, mg, tmp, qt, n_head, 0)
@@ -521,7 +546,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             e2e = run_e2e(args, dev, mg, torch, stream, qt, links, x0, argbuf, step_bytes)
 
     # ---------------- secondary measurements ----------------
-    secondary = {}
+    secondary = {} if world == 1 else dict(secondary_multi)
     if world == 1 and not args.no_secondary:
         per_launch_logits = yh.read(np.float32)
         secondary["chain_kernel"] = _guarded(run_chain_kernel, dev, mg, torch, stream, peaks, qt, links, step_bytes)

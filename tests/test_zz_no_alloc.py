@@ -43,10 +43,14 @@ def test_noalloc_matches_allocating_entry_fp16_image(dev):
     y_ref, y_new = dev.empty(N, mg.F16), dev.empty(N, mg.F16)
     mg.dispatch_gemv(dev, None, dx, img, y_ref, N, K).wait()
     ref = O.f16_to_f32(y_ref.read(np.uint16))
+    # the oracle's restatement of the reference gemv on the same fp16 data
+    assert_close(ref, O.f16_to_f32(O.gemv_f16(x, W, N, K)), TOL_16, "dispatch_gemv fp16 image")
     for _ in range(2):
         mg.dispatch_gemv_noalloc(dev, dx, img, y_new, N, K)
         dev.finish()
-        assert_close(O.f16_to_f32(y_new.read(np.uint16)), ref, TOL_16, "noalloc fp16 image")
+        got = O.f16_to_f32(y_new.read(np.uint16))
+        assert_close(got, ref, TOL_16, "noalloc fp16 image")
+        assert_close(got, O.f16_to_f32(O.gemv_f16(x, W, N, K)), TOL_16, "noalloc fp16 image vs oracle")
 
 
 def test_noalloc_largest_size_and_mixed_types(dev):
@@ -60,11 +64,13 @@ def test_noalloc_largest_size_and_mixed_types(dev):
     y_ref, y_new = dev.empty(N, mg.F32), dev.empty(N, mg.F32)
     mg.dispatch_gemv(dev, None, dx, dW, y_ref, N, K).wait()
     ref = y_ref.read(np.float32)
+    oracle = O.gemv_f32(x, W, N, K)
+    assert_close(ref, oracle, TOL_F32, "dispatch_gemv fp32 at the size limit")
     for _ in range(2):
         y_new.write(np.full(N, np.nan, np.float32))
         mg.dispatch_gemv_noalloc(dev, dx, dW, y_new, N, K)
         dev.finish()
-        assert_close(y_new.read(np.float32), ref, TOL_F32, "noalloc fp32 at the size limit")
+        assert_close(y_new.read(np.float32), oracle, TOL_F32, "noalloc fp32 at the size limit")
     K, N = 1024, 3000
     xb = O.bf16(O.uniform(K, 13))
     Wh = O.f16(O.uniform(K * N, 14))
@@ -72,10 +78,33 @@ def test_noalloc_largest_size_and_mixed_types(dev):
     y_ref, y_new = dev.empty(N, mg.F16), dev.empty(N, mg.F16)
     mg.dispatch_gemv(dev, None, dx, dW, y_ref, N, K).wait()
     ref = O.f16_to_f32(y_ref.read(np.uint16))
+    oracle = O.gemv_f32(O.bf16_to_f32(xb), O.f16_to_f32(Wh), N, K)
+    assert_close(ref, oracle, TOL_16, "dispatch_gemv bf16 x, f16 W and y")
     for _ in range(2):
         mg.dispatch_gemv_noalloc(dev, dx, dW, y_new, N, K)
         dev.finish()
-        assert_close(O.f16_to_f32(y_new.read(np.uint16)), ref, TOL_16, "noalloc bf16 x, f16 W and y")
+        assert_close(O.f16_to_f32(y_new.read(np.uint16)), oracle, TOL_16, "noalloc bf16 x, f16 W and y")
+
+
+def test_noalloc_allocates_nothing(dev):
+    # the device's free memory is the same before and after a run of calls (cudaMalloc
+    # reserves in 2 MiB pages, so any allocation would show); the allocating entry, for
+    # contrast, may grow the library's scratch arena on its first split-K call
+    import torch
+    K, N = 4096, 16384
+    dx = dev.array(O.uniform(K, 21), mg.F32)
+    dW = dev.array(O.uniform(K * N, 22), mg.F32, mg.LAYOUT_KN)
+    y = dev.empty(N, mg.F32)
+    mg.dispatch_gemv_noalloc(dev, dx, dW, y, N, K)  # first use: the array's address lookup
+    dev.finish()
+    free0, _ = torch.cuda.mem_get_info(dev.ordinal)
+    for _ in range(20):
+        mg.dispatch_gemv_noalloc(dev, dx, dW, y, N, K)
+    dev.finish()
+    free1, _ = torch.cuda.mem_get_info(dev.ordinal)
+    assert free1 == free0, (free0, free1)
+    assert_close(y.read(np.float32), O.gemv_f32(O.uniform(K, 21), O.uniform(K * N, 22), N, K), TOL_F32,
+                 "noalloc after 20 calls")
 
 
 def test_noalloc_rejects_sizes_beyond_its_array(dev):
