@@ -282,9 +282,9 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
     - Layers: each rank runs its own sequence's token through the 24 layers (96 dependent
       gemv_q_stream launches, captured once as a graph); the weights are the same model on every
       rank (replicated), the activations its own; no exchange.
-    - lm_head, column-sharded: the ranks' final hidden states are all-gathered (NCCL, 8 KB per
-      rank), converted to bf16, and every rank applies its 51200/N rows of the lm_head to all N
-      sequences (the skinny GEMM, M = N, fp32 logits).
+    - lm_head, column-sharded: each rank converts its final hidden state to bf16, the N of them
+      are all-gathered (NCCL, 4 KB per rank), and every rank applies its 51200/N rows of the
+      lm_head to all N sequences (the skinny GEMM, M = N, fp32 logits).
     - Greedy token: mgpu_argmax_rows gives each sequence's {index, value} over this rank's
       columns; an NCCL all-to-all sends sequence s's pair to rank s (8 bytes per pair), and
       mgpu_argmax_combine turns the N pairs into that sequence's token on its own GPU.
@@ -310,9 +310,10 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
             prev = y
     assert links[-1][3] is hidden
     Wh = make_q(dev, mg, tmp, qt, K_h, n_head, head_seed(rank))
-    Hall_t = torch.empty(world * K_h, dtype=torch.float32, device="cuda")
-    Hall = dev.wrap(Hall_t.data_ptr(), world * K_h * 4, mg.F32)
-    Hb = dev.empty(world * K_h, mg.BF16)
+    hb_t = torch.empty(K_h, dtype=torch.bfloat16, device="cuda")
+    hb = dev.wrap(hb_t.data_ptr(), K_h * 2, mg.BF16)
+    Hall_t = torch.empty(world * K_h, dtype=torch.bfloat16, device="cuda")
+    Hall = dev.wrap(Hall_t.data_ptr(), world * K_h * 2, mg.BF16)
     logits = dev.empty(world * n_head, mg.F32)
     pairs_t = torch.zeros(2 * world, dtype=torch.int32, device="cuda")
     pairs = dev.wrap(pairs_t.data_ptr(), 8 * world, mg.F32)
@@ -323,10 +324,10 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
 
     def layers_enqueue():
         enqueue_links(dev, mg, qt, links)
+        dev.convert(hidden, hb, K_h)
 
     def head_enqueue():
-        dev.convert(Hall, Hb, world * K_h)
-        mg.gemm_q(dev, Hb, Wh, logits, world, n_head, K_h, qt)
+        mg.gemm_q(dev, Hall, Wh, logits, world, n_head, K_h, qt)
         mg.argmax_rows(dev, logits, world, n_head, n_head, pairs)
 
     def capture(fn):
@@ -340,7 +341,7 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
 
     def step():
         g_layers.launch()
-        dist.all_gather_into_tensor(Hall_t, hid_t)
+        dist.all_gather_into_tensor(Hall_t, hb_t)
         g_head.launch()
         dist.all_to_all_single(recv_t, pairs_t)
         mg.argmax_combine(dev, recv, world, N_h, tok)
@@ -373,14 +374,14 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
 
     # ---- where a step's time goes (untimed steps, CUDA events between the phases, mean of
     # each phase over the steps, max over ranks) ----
-    phases = ["layers", "hidden_all_gather", "head_convert_gemm_argmax", "pairs_all_to_all", "combine"]
+    phases = ["layers_and_bf16", "hidden_all_gather", "head_gemm_argmax", "pairs_all_to_all", "combine"]
     reps = 20
     marks = [[torch.cuda.Event(enable_timing=True) for _ in range(len(phases) + 1)] for _ in range(reps)]
     for ev in marks:
         ev[0].record(stream)
         g_layers.launch()
         ev[1].record(stream)
-        dist.all_gather_into_tensor(Hall_t, hid_t)
+        dist.all_gather_into_tensor(Hall_t, hb_t)
         ev[2].record(stream)
         g_head.launch()
         ev[3].record(stream)
@@ -408,7 +409,7 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
     dist.all_gather(toks, tok_t)
     parity = {"ok": True}
     if rank == 0:
-        H = O.bf16_to_f32(O.bf16(Hall.read(np.float32))).reshape(world, K_h)
+        H = O.bf16_to_f32(Hall.read(np.uint16)).reshape(world, K_h)
         parts = []
         for r in range(world):
             a, b = column_shard(N_h, world, r)
@@ -461,8 +462,8 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
     e2e = {"value": round(step_bytes / (ems * 1e-3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": d2h, "ms_per_step": round(ems, 5), "steps": e2e_steps,
            "api": "per rank: mgpu_buf_write_async (its sequence's hidden state, pinned) + mgpu_graph_launch of the "
-                  "96 layer mgpu_gemv_q + NCCL all-gather of the hidden states + mgpu_graph_launch of mgpu_convert, "
-                  "mgpu_gemm_q (lm_head shard, M = N) and mgpu_argmax_rows + NCCL all-to-all of the pairs + "
+                  "96 layer mgpu_gemv_q and the hidden state's mgpu_convert to bf16 + NCCL all-gather of the hidden "
+                  "states + mgpu_graph_launch of mgpu_gemm_q (lm_head shard, M = N) and mgpu_argmax_rows + NCCL all-to-all of the pairs + "
                   "mgpu_argmax_combine + mgpu_buf_read_async (its 8-byte greedy result)"}
     return {"ms": ms, "step_bytes": step_bytes, "layer_bytes": layer_bytes, "n_head": n_head, "parity": parity,
             "e2e": e2e, "clocks": clocks, "launches_per_step": len(links) + 4, "links": links, "Wh": Wh,
@@ -599,7 +600,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                    "l2": "inputs larger than L2: 738 MB of packed weights per step vs 126 MB L2",
                    "parallelism": "single GPU" if world == 1 else
                    f"sequences x{world} (one per GPU, layer weights replicated); lm_head column-shard x{world} "
-                   f"applied to all {world} sequences; NCCL all-gather of the hidden states (8 KB per GPU) and "
+                   f"applied to all {world} sequences; NCCL all-gather of the bf16 hidden states (4 KB per GPU) and "
                    f"all-to-all of the greedy (index, value) pairs (8 bytes per sequence and GPU)",
                    "seed": SEED, "prng": "SplitMix64 + Box-Muller (device)"},
         "roofline": {"bound": "hbm", "kernel": "gemv_q_stream", "launches_per_step": len(links),

@@ -238,7 +238,22 @@ __global__ void __launch_bounds__(1024) argmax_kernel(int type, const void* __re
     out += 2 * blockIdx.x;
     float best = -1e30f;
     int bi = 0x7FFFFFFF;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    // eight of a thread's values loaded before any is compared, so that their loads are in
+    // flight together; the comparisons stay in index order (first maximum)
+    constexpr int U = 8;
+    int i0 = threadIdx.x;
+    for (; i0 + (U - 1) * (int)blockDim.x < n; i0 += U * blockDim.x) {
+        float v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) v[u] = argmax_value(type, x, base + i0 + u * blockDim.x);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (v[u] > best) {
+                best = v[u];
+                bi = i0 + u * blockDim.x;
+            }
+    }
+    for (int i = i0; i < n; i += blockDim.x) {
         const float v = argmax_value(type, x, base + i);
         if (v > best) {
             best = v;
