@@ -283,13 +283,16 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
       gemv_q_stream launches, captured once as a graph); the weights are the same model on every
       rank (replicated), the activations its own; no exchange.
     - lm_head, column-sharded: each rank converts its final hidden state to bf16, the N of them
-      are all-gathered (NCCL, 4 KB per rank), and every rank applies its 51200/N rows of the
-      lm_head to all N sequences (the skinny GEMM, M = N, fp32 logits).
+      are all-gathered over NVLink (mgpu_peer_allgather: stores into every peer's receive slots,
+      4 KB per rank), and every rank applies its 51200/N rows of the lm_head to all N sequences
+      (the skinny GEMM, M = N, fp32 logits).
     - Greedy token: mgpu_argmax_rows gives each sequence's {index, value} over this rank's
-      columns; an NCCL all-to-all sends sequence s's pair to rank s (8 bytes per pair), and
+      columns; mgpu_peer_alltoall sends sequence s's pair to rank s (8 bytes per pair), and
       mgpu_argmax_combine turns the N pairs into that sequence's token on its own GPU.
-    Whole-job bytes per step: N x the layer weights (each rank streams them for its sequence) +
-    the lm_head once; the time is the max over ranks of the device time per step."""
+    The whole step is one captured graph per rank (no collective-library call, no host round
+    trip between the phases).  Whole-job bytes per step: N x the layer weights (each rank
+    streams them for its sequence) + the lm_head once; the time is the max over ranks of the
+    device time per step."""
     from mvlm_b200.shard import column_shard
     K_h, N_h = HEAD[1], HEAD[2]
     h0, h1 = column_shard(N_h, world, rank)
@@ -310,41 +313,45 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
             prev = y
     assert links[-1][3] is hidden
     Wh = make_q(dev, mg, tmp, qt, K_h, n_head, head_seed(rank))
-    hb_t = torch.empty(K_h, dtype=torch.bfloat16, device="cuda")
-    hb = dev.wrap(hb_t.data_ptr(), K_h * 2, mg.BF16)
-    Hall_t = torch.empty(world * K_h, dtype=torch.bfloat16, device="cuda")
-    Hall = dev.wrap(Hall_t.data_ptr(), world * K_h * 2, mg.BF16)
+    hb = dev.empty(K_h, mg.BF16)
     logits = dev.empty(world * n_head, mg.F32)
-    pairs_t = torch.zeros(2 * world, dtype=torch.int32, device="cuda")
-    pairs = dev.wrap(pairs_t.data_ptr(), 8 * world, mg.F32)
-    recv_t = torch.zeros(2 * world, dtype=torch.int32, device="cuda")
-    recv = dev.wrap(recv_t.data_ptr(), 8 * world, mg.F32)
+    pairs = dev.empty(2 * world, mg.F32)
     tok_t = torch.zeros(2, dtype=torch.int32, device="cuda")
     tok = dev.wrap(tok_t.data_ptr(), 8, mg.F32)
+    # the two exchanges over peer memory (NVLink): receive slots mapped by every rank through
+    # CUDA IPC, the 64-byte handles exchanged once with torch.distributed
+    g_hid = mg.PeerGroup(dev, rank, world, K_h * 2)
+    g_pair = mg.PeerGroup(dev, rank, world, 8)
+    for grp in (g_hid, g_pair):
+        handles = [None] * world
+        dist.all_gather_object(handles, grp.handle())
+        grp.connect(handles)
+    Hall = g_hid.slots(mg.BF16)   # [world][K_h]: every sequence's hidden state
+    recv = g_pair.slots(mg.F32)   # [world][2]: this sequence's pair from every rank
 
-    def layers_enqueue():
-        enqueue_links(dev, mg, qt, links)
-        dev.convert(hidden, hb, K_h)
+    phases = [("layers_and_bf16", lambda: (enqueue_links(dev, mg, qt, links), dev.convert(hidden, hb, K_h))),
+              ("hidden_all_gather", lambda: g_hid.allgather(hb, K_h * 2)),
+              ("head_gemm_argmax", lambda: (mg.gemm_q(dev, Hall, Wh, logits, world, n_head, K_h, qt),
+                                            mg.argmax_rows(dev, logits, world, n_head, n_head, pairs))),
+              ("pairs_all_to_all", lambda: g_pair.alltoall(pairs, 8)),
+              ("combine", lambda: mg.argmax_combine(dev, recv, world, N_h, tok))]
 
-    def head_enqueue():
-        mg.gemm_q(dev, Hall, Wh, logits, world, n_head, K_h, qt)
-        mg.argmax_rows(dev, logits, world, n_head, n_head, pairs)
+    def step_enqueue():
+        for _, fn in phases:
+            fn()
 
     def capture(fn):
+        # an eager pass first (every rank in the same order: the exchanges run in lockstep)
         fn()
         dev.finish()
         dev.capture_begin()
         fn()
         return dev.capture_end()
 
-    g_layers, g_head = capture(layers_enqueue), capture(head_enqueue)
+    g_step = capture(step_enqueue)
 
     def step():
-        g_layers.launch()
-        dist.all_gather_into_tensor(Hall_t, hb_t)
-        g_head.launch()
-        dist.all_to_all_single(recv_t, pairs_t)
-        mg.argmax_combine(dev, recv, world, N_h, tok)
+        g_step.launch()
 
     for _ in range(args.warmup):
         step()
@@ -372,28 +379,22 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
     layer_bytes = sum(qbytes(qt, K, N) for _, K, N in LAYER_SHAPES) * LAYERS
     step_bytes = world * layer_bytes + qbytes(qt, K_h, N_h)
 
-    # ---- where a step's time goes (untimed steps, CUDA events between the phases, mean of
-    # each phase over the steps, max over ranks) ----
-    phases = ["layers_and_bf16", "hidden_all_gather", "head_gemm_argmax", "pairs_all_to_all", "combine"]
+    # ---- where a step's time goes (untimed steps, each phase its own graph with CUDA events
+    # between them, mean over the steps, max over ranks) ----
+    g_phases = [capture(fn) for _, fn in phases]
     reps = 20
     marks = [[torch.cuda.Event(enable_timing=True) for _ in range(len(phases) + 1)] for _ in range(reps)]
     for ev in marks:
         ev[0].record(stream)
-        g_layers.launch()
-        ev[1].record(stream)
-        dist.all_gather_into_tensor(Hall_t, hb_t)
-        ev[2].record(stream)
-        g_head.launch()
-        ev[3].record(stream)
-        dist.all_to_all_single(recv_t, pairs_t)
-        ev[4].record(stream)
-        mg.argmax_combine(dev, recv, world, N_h, tok)
-        ev[5].record(stream)
+        for i, gph in enumerate(g_phases):
+            gph.launch()
+            ev[i + 1].record(stream)
     torch.cuda.synchronize()
     per = torch.tensor([sum(ev[i].elapsed_time(ev[i + 1]) for ev in marks) / reps * 1e3 for i in range(len(phases))],
                        dtype=torch.float64, device="cuda")
     dist.all_reduce(per, op=dist.ReduceOp.MAX)
-    breakdown = {name: round(float(v), 2) for name, v in zip(phases, per.tolist())}
+    breakdown = {name: round(float(v), 2) for (name, _), v in zip(phases, per.tolist())}
+    del g_phases
 
     # ---- parity, after the timed region: every sequence's full logits (the ranks' shards
     # gathered on rank 0) against the oracle's lm_head on the same bf16 hidden state, within the
@@ -435,10 +436,13 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
         host_x = np.ctypeslib.as_array((ctypes_float() * (h2d // 4)).from_address(hx))
         host_x[:] = np.random.default_rng(SEED + rank).standard_normal(h2d // 4).astype(np.float32)
 
+        # the copies from and to pinned memory captured with the step: one graph launch per token
+        g_e2e = capture(lambda: (mg._check(L.mgpu_buf_write_async(x0.h, 0, hx, h2d), "buf_write_async"),
+                                 step_enqueue(),
+                                 mg._check(L.mgpu_buf_read_async(tok.h, 0, hy, d2h), "buf_read_async")))
+
         def one():
-            mg._check(L.mgpu_buf_write_async(x0.h, 0, hx, h2d), "buf_write_async")
-            step()
-            mg._check(L.mgpu_buf_read_async(tok.h, 0, hy, d2h), "buf_read_async")
+            g_e2e.launch()
 
         for _ in range(3):
             one()
@@ -455,18 +459,22 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
         t = torch.tensor([ems], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ems = float(t[0])
+        del g_e2e
     finally:
         L.mgpu_host_free(hx)
         L.mgpu_host_free(hy)
-    del g_layers, g_head
+    del g_step
     e2e = {"value": round(step_bytes / (ems * 1e-3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": d2h, "ms_per_step": round(ems, 5), "steps": e2e_steps,
-           "api": "per rank: mgpu_buf_write_async (its sequence's hidden state, pinned) + mgpu_graph_launch of the "
-                  "96 layer mgpu_gemv_q and the hidden state's mgpu_convert to bf16 + NCCL all-gather of the hidden "
-                  "states + mgpu_graph_launch of mgpu_gemm_q (lm_head shard, M = N) and mgpu_argmax_rows + NCCL all-to-all of the pairs + "
-                  "mgpu_argmax_combine + mgpu_buf_read_async (its 8-byte greedy result)"}
+           "api": "per rank, one mgpu_graph_launch per token of: mgpu_buf_write_async (its sequence's hidden state, "
+                  "pinned), the 96 layer mgpu_gemv_q, mgpu_convert of the hidden state to bf16, mgpu_peer_allgather "
+                  "(4 KB per GPU over NVLink), mgpu_gemm_q (lm_head shard, M = N), mgpu_argmax_rows, "
+                  "mgpu_peer_alltoall (8 bytes per sequence and GPU), mgpu_argmax_combine, mgpu_buf_read_async (its "
+                  "8-byte greedy result)"}
+    g_hid.destroy()
+    g_pair.destroy()
     return {"ms": ms, "step_bytes": step_bytes, "layer_bytes": layer_bytes, "n_head": n_head, "parity": parity,
-            "e2e": e2e, "clocks": clocks, "launches_per_step": len(links) + 4, "links": links, "Wh": Wh,
+            "e2e": e2e, "clocks": clocks, "launches_per_step": len(links) + 6, "links": links, "Wh": Wh,
             "breakdown_us": breakdown}
 
 
@@ -600,8 +608,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                    "l2": "inputs larger than L2: 738 MB of packed weights per step vs 126 MB L2",
                    "parallelism": "single GPU" if world == 1 else
                    f"sequences x{world} (one per GPU, layer weights replicated); lm_head column-shard x{world} "
-                   f"applied to all {world} sequences; NCCL all-gather of the bf16 hidden states (4 KB per GPU) and "
-                   f"all-to-all of the greedy (index, value) pairs (8 bytes per sequence and GPU)",
+                   f"applied to all {world} sequences; all-gather of the bf16 hidden states (4 KB per GPU) and "
+                   f"all-to-all of the greedy (index, value) pairs (8 bytes per sequence and GPU) over NVLink "
+                   f"peer memory (mgpu_peer_allgather / mgpu_peer_alltoall), one graph per step",
                    "seed": SEED, "prng": "SplitMix64 + Box-Muller (device)"},
         "roofline": {"bound": "hbm", "kernel": "gemv_q_stream", "launches_per_step": len(links),
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -647,9 +656,10 @@ def check_decode_parity(mg, qt, links) -> dict:
 def run_e2e(args, dev, mg, torch, stream, qt, links, x0, argbuf, step_bytes) -> dict:
     """The step through the public C ABI, from pinned host memory to pinned host memory, as an
     engine drives a decode token: mgpu_buf_write_async of the token's hidden state (8 KB), the
-    captured step (97 mgpu_gemv_q and the device argmax of the logits, mgpu_argmax) replayed with
-    mgpu_graph_launch, and one mgpu_buf_read_async of the 8-byte greedy result.  Device time of
-    the whole loop, copies included, by CUDA events on the stream."""
+    97 mgpu_gemv_q, the device argmax of the logits (mgpu_argmax) and one mgpu_buf_read_async of
+    the 8-byte greedy result, all captured once (the copies from and to pinned memory become
+    graph nodes) and replayed with mgpu_graph_launch, one launch per token.  Device time of the
+    whole loop, copies included, by CUDA events on the stream."""
     L = mg.lib()
     yh = links[-1][3]
     n_head = links[-1][4]
@@ -661,8 +671,10 @@ def run_e2e(args, dev, mg, torch, stream, qt, links, x0, argbuf, step_bytes) -> 
         host_x[:] = np.random.default_rng(SEED).standard_normal(h2d // 4).astype(np.float32)
 
         def enqueue():
+            mg._check(L.mgpu_buf_write_async(x0.h, 0, hx, h2d), "buf_write_async")
             enqueue_links(dev, mg, qt, links)
             mg.argmax(dev, yh, n_head, argbuf)
+            mg._check(L.mgpu_buf_read_async(argbuf.h, 0, hy, d2h), "buf_read_async")
 
         enqueue()  # eager pass: validates arguments outside the capture
         dev.finish()
@@ -671,9 +683,7 @@ def run_e2e(args, dev, mg, torch, stream, qt, links, x0, argbuf, step_bytes) -> 
         graph = dev.capture_end()
 
         def one():
-            mg._check(L.mgpu_buf_write_async(x0.h, 0, hx, h2d), "buf_write_async")
             graph.launch()
-            mg._check(L.mgpu_buf_read_async(argbuf.h, 0, hy, d2h), "buf_read_async")
 
         steps = max(3, min(args.steps, 2000))
         for _ in range(3):
@@ -689,8 +699,9 @@ def run_e2e(args, dev, mg, torch, stream, qt, links, x0, argbuf, step_bytes) -> 
         ms = e0.elapsed_time(e1) / steps
         return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 5), "steps": steps,
-                "api": "mgpu_buf_write_async (the token's hidden state, pinned) + mgpu_graph_launch of the "
-                       "captured 97 mgpu_gemv_q + mgpu_argmax + mgpu_buf_read_async (the 8-byte greedy result)"}
+                "api": "one mgpu_graph_launch per token of the captured mgpu_buf_write_async (the token's hidden "
+                       "state, pinned) + 97 mgpu_gemv_q + mgpu_argmax + mgpu_buf_read_async (the 8-byte greedy "
+                       "result, pinned)"}
     finally:
         L.mgpu_host_free(hx)
         L.mgpu_host_free(hy)

@@ -282,6 +282,37 @@ int mgpu_argmax_logits(const mgpu_device* dev, mgpu_buf* logits, int vocab_size)
  * result is argmax_logits' first maximum over the whole row.  One thread, one launch. */
 mgpu_event* mgpu_argmax_combine(const mgpu_device* dev, mgpu_buf* pairs, int n_ranks, int n_total, mgpu_buf* out);
 
+/* ---------------------------------------------------------------- peer groups ----- */
+/* New (the reference runs on one device): small exchanges between the GPUs of one node over
+ * NVLink, without a collective library, for the column-sharded lm_head of a batched decode
+ * (each GPU's hidden state to every GPU; each sequence's argmax pair to the GPU that owns it).
+ * A group holds, on each GPU, world receive slots of slot_bytes plus one flag per GPU, in one
+ * allocation that the other GPUs map through CUDA IPC.  Every GPU of a group must run the same
+ * exchanges in the same order; an exchange is one kernel on the device's stream that stores
+ * into the peers' slots, publishes its flags and waits (bounded, default 2 s; on expiry the
+ * device status reports MGPU_ERR_DEVICE_TIMEOUT) for the peers' flags.  Exchanges can be
+ * captured into graphs.  Set-up, once per group:
+ *   g = mgpu_peer_group_create(dev, rank, world, slot_bytes);
+ *   mgpu_peer_group_handle(g, mine);                  64 bytes, to send to every rank
+ *   mgpu_peer_group_connect(g, all);                  world x 64 bytes in rank order
+ * (or mgpu_peer_group_connect_ptrs with the peers' slot addresses when the groups live in one
+ * process).  The slots of this GPU are mgpu_peer_group_slots(g) (world x slot_bytes; slot r
+ * holds rank r's bytes); they stay valid until the next exchange on the group. */
+typedef struct mgpu_peer_group mgpu_peer_group;
+mgpu_peer_group* mgpu_peer_group_create(mgpu_device* dev, int rank, int world, size_t slot_bytes);
+int mgpu_peer_group_handle(const mgpu_peer_group* g, void* out64);
+int mgpu_peer_group_connect(mgpu_peer_group* g, const void* handles);
+int mgpu_peer_group_connect_ptrs(mgpu_peer_group* g, void* const* peer_slots);
+void* mgpu_peer_group_local_ptr(const mgpu_peer_group* g);
+mgpu_buf* mgpu_peer_group_slots(mgpu_peer_group* g);
+int mgpu_peer_group_set_wait_limit(mgpu_peer_group* g, uint64_t limit_ns);
+/* src (bytes, a multiple of 8, <= slot_bytes; src 16-byte aligned) into slot `rank` of every
+ * GPU.  slot_bytes is rounded up to a multiple of 8 at creation. */
+mgpu_event* mgpu_peer_allgather(mgpu_peer_group* g, const mgpu_buf* src, size_t bytes);
+/* bytes [p * bytes_per_peer, (p + 1) * bytes_per_peer) of src into slot `rank` of GPU p. */
+mgpu_event* mgpu_peer_alltoall(mgpu_peer_group* g, const mgpu_buf* src, size_t bytes_per_peer);
+void mgpu_peer_group_destroy(mgpu_peer_group* g);
+
 /* ---------------------------------------------------------------- events ---------- */
 int mgpu_wait_event(mgpu_event* ev);                 /* clWaitForEvents(1, &ev) */
 void mgpu_release_event(mgpu_event* ev);             /* clReleaseEvent */

@@ -85,6 +85,16 @@ SIGNATURES = {
     "mgpu_argmax_logits": (_i, [_vp, _vp, _i]),
     "mgpu_argmax_rows": (_vp, [_vp, _vp, _i, _i, _i64, _vp]),
     "mgpu_argmax_combine": (_vp, [_vp, _vp, _i, _i, _vp]),
+    "mgpu_peer_group_create": (_vp, [_vp, _i, _i, _sz]),
+    "mgpu_peer_group_handle": (_i, [_vp, _vp]),
+    "mgpu_peer_group_connect": (_i, [_vp, _vp]),
+    "mgpu_peer_group_connect_ptrs": (_i, [_vp, _vp]),
+    "mgpu_peer_group_local_ptr": (_vp, [_vp]),
+    "mgpu_peer_group_slots": (_vp, [_vp]),
+    "mgpu_peer_group_set_wait_limit": (_i, [_vp, _u64]),
+    "mgpu_peer_allgather": (_vp, [_vp, _vp, _sz]),
+    "mgpu_peer_alltoall": (_vp, [_vp, _vp, _sz]),
+    "mgpu_peer_group_destroy": (None, [_vp]),
     "mgpu_wait_event": (_i, [_vp]),
     "mgpu_release_event": (None, [_vp]),
     "mgpu_profile_end": (_d, [_vp]),
@@ -493,6 +503,64 @@ def argmax_combine(dev: Device, pairs: Buffer, n_ranks: int, n_total: int, out: 
     """out (8 bytes) <- the global {index, value} from the ranks' gathered mgpu_argmax pairs of a
     row column-sharded over n_ranks GPUs (the reference's first maximum over the whole row)."""
     return _ev(lib().mgpu_argmax_combine(dev.h, pairs.h, n_ranks, n_total, out.h), "argmax_combine")
+
+
+class PeerGroup:
+    """Exchanges between the GPUs of one node through peer memory (mgpu_peer_group_*): world
+    receive slots of slot_bytes on every GPU, mapped by the others through CUDA IPC.  Connect
+    with the handles of all ranks in rank order (`handle()` on each, exchanged by the caller), or
+    with `connect_ptrs` when the groups live in one process."""
+
+    def __init__(self, dev: Device, rank: int, world: int, slot_bytes: int):
+        h = lib().mgpu_peer_group_create(dev.h, rank, world, slot_bytes)
+        if not h:
+            _raise_last("peer_group_create")
+        self.dev, self.h, self.rank, self.world = dev, h, rank, world
+        self.slot_bytes = (slot_bytes + 7) // 8 * 8
+
+    def handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        _check(lib().mgpu_peer_group_handle(self.h, buf), "peer_group_handle")
+        return buf.raw
+
+    def connect(self, handles):
+        blob = b"".join(handles)
+        if len(blob) != 64 * self.world:
+            raise MgpuError(ERR_INVALID_ARG, "peer_group_connect: one 64-byte handle per rank")
+        _check(lib().mgpu_peer_group_connect(self.h, blob), "peer_group_connect")
+        return self
+
+    def connect_ptrs(self, ptrs):
+        arr = (ctypes.c_void_p * self.world)(*ptrs)
+        _check(lib().mgpu_peer_group_connect_ptrs(self.h, arr), "peer_group_connect_ptrs")
+        return self
+
+    def local_ptr(self) -> int:
+        return lib().mgpu_peer_group_local_ptr(self.h)
+
+    def slots(self, type_: int) -> Buffer:
+        """A view of this GPU's slots (slot r = rank r's bytes), tagged with type_."""
+        v = lib().mgpu_buf_view(lib().mgpu_peer_group_slots(self.h), 0, self.world * self.slot_bytes)
+        if not v:
+            _raise_last("peer_group_slots")
+        return Buffer(self.dev, v, self.world * self.slot_bytes).set_format(type_)
+
+    def set_wait_limit(self, ns: int):
+        _check(lib().mgpu_peer_group_set_wait_limit(self.h, ns), "peer_group_set_wait_limit")
+
+    def allgather(self, src: Buffer, nbytes: int) -> Event:
+        return _ev(lib().mgpu_peer_allgather(self.h, src.h, nbytes), "peer_allgather")
+
+    def alltoall(self, src: Buffer, bytes_per_peer: int) -> Event:
+        return _ev(lib().mgpu_peer_alltoall(self.h, src.h, bytes_per_peer), "peer_alltoall")
+
+    def destroy(self):
+        if self.h and _lib is not None:
+            _lib.mgpu_peer_group_destroy(self.h)
+        self.h = None
+
+    def __del__(self):
+        self.destroy()
 
 
 def argmax_logits(dev: Device, logits: Buffer, vocab_size: int) -> int:

@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libmgpu.so")
-SOURCES = ["runtime.cu", "gemv.cu", "chain.cu", "gemm_tc.cu", "skinny.cu", "misc.cu"]
+SOURCES = ["runtime.cu", "gemv.cu", "chain.cu", "gemm_tc.cu", "skinny.cu", "misc.cu", "peer.cu"]
 HEADERS = ["common.cuh", "kernels.h", "qdot.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

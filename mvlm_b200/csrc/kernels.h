@@ -135,6 +135,24 @@ cudaError_t gemm_q4_skinny(const LaunchCtx& c, const GemmOperand& A, const GemmO
 // dims[2]; byte strides of dims 1 and 2 (multiples of 16, in any order); box {box[0..2]}.
 bool make_tensor_map_u16_3d(CUtensorMap* m, const void* ptr, const int64_t dims[3], const int64_t strides[2],
                             const int box[3]);
+// Exchange over peer memory (peer.cu): this GPU's `bytes` (from src, or src + p * src_stride
+// for peer p) into slot `rank` of every peer's receive region, then one flag per peer, then a
+// bounded wait for every peer's flag of this exchange.
+constexpr int kMaxPeers = 8;
+struct PeerExchangeArgs {
+    const uint8_t* src;
+    size_t src_stride;  // 0: the same bytes to every peer (all-gather); else per-peer chunks (all-to-all)
+    size_t bytes;       // per peer, a multiple of 8, <= slot_bytes (a multiple of 8)
+    size_t slot_bytes;
+    uint8_t* dst[kMaxPeers];                  // peer p's receive slots (this GPU's own for p == rank)
+    unsigned long long* dst_flag[kMaxPeers];  // peer p's flags
+    unsigned long long* my_flags;             // this GPU's flags (world entries)
+    unsigned long long* epoch;                // this GPU's exchange counter
+    int rank, world;
+    uint64_t limit_ns;
+    int* status;
+};
+cudaError_t peer_exchange(const LaunchCtx& c, const PeerExchangeArgs& a);
 // Why a GEMM request cannot run (nullptr when it can).
 const char* gemm_check(const GemmOperand& A, const GemmOperand& B, const GemmOperand& C, int M, int N, int K);
 

@@ -1333,3 +1333,166 @@ int mgpu_convert(const mgpu_device* cd, mgpu_buf* src, mgpu_buf* dst, int64_t n)
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ peer groups ------
+// Exchanges between the GPUs of one node through peer memory (peer.cu).  One allocation per GPU:
+// [world slots of slot_bytes, padded to 256][world u64 flags][u64 epoch], zeroed at creation.
+struct mgpu_peer_group {
+    mgpu_device* dev;
+    int rank, world;
+    size_t slot_bytes;
+    size_t slots_bytes;  // world * slot_bytes, rounded up to 256
+    void* base;
+    void* peer[mgpu_k::kMaxPeers];
+    bool opened[mgpu_k::kMaxPeers];  // mapped through CUDA IPC (unmapped on destroy)
+    bool connected;
+    uint64_t limit_ns;
+    mgpu_buf* slots;  // view of this GPU's slots, owned by the group
+};
+
+mgpu_peer_group* mgpu_peer_group_create(mgpu_device* d, int rank, int world, size_t slot_bytes) {
+    API_ENTRY();
+    REQUIRE(d && world >= 1 && world <= mgpu_k::kMaxPeers && rank >= 0 && rank < world && slot_bytes > 0,
+            "mgpu_peer_group_create: bad arguments (world 1..%d)", mgpu_k::kMaxPeers);
+    DeviceGuard g(d->ordinal);
+    mgpu_peer_group* pg = new mgpu_peer_group();
+    pg->dev = d;
+    pg->rank = rank;
+    pg->world = world;
+    pg->slot_bytes = (slot_bytes + 7) / 8 * 8;
+    pg->slots_bytes = ((size_t)world * pg->slot_bytes + 255) / 256 * 256;
+    pg->limit_ns = 2000000000ull;  // the kernels' bounded-wait limit: 2 s
+    const size_t total = pg->slots_bytes + 256;
+    if (!cuda_ok(cudaMalloc(&pg->base, total), "cudaMalloc(peer group)")) {
+        delete pg;
+        return nullptr;
+    }
+    if (!cuda_ok(cudaMemsetAsync(pg->base, 0, total, d->stream), "cudaMemsetAsync(peer group)") ||
+        !cuda_ok(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize")) {
+        cudaFree(pg->base);
+        delete pg;
+        return nullptr;
+    }
+    pg->slots = new_buf(d, pg->base, (size_t)world * pg->slot_bytes, false);
+    return pg;
+}
+
+int mgpu_peer_group_handle(const mgpu_peer_group* pg, void* out64) {
+    if (!pg || !out64) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_peer_group_handle: null argument");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+    DeviceGuard g(pg->dev->ordinal);
+    cudaIpcMemHandle_t h;
+    if (!cuda_ok(cudaIpcGetMemHandle(&h, pg->base), "cudaIpcGetMemHandle")) return t_err;
+    memcpy(out64, &h, sizeof(h));
+    return MGPU_OK;
+}
+
+int mgpu_peer_group_connect(mgpu_peer_group* pg, const void* handles) {
+    if (!pg || !handles || pg->connected) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_peer_group_connect: null argument or already connected");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    DeviceGuard g(pg->dev->ordinal);
+    for (int p = 0; p < pg->world; ++p) {
+        if (p == pg->rank) {
+            pg->peer[p] = pg->base;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char*>(handles) + (size_t)p * sizeof(h), sizeof(h));
+        if (!cuda_ok(cudaIpcOpenMemHandle(&pg->peer[p], h, cudaIpcMemLazyEnablePeerAccess),
+                     "cudaIpcOpenMemHandle")) {
+            for (int q = 0; q < p; ++q)
+                if (pg->opened[q]) cudaIpcCloseMemHandle(pg->peer[q]);
+            memset(pg->opened, 0, sizeof(pg->opened));
+            return t_err;
+        }
+        pg->opened[p] = true;
+    }
+    pg->connected = true;
+    return MGPU_OK;
+}
+
+int mgpu_peer_group_connect_ptrs(mgpu_peer_group* pg, void* const* peer_slots) {
+    if (!pg || !peer_slots || pg->connected) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_peer_group_connect_ptrs: null argument or already connected");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    for (int p = 0; p < pg->world; ++p) {
+        pg->peer[p] = p == pg->rank ? pg->base : peer_slots[p];
+        if (!pg->peer[p]) {
+            set_error(MGPU_ERR_INVALID_ARG, "mgpu_peer_group_connect_ptrs: no address for rank %d", p);
+            return MGPU_ERR_INVALID_ARG;
+        }
+    }
+    pg->connected = true;
+    return MGPU_OK;
+}
+
+void* mgpu_peer_group_local_ptr(const mgpu_peer_group* pg) { return pg ? pg->base : nullptr; }
+
+mgpu_buf* mgpu_peer_group_slots(mgpu_peer_group* pg) { return pg ? pg->slots : nullptr; }
+
+int mgpu_peer_group_set_wait_limit(mgpu_peer_group* pg, uint64_t limit_ns) {
+    if (!pg || limit_ns == 0) {
+        set_error(MGPU_ERR_INVALID_ARG, "mgpu_peer_group_set_wait_limit: bad arguments");
+        return MGPU_ERR_INVALID_ARG;
+    }
+    pg->limit_ns = limit_ns;
+    return MGPU_OK;
+}
+
+static mgpu_event* peer_exchange(mgpu_peer_group* pg, const mgpu_buf* src, size_t bytes, size_t stride,
+                                 const char* what) {
+    API_ENTRY();
+    REQUIRE(pg && src && pg->connected, "%s: group not connected or null source", what);
+    REQUIRE(bytes > 0 && bytes % 8 == 0 && bytes <= pg->slot_bytes, "%s: %zu bytes (a multiple of 8, at most %zu)",
+            what, bytes, pg->slot_bytes);
+    REQUIRE((reinterpret_cast<uintptr_t>(src->ptr) & 15) == 0, "%s: source not 16-byte aligned", what);
+    REQUIRE(src->bytes >= (stride ? (size_t)pg->world * stride : bytes), "%s: source too small", what);
+    mgpu_device* d = pg->dev;
+    DeviceGuard g(d->ordinal);
+    mgpu_k::PeerExchangeArgs a = {};
+    a.src = static_cast<const uint8_t*>(src->ptr);
+    a.src_stride = stride;
+    a.bytes = bytes;
+    a.slot_bytes = pg->slot_bytes;
+    for (int p = 0; p < pg->world; ++p) {
+        a.dst[p] = static_cast<uint8_t*>(pg->peer[p]);
+        a.dst_flag[p] = reinterpret_cast<unsigned long long*>(static_cast<char*>(pg->peer[p]) + pg->slots_bytes);
+    }
+    a.my_flags = reinterpret_cast<unsigned long long*>(static_cast<char*>(pg->base) + pg->slots_bytes);
+    a.epoch = a.my_flags + pg->world;
+    a.rank = pg->rank;
+    a.world = pg->world;
+    a.limit_ns = pg->limit_ns;
+    a.status = d->d_status;
+    mgpu_event* ev = event_begin(d);
+    if (!cuda_ok(mgpu_k::peer_exchange(ctx_of(d), a), what)) {
+        if (ev) d->event_pool.push_back(ev);
+        return nullptr;
+    }
+    return event_end(d, ev);
+}
+
+mgpu_event* mgpu_peer_allgather(mgpu_peer_group* pg, const mgpu_buf* src, size_t bytes) {
+    return peer_exchange(pg, src, bytes, 0, "mgpu_peer_allgather");
+}
+
+mgpu_event* mgpu_peer_alltoall(mgpu_peer_group* pg, const mgpu_buf* src, size_t bytes_per_peer) {
+    return peer_exchange(pg, src, bytes_per_peer, bytes_per_peer, "mgpu_peer_alltoall");
+}
+
+void mgpu_peer_group_destroy(mgpu_peer_group* pg) {
+    if (!pg) return;
+    DeviceGuard g(pg->dev->ordinal);
+    cudaStreamSynchronize(pg->dev->stream);
+    for (int p = 0; p < pg->world; ++p)
+        if (pg->opened[p]) cudaIpcCloseMemHandle(pg->peer[p]);
+    cudaFree(pg->base);
+    delete pg->slots;
+    delete pg;
+}
