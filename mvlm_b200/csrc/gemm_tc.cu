@@ -99,7 +99,32 @@ struct GemmArgs {
     // fp32 partials stay in shared memory and the cluster sums them over DSMEM (splits ==
     // csplit, tickets and partials unused).
     int csplit;
+    // Tile order: 0 = m-fastest over all of M; g > 0 = bands of g m-blocks, m-fastest inside a
+    // band, the bands one after the other, so that a band's A rows stay in L2 while every
+    // n-block passes over them (large M, where A does not fit L2 beside B).
+    int group_m;
 };
+
+// The (m-block, n-block) of tile index `tile` in the order above.
+__device__ __forceinline__ void tile_coords(const GemmArgs& g, int tile, int& m_blk, int& n_blk) {
+    if (g.group_m <= 0 || g.group_m >= g.tiles_m) {
+        m_blk = tile % g.tiles_m;
+        n_blk = tile / g.tiles_m;
+        return;
+    }
+    const int per_band = g.group_m * g.tiles_n;
+    const int band = tile / per_band;
+    const int first_m = band * g.group_m;
+    const int gm = min(g.group_m, g.tiles_m - first_m);  // the last band may be narrower
+    const int r = tile - band * per_band;
+    m_blk = first_m + r % gm;
+    n_blk = r / gm;
+}
+__device__ __forceinline__ int tile_n_blk(const GemmArgs& g, int tile) {
+    int m, n;
+    tile_coords(g, tile, m, n);
+    return n;
+}
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -351,7 +376,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             if constexpr (!kQuant) {
                 if (ufirst < total_units) {
                     const int tile = ufirst % total_tiles, kb0 = (ufirst / total_tiles) * g.kb_per_split;
-                    const int n_blk = tile / g.tiles_m;
+                    const int n_blk = tile_n_blk(g, tile);
                     pre = min(S, kb_end(kb0) - kb0);
                     for (int p = 0; p < pre; ++p) {
                         // fresh ring: every slot is free
@@ -363,7 +388,8 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int unit = ufirst; unit < total_units && !abort_flag; unit += ustep) {
                 const int tile = unit % total_tiles, kb0 = (unit / total_tiles) * g.kb_per_split;
-                const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
+                int m_blk, n_blk;
+                tile_coords(g, tile, m_blk, n_blk);
                 for (int kb = kb0; kb < kb_end(kb0); ++kb, ++it) {
                     const uint32_t s = it % S, ph = (it / S) & 1u;
                     uint8_t* a_dst = smem + s * SB;
@@ -445,7 +471,8 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         const bool vec_ok = (g.ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0);
         for (int unit = ufirst; unit < total_units; unit += ustep, ++tcount) {
             const int tile = unit % total_tiles, split = unit / total_tiles;
-            const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
+            int m_blk, n_blk;
+            tile_coords(g, tile, m_blk, n_blk);
             const uint32_t acc = tcount & 1u, acc_ph = (tcount >> 1) & 1u;
             if (abort_flag || !mbar_wait(&tfull_bar[acc], acc_ph, g.status)) {
                 abort_flag = 1;
@@ -607,7 +634,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             if (!mbar_wait(&pk_empty[slot], ((gi >> 1) & 1u) ^ 1u, g.status)) return false;
             mbar_arrive_expect_tx(&pk_full[slot], (uint32_t)(BNC * GB));
             // this CTA's B rows of the tile (pair mode: rows BNC * rank ..), into its own ring
-            tma_load_2d(pk + slot * (BNC * GB), &tmB, grp * (GB / 2), (tile / g.tiles_m) * BN + (int)rank * BNC,
+            tma_load_2d(pk + slot * (BNC * GB), &tmB, grp * (GB / 2), tile_n_blk(g, tile) * BN + (int)rank * BNC,
                         &pk_full[slot]);
             return true;
         };
@@ -684,7 +711,7 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
             const int unit = (int)blockIdx.x + (int)(it / g.kb_per_split) * (int)gridDim.x;
             const int tile = unit % total_tiles;
             const int kb = (unit / total_tiles) * g.kb_per_split + (int)(it % g.kb_per_split);
-            const int n_blk = live ? tile / g.tiles_m : 0;
+            const int n_blk = live ? tile_n_blk(g, tile) : 0;
 #pragma unroll
             for (int v = 0; v < UPT; ++v) {
                 const int u = dt + v * kDqWarps * 32;
@@ -740,7 +767,8 @@ __global__ void __launch_bounds__(gemm_threads(BMODE), 1)
         constexpr int RP = BN + 4;  // partial row pitch in floats
         constexpr int C4 = BN / 4;
         const int tile = ufirst % total_tiles;
-        const int m_blk = tile % g.tiles_m, n_blk = tile / g.tiles_m;
+        int m_blk, n_blk;
+        tile_coords(g, tile, m_blk, n_blk);
         const int rows_per = (BM + csplit - 1) / csplit;
         const int r0 = (int)ksplit * rows_per, r1 = min(BM, r0 + rows_per);
         uint32_t src[8];
@@ -1160,6 +1188,14 @@ cudaError_t gemm(const LaunchCtx& c, const GemmOperand& A, const GemmOperand& B,
     g.tickets = p.splits > 1 && p.csplit == 1 ? split->tickets : nullptr;
     g.partials = p.splits > 1 && p.csplit == 1 ? split->partials : nullptr;
     g.csplit = p.csplit;
+    // Tile order: when A is larger than ~3/4 of L2, bands of m-blocks whose A rows take about a
+    // third of L2, so that every n-block passes over a band while it is L2-resident instead of
+    // each n-block streaming all of A from HBM again (SigLIP at B = 64: A = 107-401 MB).
+    {
+        const size_t a_block = (size_t)BM * mt * cg * K * 2;  // A rows of one m-block, 16-bit
+        const int band = (int)std::max<size_t>(1, (40ull << 20) / a_block);
+        g.group_m = (size_t)tiles_m * a_block > (96ull << 20) && band < tiles_m ? band : 0;
+    }
 
     CUtensorMap ma, mb;
     memset(&mb, 0, sizeof(mb));
