@@ -12,15 +12,18 @@
 //     chain's data, so the stream does not stop at the links: while the consumers wait for a
 //     GEMV's input vector, the ring fills with that GEMV's rows;
 //   - sixteen consumer warps decode with the exact integer dp4a inner products of qdot.cuh
-//     (each thread one 32-element block column of the rows, activations in 23-bit fixed point);
+//     (each thread one 32-element block column of the rows, activations in 16-bit fixed point);
 //   - a GEMV whose input is the output of an earlier GEMV of the chain reads it straight from
-//     that GEMV's y.  Each CTA counts the links it has finished in a 64-bit flag of its own
-//     (monotonic over all launches of the chain, so it is never reset): after its rows of a
-//     link that a later link reads, its consumers meet at a barrier and one thread stores the
-//     new count with release semantics.  A reader thread polls, with acquire loads, only the
-//     flags of the CTAs that wrote the elements it reads, then reads them.  A handful of flag
-//     lines take the polling, not the data the writers are storing.
-// Launches of one chain must not overlap (the flags and the launch counter are the chain's
+//     that GEMV's y.  Every GEMV that a later one reads has a 64-bit counter of its own,
+//     monotonic over all launches of the chain (never reset): a CTA that has stored its rows
+//     of the GEMV meets its consumers at a barrier, and one thread adds 1 to the counter with a
+//     release reduction.  Before a dependent GEMV one thread of each CTA polls that single
+//     counter with acquire loads until all G CTAs of this launch have added to it, and a
+//     barrier then lets the CTA's consumers read the vector: one poller per CTA, one line per
+//     GEMV, and one round trip to L2 for the data once the count is seen.  (Per-thread polls of
+//     the flags of each element's writer CTAs, tried first, cost several dependent round trips
+//     per thread before the data load.)
+// Launches of one chain must not overlap (the counters and the launch counter are the chain's
 // own), and all its CTAs must be resident together: the launch is cooperative.
 #include <cuda_runtime.h>
 
@@ -37,9 +40,9 @@ constexpr int kChainMaxSlots = 12;
 constexpr int kChainMaxStages = 192;  // the stage table is copied to shared memory
 constexpr int kChainF = 4;            // chunks whose rows are reduced together
 constexpr int kChainMaxK = 8192;
-constexpr size_t kChainPlaneBytes = (size_t)3 * (kChainMaxK / 4) * 4 + (size_t)2 * (kChainMaxK / 32) * 4;
+constexpr size_t kChainPlaneBytes = (size_t)kXPlanes * (kChainMaxK / 4) * 4 + (size_t)(kChainMaxK / 32) * 4;
 constexpr size_t kChainPartBytes = (size_t)2 * 128 * 4;  // 2 buffers of F * RPT * NC / 32 <= 128 floats
-constexpr int kFlagStride = 8;  // u64 words between two CTAs' flags (64 bytes)
+constexpr int kFlagStride = 8;  // u64 words between two stages' counters (64 bytes)
 
 // A chunk is RPT rows per consumer thread: NC * RPT blocks, whatever K is (Q4_0 18432 bytes,
 // Q8_0 17408).  Thread t decodes the block at byte t * BB of the chunk (+ i * NC * BB for its
@@ -56,7 +59,7 @@ struct ChainArgs {
     int n_stages;
     int slots;                    // ring depth
     unsigned int* sync;           // [0..1] launch counter (u64), [2] finish ticket, [3] poison
-    unsigned long long* flags;    // per CTA (stride kFlagStride): links finished, over all launches
+    unsigned long long* flags;    // per stage (stride kFlagStride): CTAs that finished it, over all launches
     unsigned long long* times;    // null, or [n_stages] stage end (ns, max over CTAs) + start (min)
     int* status;
 };
@@ -111,44 +114,29 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// The CTA (of G) that computes row r of an N-row stage; CTA c owns rows [N c / G, N (c+1) / G).
-__device__ __forceinline__ int row_owner(long long r, long long N, int G) {
-    return (int)(((r + 1) * G - 1) / N);
-}
-
-// Wait until the CTAs that wrote rows [r0, r1] of the producing stage's output have finished
-// it (their flags reach `target`), with acquire loads; false when it gave up.
-__device__ __forceinline__ bool wait_writers(const ChainArgs& a, long long r0, long long r1, long long n_dep,
-                                             unsigned long long target, volatile int* s_abort) {
-    const int G = gridDim.x;
-    const int c0 = row_owner(r0, n_dep, G), c1 = row_owner(r1, n_dep, G);
-    for (int c = c0; c <= c1; ++c) {
-        const unsigned long long* f = a.flags + (size_t)c * kFlagStride;
-        if (ld_acquire_u64(f) >= target) continue;
-        const uint64_t t0 = globaltimer();
-        uint32_t spins = 0;
-        while (ld_relaxed_u64(f) < target) {
-            if ((++spins & 15u) == 0u) {
-                if (*s_abort || poisoned(a.sync)) {
-                    *s_abort = 1;
-                    return false;
-                }
-                if (globaltimer() - t0 > kWaitLimitNs) {
-                    chain_fail(a, s_abort);
-                    return false;
-                }
+// Wait until stage dep's counter reaches `target` (every CTA of this launch has stored its rows
+// of it), polling with acquire loads; false when it gave up.  One thread per CTA calls this.
+__device__ __forceinline__ bool wait_stage(const ChainArgs& a, int dep, unsigned long long target,
+                                           volatile int* s_abort) {
+    const unsigned long long* f = a.flags + (size_t)dep * kFlagStride;
+    if (ld_acquire_u64(f) >= target) return true;
+    const uint64_t t0 = globaltimer();
+    uint32_t spins = 0;
+    while (ld_acquire_u64(f) < target) {
+        if ((++spins & 15u) == 0u) {
+            if (*s_abort || poisoned(a.sync)) {
+                *s_abort = 1;
+                return false;
+            }
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                chain_fail(a, s_abort);
+                return false;
             }
         }
-        ld_acquire_u64(f);  // the acquire that orders the data reads after the count
     }
     return true;
 }
@@ -172,41 +160,27 @@ __device__ __forceinline__ float4 load_x_word(const void* x, int xtype, int w) {
     return f;
 }
 
-// The stage's input vector into fixed point (qdot.cuh's layout) in shared memory: each thread
-// first waits for the writers of its own words (when the input is an earlier stage's output),
-// then issues all its loads, then converts.  Returns false when a wait gave up.
+// The stage's input vector into fixed point (qdot.cuh's layout) in shared memory: every thread
+// issues all its loads (at L2), then converts.  The caller has waited for the stage that wrote it.
 template <int NC, int ITERS>
-__device__ __forceinline__ bool prepare_x_chain(const ChainArgs& a, const mgpu_k::ChainStage& st,
-                                                unsigned long long target, uint32_t* planes, float* bscale,
-                                                float* bsum, int tid, volatile int* s_abort) {
+__device__ __forceinline__ void prepare_x_chain(const mgpu_k::ChainStage& st, uint32_t* planes, float* bscale,
+                                                int tid) {
     const int words = st.K / 4;
-    bool ok = true;
-    if (st.dep >= 0) {
-        // the writers of this thread's words it * NC + tid (elements 4w .. 4w+3): one or two CTAs each
-#pragma unroll
-        for (int it = 0; it < ITERS; ++it) {
-            const int w = it * NC + tid;
-            if (ok && w < words)
-                ok = wait_writers(a, st.dep_off + 4LL * w, st.dep_off + 4LL * w + 3, st.dep_n, target, s_abort);
-        }
-    }
     float4 v4[ITERS];
 #pragma unroll
     for (int it = 0; it < ITERS; ++it) {
         const int w = it * NC + tid;
         if (w < words) v4[it] = load_x_word(st.x, st.xtype, w);
     }
-    // every lane converts (the block exponent is agreed with shuffles over 8 lanes); words of a
-    // failed wait hold stale values, which the caller discards
+    // every lane converts (the block exponent is agreed with shuffles over 8 lanes)
 #pragma unroll
     for (int it = 0; it < ITERS; ++it) {
         const int w = it * NC + tid;
         if (w < words) {
             const float v[4] = {v4[it].x, v4[it].y, v4[it].z, v4[it].w};
-            convert_x_word(v, w, words, planes, bscale, bsum, (tid & 7) == 0);
+            convert_x_word(v, w, words, planes, bscale, (tid & 7) == 0);
         }
     }
-    return ok;
 }
 
 // y[row] in the stage's type.
@@ -256,9 +230,8 @@ __global__ void __launch_bounds__(NC + 32, 1) gemv_chain_kernel(ChainArgs a) {
 
     uint8_t* ring = smem;
     uint32_t* planes = reinterpret_cast<uint32_t*>(smem + (size_t)S * kChunk);
-    float* bscale = reinterpret_cast<float*>(planes + 3 * (kChainMaxK / 4));
-    float* bsum = bscale + kChainMaxK / 32;
-    float* part = bsum + kChainMaxK / 32;  // two buffers of kPartFloats
+    float* bscale = reinterpret_cast<float*>(planes + kXPlanes * (kChainMaxK / 4));
+    float* part = bscale + kChainMaxK / 32;  // two buffers of kPartFloats
     // the stage table, copied once (every link's record is then a shared-memory read), and this
     // CTA's rows [r0, r1) of every stage, worked out once
     mgpu_k::ChainStage* table = reinterpret_cast<mgpu_k::ChainStage*>(part + 2 * 128);
@@ -275,9 +248,9 @@ __global__ void __launch_bounds__(NC + 32, 1) gemv_chain_kernel(ChainArgs a) {
     }
     __syncthreads();
     const bool refuse = s_refuse != 0u;
-    // flags count the links a CTA has finished over all launches: link s of this launch is
-    // finished when the count reaches base + s + 1
-    const unsigned long long base = s_epoch * (unsigned long long)a.n_stages;
+    // a stage's counter counts the CTAs that finished it over all launches: this launch's CTAs
+    // have all finished it when it reaches (launches before this one + 1) * G
+    const unsigned long long target = (s_epoch + 1ull) * (unsigned long long)G;
 
     if (warp == kWarps) {
         // ---------------- producer: every stage's rows of this CTA, in stage order ----------------
@@ -324,22 +297,27 @@ __global__ void __launch_bounds__(NC + 32, 1) gemv_chain_kernel(ChainArgs a) {
             const int r0 = rows[s].x, r1 = rows[s].y;
             const int nch = (r1 - r0 + TR - 1) >> (__ffs(TR) - 1);
 
-            // the input vector, in fixed point, to shared memory
+            // wait (one thread) for the stage that writes the input; the barrier also keeps the
+            // previous stage's readers of the activation planes ahead of their rewrite
             {
-                const unsigned long long target = base + (unsigned long long)(st.dep + 1);
-                bool ok;
-                if (K <= NC * 4) ok = prepare_x_chain<NC, 1>(a, st, target, planes, bscale, bsum, tid, s_abort);
-                else if (K <= NC * 8) ok = prepare_x_chain<NC, 2>(a, st, target, planes, bscale, bsum, tid, s_abort);
-                else ok = prepare_x_chain<NC, kChainMaxK / (NC * 4)>(a, st, target, planes, bscale, bsum, tid, s_abort);
-                abort = abort || !ok;
+                bool ok = true;
+                if (st.dep >= 0 && tid == 0) ok = wait_stage(a, st.dep, target, s_abort);
+                if (barrier_or<NC>(abort || !ok)) {
+                    abort = true;
+                    break;
+                }
             }
+            // the input vector, in fixed point, to shared memory
+            if (K <= NC * 4) prepare_x_chain<NC, 1>(st, planes, bscale, tid);
+            else if (K <= NC * 8) prepare_x_chain<NC, 2>(st, planes, bscale, tid);
+            else prepare_x_chain<NC, kChainMaxK / (NC * 4)>(st, planes, bscale, tid);
             if (barrier_or<NC>(abort)) {
                 abort = true;
                 break;
             }
             const int col = tid & (nb - 1), rslot = tid >> lg, wpr = nb >> 5;
             XFixed xf;
-            load_xfixed(planes, bscale, bsum, words, col, xf);
+            load_xfixed(planes, bscale, words, col, xf);
             const uint32_t par4 = (uint32_t)(tid * BB) & 3u;  // block starts at byte 0 or 2 of a word
             const uint32_t sel = par4 ? 0x7654u : 0x5432u;
             const uint32_t dsel = par4 ? 0x4432u : 0x4410u;
@@ -406,16 +384,12 @@ __global__ void __launch_bounds__(NC + 32, 1) gemv_chain_kernel(ChainArgs a) {
                 pbuf ^= 1;
             }
             if (abort) break;
-            // The next stage rewrites the activation planes, which needs a barrier after every
-            // thread's load_xfixed: a stage with chunks has passed one, and when a later stage
-            // reads this one's output, the barrier before its flag is posted serves too.
-            if (st.post || nch == 0) {
+            // Every CTA adds to the counter of a stage a later stage reads, rows or none, once
+            // all its consumers have stored their rows (the barrier); the release reduction makes
+            // those stores visible before the count.
+            if (st.post) {
                 if (barrier_or<NC>(abort)) break;
-                if (st.post && nch > 0 && tid == NC - 32) {
-                    // every row this CTA stored for the stage happens before this (barrier), and
-                    // the release store makes them visible before the new count
-                    st_release_u64(a.flags + (size_t)b * kFlagStride, base + (unsigned long long)s + 1ull);
-                }
+                if (tid == NC - 32) red_release_add_u64(a.flags + (size_t)s * kFlagStride, 1ull);
             }
             if (a.times && tid == 0 && nch > 0) atomicMax(a.times + s, (unsigned long long)globaltimer());
         }
@@ -490,7 +464,7 @@ bool chain_shape_ok(int K) { return K >= 1024 && K <= kChainMaxK && K % 1024 == 
 
 int chain_max_links() { return kChainMaxStages; }
 
-size_t chain_flag_bytes(int sm_count) { return (size_t)sm_count * kFlagStride * sizeof(unsigned long long); }
+size_t chain_flag_bytes(int) { return (size_t)kChainMaxStages * kFlagStride * sizeof(unsigned long long); }
 
 cudaError_t gemv_chain(const LaunchCtx& c, int qtype, const ChainStage* stages, int n, unsigned int* sync,
                        unsigned long long* flags, unsigned long long* times) {

@@ -3,13 +3,13 @@
 // gemv_q_stream: y = dequant(W) . x for GGUF Q4_0 / Q8_0 weights kept packed in their
 //   [N][K/32] block layout.  Each CTA owns an even share of the rows.  One producer thread
 //   streams the CTA's contiguous byte range from HBM into a 2..8-stage shared-memory ring with
-//   cp.async.bulk (the 1-D TMA engine, 16-byte granular, no registers held in flight); 8
+//   cp.async.bulk (the 1-D TMA engine, 16-byte granular, no registers held in flight); 16
 //   consumer warps decode the 18 / 34-byte blocks out of shared memory.  Each consumer thread
 //   owns one 32-element block column for the whole launch; its 32 activations are turned
-//   once into 23-bit fixed point (three byte planes), and every block's dot product is exact
+//   once into 16-bit fixed point (two byte planes), and every block's dot product is exact
 //   integer dp4a arithmetic on the packed nibbles / int8s (no per-weight unpacking), scaled
 //   once per block in fp32 by the fp16 d.  Row sums are reduced across lanes with a
-//   transposing shuffle butterfly.  Two CTAs per SM; launched with programmatic dependent
+//   transposing shuffle butterfly.  Up to two CTAs per SM; launched with programmatic dependent
 //   launch: the producer starts streaming weights while the previous kernel drains, and the
 //   consumers execute griddepcontrol.wait before reading x (which the previous kernel may
 //   write).
@@ -33,8 +33,13 @@ using namespace mgpu_dev;
 
 namespace {
 
-constexpr int kConsumerThreads = 256;
+constexpr int kConsumerThreads = 256;  // gemv_q_mma
 constexpr int kGemvThreads = kConsumerThreads + 32;
+// gemv_q_stream: 16 consumer warps + the producer warp.  Two such CTAs fit an SM (the current
+// GEMV and, under programmatic dependent launch, the next one) at <= 56 registers a thread.
+constexpr int kStreamThreads = 512;
+constexpr int kStreamBlock = kStreamThreads + 32;
+static_assert(kStreamThreads == kRmsThreads, "the fused RMSNorm must reduce like the standalone kernel");
 constexpr int kGemvMaxStages = 8;  // ring depth is chosen per shape, up to this
 constexpr int kGemvCtasPerSm = 2;                 // at most; see the launcher
 constexpr uint32_t kGemvSmemBudget = 100 * 1024;  // per CTA: two CTAs share an SM
@@ -66,7 +71,7 @@ struct GemvQArgs {
 };
 
 template <int QT, int RPT, typename XT, typename YT>
-__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(GemvQArgs a) {
+__global__ void __launch_bounds__(kStreamBlock, kGemvCtasPerSm) gemv_q_stream(GemvQArgs a) {
     constexpr int BB = QTraits<QT>::kBlockBytes;
     constexpr int NW = QTraits<QT>::kWords;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -76,7 +81,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int nb = a.nb;
-    const int RP = kConsumerThreads / nb;  // rows decoded per step
+    const int RP = kStreamThreads / nb;  // rows decoded per step
     const int TR = RP * RPT;               // rows per chunk
     const int G = gridDim.x;
     const int r0 = (int)((long long)a.N * blockIdx.x / G);
@@ -86,7 +91,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     if (tid == 0) {
         for (int s = 0; s < a.stages; ++s) {
             mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], kConsumerThreads / 32);
+            mbar_init(&empty_bar[s], kStreamThreads / 32);
         }
         fence_mbar_init();
         // Dependent kernels may be scheduled now; they only read this kernel's output after
@@ -95,7 +100,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     }
     __syncthreads();
 
-    if (warp == kConsumerThreads / 32) {
+    if (warp == kStreamThreads / 32) {
         // ---- producer: stream this CTA's rows chunk by chunk ----
         // Weights are never written by the preceding kernel, so streaming starts before
         // griddepcontrol.wait and overlaps the previous kernel's tail.
@@ -130,31 +135,30 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
     // are read correctly after griddepcontrol.wait.
     {
         const int nlines = (nb * 32 * (int)sizeof(XT) + 127) / 128;
-        for (int l = (int)blockIdx.x + tid * G; l < nlines; l += kConsumerThreads * G)
+        for (int l = (int)blockIdx.x + tid * G; l < nlines; l += kStreamThreads * G)
             asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.x) + (size_t)l * 128));
     }
     // x (and y) may belong to the preceding kernel of the stream: wait for it to complete.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int K = nb * 32;
     uint32_t* planes = reinterpret_cast<uint32_t*>(smem + (size_t)a.stages * a.stage_stride);
-    float* bscale = reinterpret_cast<float*>(planes + 3 * (K / 4));
-    float* bsum = bscale + nb;
+    float* bscale = reinterpret_cast<float*>(planes + kXPlanes * (K / 4));
     if (a.gamma)
-        prepare_x_norm<XT>(reinterpret_cast<const XT*>(a.x), a.gamma, a.gtype, a.eps, K, planes, bscale, bsum,
-                           bsum + nb, tid, kConsumerThreads);  // (the row partials' space, not in use yet)
+        prepare_x_norm<XT>(reinterpret_cast<const XT*>(a.x), a.gamma, a.gtype, a.eps, K, planes, bscale,
+                           bscale + nb, tid, kStreamThreads);  // (the row partials' space, not in use yet)
     else
-        prepare_x<XT>(reinterpret_cast<const XT*>(a.x), K, planes, bscale, bsum, tid, kConsumerThreads);
-    named_barrier_sync(1, kConsumerThreads);
+        prepare_x<XT>(reinterpret_cast<const XT*>(a.x), K, planes, bscale, tid, kStreamThreads);
+    named_barrier_sync(1, kStreamThreads);
     const int col = tid % nb;  // block column owned by this thread for the whole launch
     XFixed xf;
-    load_xfixed(planes, bscale, bsum, K / 4, col, xf);
+    load_xfixed(planes, bscale, K / 4, col, xf);
     const uint32_t par = (uint32_t)(tid * BB) & 3u;  // block starts at byte 0 or 2 of a word
     const uint32_t sel = par ? 0x7654u : 0x5432u;
     const uint32_t dsel = par ? 0x4432u : 0x4410u;
     const uint32_t toff = (uint32_t)(tid * BB) - par;
     const int wpr = nb >> 5;  // warps per row slot
     const int slot = tid / nb;
-    float* part = bsum + nb;  // chunks_per_flush * TR * wpr floats
+    float* part = bscale + nb;  // chunks_per_flush * TR * wpr floats
     YT* __restrict__ y = reinterpret_cast<YT*>(a.y);
 
     int s = 0;
@@ -165,7 +169,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
         float acc[RPT];
 #pragma unroll
         for (int i = 0; i < RPT; ++i) {
-            const uint32_t* wp = reinterpret_cast<const uint32_t*>(st + i * (kConsumerThreads * BB));
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(st + i * (kStreamThreads * BB));
             uint32_t w[NW];
 #pragma unroll
             for (int q = 0; q < NW; ++q) w[q] = wp[q];
@@ -185,15 +189,15 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q_stream(Ge
         const int cf = c % a.chunks_per_flush;
         if ((lane & ((32 / RPT) - 1)) == 0) part[(cf * TR + slot + RP * ri) * wpr + (warp % wpr)] = v;
         if (cf == a.chunks_per_flush - 1 || c == nchunks - 1) {
-            named_barrier_sync(1, kConsumerThreads);
+            named_barrier_sync(1, kStreamThreads);
             const int row0 = r0 + (c - cf) * TR;
             const int nrows = min((cf + 1) * TR, r1 - row0);
-            for (int r = tid; r < nrows; r += kConsumerThreads) {
+            for (int r = tid; r < nrows; r += kStreamThreads) {
                 float sum = 0.0f;
                 for (int w = 0; w < wpr; ++w) sum += part[r * wpr + w];
                 y[row0 + r] = from_f32<YT>(sum);
             }
-            named_barrier_sync(1, kConsumerThreads);
+            named_barrier_sync(1, kStreamThreads);
         }
     }
 }
@@ -740,18 +744,18 @@ struct GemvQLaunch {
                               ((reinterpret_cast<uintptr_t>(W) & 15) == 0) &&
                               ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
             // the RMSNorm prologue is in the streaming dp4a kernel only
-            if (norm && !(fast && (kConsumerThreads % nb) == 0)) return cudaErrorNotSupported;
+            if (norm && !(fast && (kStreamThreads % nb) == 0)) return cudaErrorNotSupported;
             if (!fast) {
                 const int blocks = (N * 32 + 255) / 256;
                 gemv_q_generic<QT, XT, YT><<<blocks, 256, 0, c.stream>>>(W, (const XT*)x, (YT*)y, N, nb, row_bytes);
                 return cudaGetLastError();
             }
             // The dp4a kernel gives each thread one block column of a row slot, so it needs
-            // nb to divide 256 (K = 1024, 2048, 4096, 8192).  Other K go to the MMA kernel
-            // when it can stage them.  (Timed inside a chain of dependent GEMVs of different
-            // shapes, the dp4a kernel is the faster of the two on every Phi-1.5 shape, so it
-            // takes all K it supports.)
-            const bool dp4a_ok = (kConsumerThreads % nb) == 0;
+            // nb to divide its 512 consumer threads (K = 1024, 2048, 4096, 8192 with nb <= 256).
+            // Other K go to the MMA kernel when it can stage them.  (Timed inside a chain of
+            // dependent GEMVs of different shapes, the dp4a kernel is the faster of the two on
+            // every Phi-1.5 shape, so it takes all K it supports.)
+            const bool dp4a_ok = (kStreamThreads % nb) == 0;
             if (!dp4a_ok) {
                 const cudaError_t e = run_mma(c, W, x, y, N, K, true);
                 if (e != cudaErrorNotSupported) return e;
@@ -761,7 +765,7 @@ struct GemvQLaunch {
                 gemv_q_generic<QT, XT, YT><<<blocks, 256, 0, c.stream>>>(W, (const XT*)x, (YT*)y, N, nb, row_bytes);
                 return cudaGetLastError();
             }
-            const int RP = kConsumerThreads / nb;
+            const int RP = kStreamThreads / nb;
             // Layer-sized GEMVs take one CTA per SM: a launch then leaves room on every SM for
             // one CTA of the next GEMV in the stream, which under programmatic dependent launch
             // becomes resident early and streams its weights while this one finishes.  Large
@@ -771,25 +775,26 @@ struct GemvQLaunch {
             const int per_sm = N > c.sm_count * kBigRows ? kGemvCtasPerSm : 1;
             const int G = max(1, min(c.sm_count * per_sm, (N + RP - 1) / RP));
             const int rows_per_cta = (N + G - 1) / G;
-            // Rows per thread (8, 4, 2, 1) and ring depth (2..8 stages).  Eight rows per thread
-            // whenever two stages of them fit: a decode chain then launches one function for
-            // every shape, and a dependent launch of a different function was measured to cost
-            // ~1.4 us more than one of the same function (a 97-GEMV Phi-1.5 step with 4 rows per
-            // thread for qkv / out and 8 for fc1 / fc2 / lm_head took 455.8 us, with 8 for all
-            // 385.8 us; per-shape chains of one function were equally fast either way).  The
-            // ring then holds all of a layer-sized GEMV's rows, so its weights stream in before
-            // griddepcontrol.wait returns.  Otherwise: a ring that holds all of the CTA's rows
-            // with the widest chunk that computes at most 25 % padding rows; then, for GEMVs too
-            // large to prefetch whole, a 4-stage ring of the widest chunk that fits.  Row
-            // partials of up to kPartFloats are buffered between flushes.
+            // Rows per thread (4, 2, 1) and ring depth (2..8 stages).  Four rows per thread
+            // (a 36 KB chunk of Q4_0 K = 2048 rows) whenever two stages of them fit: a decode
+            // chain then launches one function for every shape, and a dependent launch of a
+            // different function was measured to cost ~1.4 us more than one of the same
+            // function (a 97-GEMV Phi-1.5 step mixing two row counts took 455.8 us, one row
+            // count for all 385.8 us).  The ring then holds all of a layer-sized GEMV's rows, so
+            // its weights stream in before griddepcontrol.wait returns.  Otherwise: a ring that
+            // holds all of the CTA's rows with the widest chunk that computes at most 25 %
+            // padding rows; then, for GEMVs too large to prefetch whole, a 4-stage ring of the
+            // widest chunk that fits.  Row partials of up to kPartFloats are buffered between
+            // flushes.
             constexpr int kPartFloats = 4096;
+            constexpr int kMaxRpt = 4;
             const int wpr = nb / 32;
-            const size_t x_bytes = (size_t)3 * (K / 4) * 4 + (size_t)2 * nb * 4;
+            const size_t x_bytes = (size_t)kXPlanes * (K / 4) * 4 + (size_t)nb * 4;
             auto stride = [&](int r) { return ((size_t)RP * r * row_bytes + 1023) / 1024 * 1024; };
             auto chunks_of = [&](int r) { return (rows_per_cta + RP * r - 1) / (RP * r); };
             auto part_floats = [&](int r) {
                 const int cpf = max(1, min(chunks_of(r), kPartFloats / (RP * r * wpr)));
-                return (size_t)cpf * RP * r * wpr;
+                return (size_t)max(cpf * RP * r * wpr, kStreamThreads / 32);  // (also the RMSNorm scratch)
             };
             auto depth = [&](int r, int cap) {
                 const size_t fixed = x_bytes + 4 * part_floats(r);
@@ -797,11 +802,11 @@ struct GemvQLaunch {
                 return max(2, min(cap, min(chunks_of(r), (int)((kGemvSmemBudget - fixed) / stride(r)))));
             };
             int rpt = 0, stages = 0;
-            if (const int d8 = depth(8, kGemvMaxStages)) {
-                rpt = 8;
-                stages = d8;
+            if (const int d = depth(kMaxRpt, kGemvMaxStages)) {
+                rpt = kMaxRpt;
+                stages = d;
             }
-            for (int r = 8; r >= 1 && !rpt; r >>= 1) {
+            for (int r = kMaxRpt; r >= 1 && !rpt; r >>= 1) {
                 const int d = depth(r, kGemvMaxStages);
                 const int waste = chunks_of(r) * RP * r - rows_per_cta;
                 if (d && d >= chunks_of(r) && 4 * waste <= rows_per_cta) {
@@ -809,14 +814,14 @@ struct GemvQLaunch {
                     stages = d;
                 }
             }
-            for (int r = 8; r >= 1 && !rpt; r >>= 1) {
+            for (int r = kMaxRpt; r >= 1 && !rpt; r >>= 1) {
                 const int d = depth(r, 4);
                 if (d >= min(4, chunks_of(r))) {
                     rpt = r;
                     stages = d;
                 }
             }
-            for (int r = 8; r >= 1 && !rpt; r >>= 1) {
+            for (int r = kMaxRpt; r >= 1 && !rpt; r >>= 1) {
                 const int d = depth(r, 4);
                 if (d) {
                     rpt = r;
@@ -836,14 +841,13 @@ struct GemvQLaunch {
             a.row_bytes = (uint32_t)row_bytes;
             a.stage_stride = (uint32_t)stride(rpt);
             a.stages = stages;
-            a.chunks_per_flush = (int)(part_floats(rpt) / ((size_t)RP * rpt * wpr));
+            a.chunks_per_flush = max(1, min(chunks_of(rpt), kPartFloats / (RP * rpt * wpr)));
             a.status = c.status;
             a.gamma = norm ? norm->gamma : nullptr;
             a.gtype = norm ? norm->gtype : 0;
             a.eps = norm ? norm->eps : 0.0f;
             const size_t smem = (size_t)a.stages * a.stage_stride + x_bytes + 4 * part_floats(rpt);
             switch (rpt) {
-                case 8: return launch<8, XT, YT>(c, a, G, smem);
                 case 4: return launch<4, XT, YT>(c, a, G, smem);
                 case 2: return launch<2, XT, YT>(c, a, G, smem);
                 default: return launch<1, XT, YT>(c, a, G, smem);
@@ -975,7 +979,7 @@ struct GemvQLaunch {
             }
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(G);
-            cfg.blockDim = dim3(kGemvThreads);
+            cfg.blockDim = dim3(kStreamBlock);
             cfg.dynamicSmemBytes = smem;
             cfg.stream = c.stream;
             cudaLaunchAttribute attr[1];

@@ -69,7 +69,7 @@ struct ChainStage {
 bool chain_shape_ok(int K);
 // Links one chain may hold (its stage table is copied to shared memory).
 int chain_max_links();
-// Bytes of the per-CTA flags a chain owns (zeroed once; the kernel only counts them up).
+// Bytes of the per-stage counters a chain owns (zeroed once; the kernel only counts them up).
 size_t chain_flag_bytes(int sm_count);
 // One cooperative launch (one CTA per SM) over the n stages (all of qtype) at `stages` (device
 // memory).  sync: 4 zeroed words owned by the chain (launch counter (u64), finish ticket,

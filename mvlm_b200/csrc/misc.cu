@@ -166,34 +166,34 @@ __device__ __forceinline__ float argmax_value(int type, const void* x, int64_t i
 }
 
 // RMSNorm over rows (src/kernels/layernorm.cl:41-146, dispatched by compute.cpp:156-184): one
-// CTA of 256 threads per row, y = x * rsqrt(mean(x^2) + eps) * w in fp32, stored in y's type.
+// CTA of kRmsThreads threads per row, y = x * rsqrt(mean(x^2) + eps) * w in fp32, stored in y's type.
 // Rows of a multiple of 4 elements at 16-byte (fp32) / 8-byte (16-bit) aligned addresses use
 // the word order and reduction of rms_scale, the same as the fused GEMV prologue, so the two
 // give the same bits; other rows take a per-element loop.
 template <typename T>
-__global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ in, T* __restrict__ out, int wtype,
+__global__ void __launch_bounds__(kRmsThreads) rms_norm_kernel(const T* __restrict__ in, T* __restrict__ out, int wtype,
                                                        const void* __restrict__ w, int H, float eps, bool words) {
-    __shared__ float red[8];
+    __shared__ float red[kRmsThreads / 32];
     const int tid = threadIdx.x;
     const T* x = in + (size_t)blockIdx.x * H;
     T* y = out + (size_t)blockIdx.x * H;
     float ss = 0.0f;
     if (words) {
-        for (int i = tid; i < H / 4; i += 256) {
+        for (int i = tid; i < H / 4; i += kRmsThreads) {
             float v[4];
             load_word4(x, i, v);
 #pragma unroll
             for (int j = 0; j < 4; ++j) ss = fmaf(v[j], v[j], ss);
         }
     } else {
-        for (int i = tid; i < H; i += 256) {
+        for (int i = tid; i < H; i += kRmsThreads) {
             const float v = to_f32<T>(x[i]);
             ss = fmaf(v, v, ss);
         }
     }
-    const float r = rms_scale(ss, red, tid, 256, H, eps);
+    const float r = rms_scale(ss, red, tid, kRmsThreads, H, eps);
     if (words) {
-        for (int i = tid; i < H / 4; i += 256) {
+        for (int i = tid; i < H / 4; i += kRmsThreads) {
             float v[4], g[4];
             load_word4(x, i, v);
             load_word4_typed(wtype, w, i, g);
@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ in,
             for (int j = 0; j < 4; ++j) y[4 * i + j] = from_f32<T>(v[j] * r * g[j]);
         }
     } else {
-        for (int i = tid; i < H; i += 256) y[i] = from_f32<T>(to_f32<T>(x[i]) * r * load_typed(wtype, w, i));
+        for (int i = tid; i < H; i += kRmsThreads) y[i] = from_f32<T>(to_f32<T>(x[i]) * r * load_typed(wtype, w, i));
     }
 }
 
@@ -355,11 +355,11 @@ cudaError_t rms_norm(const LaunchCtx& c, int type, const void* in, void* out, in
     const bool words = H % 4 == 0 && ((uintptr_t)in % align) == 0 && ((uintptr_t)out % align) == 0 &&
                        ((uintptr_t)w % (wtype == MGPU_F32 ? 16 : 8)) == 0 && (H * (type == MGPU_F32 ? 4 : 2)) % align == 0;
     if (type == MGPU_F32)
-        rms_norm_kernel<float><<<rows, 256, 0, c.stream>>>((const float*)in, (float*)out, wtype, w, H, eps, words);
+        rms_norm_kernel<float><<<rows, kRmsThreads, 0, c.stream>>>((const float*)in, (float*)out, wtype, w, H, eps, words);
     else if (type == MGPU_F16)
-        rms_norm_kernel<__half><<<rows, 256, 0, c.stream>>>((const __half*)in, (__half*)out, wtype, w, H, eps, words);
+        rms_norm_kernel<__half><<<rows, kRmsThreads, 0, c.stream>>>((const __half*)in, (__half*)out, wtype, w, H, eps, words);
     else
-        rms_norm_kernel<__nv_bfloat16><<<rows, 256, 0, c.stream>>>((const __nv_bfloat16*)in, (__nv_bfloat16*)out,
+        rms_norm_kernel<__nv_bfloat16><<<rows, kRmsThreads, 0, c.stream>>>((const __nv_bfloat16*)in, (__nv_bfloat16*)out,
                                                                    wtype, w, H, eps, words);
     return cudaGetLastError();
 }

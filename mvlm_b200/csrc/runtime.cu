@@ -812,7 +812,7 @@ struct mgpu_gemv_chain {
     int qtype;
     mgpu_k::ChainStage* d_stages;   // the stage table the kernel reads
     unsigned int* d_sync;           // launch counter (u64), finish ticket, poison
-    unsigned long long* d_flags;    // per-CTA counts of finished links
+    unsigned long long* d_flags;    // per-stage counts of the CTAs that finished it
     unsigned long long* d_times;    // n + 1 words for timed runs (allocated on first use)
 };
 
