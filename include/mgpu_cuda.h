@@ -13,6 +13,11 @@
  *     queue, src/engine/device.cpp:297-300); no call synchronises implicitly except
  *     mgpu_buf_read/write, mgpu_wait_event and mgpu_finish.
  *   - A device handle is used by one host thread at a time.
+ *   - The GEMV and GEMM kernels overlap the kernel before them in the stream: they start
+ *     reading their weight operand (W / B) before that kernel has finished, and read
+ *     activations and write outputs only after it.  A weight buffer must therefore not be
+ *     written by the GEMV or GEMM call enqueued directly before the call that reads it as
+ *     weights (uploads, copies, conversions and any other enqueued work may precede it).
  */
 #ifndef MGPU_CUDA_H
 #define MGPU_CUDA_H

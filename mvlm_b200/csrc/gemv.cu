@@ -628,6 +628,9 @@ __global__ void __launch_bounds__(256) gemv_nk_dense(const WT* __restrict__ W, i
 // CTA = 256 threads over a tile of 256 columns x kchunk rows of K; thread handles COLS
 // consecutive columns of kchunk/8 rows.  Partials of split s go to partials[s][N]; the last
 // CTA of a column tile (atomic ticket) sums splits 0..S-1 in order and resets the ticket.
+// Launched with programmatic dependent launch: the weights are never written by the
+// preceding kernel, so each thread issues its first rows' loads before griddepcontrol.wait;
+// x, the partials and the tickets are touched only after it.
 constexpr int kKnCols = 256;
 template <typename WT, typename XT, typename YT, bool UNROLL>
 __global__ void __launch_bounds__(256) gemv_kn_split(const WT* __restrict__ W, int64_t ldw,
@@ -647,7 +650,9 @@ __global__ void __launch_bounds__(256) gemv_kn_split(const WT* __restrict__ W, i
     for (int i = 0; i < CPT; ++i) acc[i] = 0.0f;
     const bool full_vec = (n0 + CPT <= N) && ((ldw * sizeof(WT)) % 16 == 0) &&
                           ((reinterpret_cast<uintptr_t>(W) & 15) == 0);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     int k = k_begin + warp;
+    bool waited = false;
     if (UNROLL && full_vec) {
         // four rows per step, all loads issued before any is used: four times the bytes in
         // flight per warp (measured faster for fp32 rows of N >= 4096, slower for N = 2048 and
@@ -663,14 +668,20 @@ __global__ void __launch_bounds__(256) gemv_kn_split(const WT* __restrict__ W, i
 #pragma unroll
                 for (int v = 0; v < V; ++v)
                     reinterpret_cast<uint4*>(wv[r])[v] = __ldg(reinterpret_cast<const uint4*>(wr) + v);
-                xv[r] = to_f32<XT>(x[k + 8 * r]);
             }
+            if (!waited) {
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                waited = true;
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) xv[r] = to_f32<XT>(x[k + 8 * r]);
 #pragma unroll
             for (int r = 0; r < R; ++r)
 #pragma unroll
                 for (int i = 0; i < CPT; ++i) acc[i] = fmaf(xv[r], to_f32<WT>(wv[r][i]), acc[i]);
         }
     }
+    if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
     for (; k < k_end; k += 8) {
         const float xv = to_f32<XT>(x[k]);
         const WT* wr = W + (size_t)k * ldw + n0;
@@ -1011,6 +1022,28 @@ struct GemvNkLaunch {
     };
 };
 
+// gemv_kn_split with programmatic dependent launch (the kernel orders its reads of x and its
+// scratch writes after griddepcontrol.wait).
+template <typename WT, typename XT, typename YT>
+cudaError_t launch_kn(cudaStream_t stream, dim3 grid, const WT* W, int64_t ldw, const XT* x, YT* y, int N, int K,
+                      int kchunk, float* partials, unsigned int* counters) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (sizeof(WT) == 4 && N >= 4096)
+        return cudaLaunchKernelEx(&cfg, gemv_kn_split<WT, XT, YT, true>, W, ldw, x, y, N, K, kchunk, partials,
+                                  counters);
+    return cudaLaunchKernelEx(&cfg, gemv_kn_split<WT, XT, YT, false>, W, ldw, x, y, N, K, kchunk, partials,
+                              counters);
+}
+
 template <typename WT>
 struct GemvKnLaunch {
     template <typename XT, typename YT>
@@ -1021,13 +1054,8 @@ struct GemvKnLaunch {
             mgpu_k::gemv_kn_scratch_bytes(N, K, c.sm_count, &splits);
             const int kchunk = (K + splits - 1) / splits;
             dim3 grid((N + kKnCols - 1) / kKnCols, splits);
-            if (sizeof(WT) == 4 && N >= 4096)
-                gemv_kn_split<WT, XT, YT, true><<<grid, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x, (YT*)y,
-                                                                           N, K, kchunk, partials, counters);
-            else
-                gemv_kn_split<WT, XT, YT, false><<<grid, 256, 0, c.stream>>>((const WT*)W, ldw, (const XT*)x, (YT*)y,
-                                                                            N, K, kchunk, partials, counters);
-            return cudaGetLastError();
+            return launch_kn<WT, XT, YT>(c.stream, grid, (const WT*)W, ldw, (const XT*)x, (YT*)y, N, K, kchunk,
+                                         partials, counters);
         }
     };
 };
@@ -1151,9 +1179,11 @@ cudaError_t gemv_kn_noalloc(const LaunchCtx& c, int wtype, const void* W, int64_
 }
 
 size_t gemv_kn_scratch_bytes(int N, int K, int sm_count, int* splits_out) {
-    // Enough CTAs for ~4 per SM, each with at least 64 rows of K.
+    // One wave: at most 4 CTAs per SM (the number resident at once), each with at least 64 rows
+    // of K.  (Rounding the split count up instead left a second wave of a few CTAs: with
+    // N = 8192, 608 CTAs for 592 slots.)
     const int col_tiles = (N + kKnCols - 1) / kKnCols;
-    int splits = (4 * sm_count + col_tiles - 1) / col_tiles;
+    int splits = (4 * sm_count) / col_tiles;
     splits = max(1, min(splits, (K + 63) / 64));
     if (splits_out) *splits_out = splits;
     return (size_t)col_tiles * sizeof(unsigned int) + (size_t)splits * N * sizeof(float) + 256;
