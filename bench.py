@@ -329,10 +329,29 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
     Hall = g_hid.slots(mg.BF16)   # [world][K_h]: every sequence's hidden state
     recv = g_pair.slots(mg.F32)   # [world][2]: this sequence's pair from every rank
 
+    # The lm_head shard over the N sequences: one GEMM with M = N (the skinny kernel), or N
+    # M = 1 GEMVs (one per sequence, each reading its row of the gathered hidden states).  The
+    # GEMV streams weights ~2x faster per byte than the skinny kernel but pays its fixed cost N
+    # times; each rank times both once (its own graph replays, no collective) and keeps the
+    # faster.
+    head_rows = [(Hall.view(i * K_h * 2, K_h * 2).set_format(mg.BF16),
+                  logits.view(i * n_head * 4, n_head * 4).set_format(mg.F32)) for i in range(world)]
+
+    def head_gemm():
+        mg.gemm_q(dev, Hall, Wh, logits, world, n_head, K_h, qt)
+
+    def head_gemvs():
+        for hx, ly in head_rows:
+            mg.gemv_q(dev, hx, Wh, ly, n_head, K_h, qt)
+
+    head_us = {name: time_graph(dev, torch, stream, fn, 20) * 1e3
+               for name, fn in (("gemm_m_eq_n", head_gemm), ("gemv_per_sequence", head_gemvs))}
+    head_kind = min(head_us, key=head_us.get)
+    head = head_gemm if head_kind == "gemm_m_eq_n" else head_gemvs
+
     phases = [("layers_and_bf16", lambda: (enqueue_links(dev, mg, qt, links), dev.convert(hidden, hb, K_h))),
               ("hidden_all_gather", lambda: g_hid.allgather(hb, K_h * 2)),
-              ("head_gemm_argmax", lambda: (mg.gemm_q(dev, Hall, Wh, logits, world, n_head, K_h, qt),
-                                            mg.argmax_rows(dev, logits, world, n_head, n_head, pairs))),
+              ("head_gemm_argmax", lambda: (head(), mg.argmax_rows(dev, logits, world, n_head, n_head, pairs))),
               ("pairs_all_to_all", lambda: g_pair.alltoall(pairs, 8)),
               ("combine", lambda: mg.argmax_combine(dev, recv, world, N_h, tok))]
 
@@ -474,8 +493,10 @@ def run_decode_multi(args, dev, mg, torch, stream, dist, rank: int, world: int, 
     g_hid.destroy()
     g_pair.destroy()
     return {"ms": ms, "step_bytes": step_bytes, "layer_bytes": layer_bytes, "n_head": n_head, "parity": parity,
-            "e2e": e2e, "clocks": clocks, "launches_per_step": len(links) + 6, "links": links, "Wh": Wh,
-            "breakdown_us": breakdown}
+            "e2e": e2e, "clocks": clocks,
+            "launches_per_step": len(links) + 5 + (world if head_kind == "gemv_per_sequence" else 1),
+            "links": links, "Wh": Wh, "breakdown_us": breakdown,
+            "head": {"kind": head_kind, "us": {k: round(v, 2) for k, v in head_us.items()}}}
 
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
@@ -509,7 +530,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                                                multi["clocks"])
         links, Wh, n_head = multi["links"], multi["Wh"], multi["n_head"]
         launches_per_step = multi["launches_per_step"]
-        secondary_multi = {"step_breakdown_us": multi["breakdown_us"]}
+        secondary_multi = {"step_breakdown_us": multi["breakdown_us"], "lm_head_shard": multi["head"]}
     else:
         n_head = HEAD[2]
         links, x0 = build_decode_step(dev, mg, tmp, qt, n_head, 0)
