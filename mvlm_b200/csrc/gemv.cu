@@ -826,8 +826,12 @@ struct GemvQLaunch {
                 }
             }
             for (int r = kMaxRpt; r >= 1 && !rpt; r >>= 1) {
+                // a 4-stage ring, or at least 64 KB in flight per CTA (two CTAs per SM keep twice
+                // that, well above what the HBM latency needs): Q8_0 rows then take two rows per
+                // thread in 35 KB chunks rather than one (the row reduction per block halves;
+                // the Q8_0 lm_head measured 22.7 us with one row per thread)
                 const int d = depth(r, 4);
-                if (d >= min(4, chunks_of(r))) {
+                if (d >= min(4, chunks_of(r)) || (d >= 2 && (size_t)d * stride(r) >= 64 * 1024)) {
                     rpt = r;
                     stages = d;
                 }
