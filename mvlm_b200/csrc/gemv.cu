@@ -197,7 +197,8 @@ __global__ void __launch_bounds__(kStreamBlock, kGemvCtasPerSm) gemv_q_stream(Ge
                 for (int w = 0; w < wpr; ++w) sum += part[r * wpr + w];
                 y[row0 + r] = from_f32<YT>(sum);
             }
-            named_barrier_sync(1, kStreamThreads);
+            // the next flush rewrites the partials: wait for every reader (not after the last)
+            if (c != nchunks - 1) named_barrier_sync(1, kStreamThreads);
         }
     }
 }
