@@ -60,8 +60,7 @@ struct ChainStage {
     uint32_t row_bytes;
     int xtype, ytype;
     int dep;             // the stage whose output x is (-1: x is ready when the chain starts)
-    int dep_off;         // x's first element within that output
-    int dep_n;           // that stage's N (its rows are split over the CTAs like every stage's)
+    int reserved[2];     // keeps the record at 64 bytes (the kernel copies it 16 bytes at a time)
     int post;            // 1: a later stage reads this one's output (the CTAs post their flags)
     int pad;
 };

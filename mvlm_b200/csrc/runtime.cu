@@ -854,7 +854,6 @@ mgpu_gemv_chain* mgpu_gemv_chain_create(const mgpu_device* cd, const mgpu_gemv_l
     REQUIRE(is_quant_type(qtype), "gemv_chain_create: link 0: W must be GGUF Q4_0 or Q8_0");
     std::vector<Range> yr(n), wr(n), xr(n);
     std::vector<int> src(n, -1);
-    std::vector<size_t> src_off(n, 0);
     for (int i = 0; i < n; ++i) {
         const mgpu_gemv_link& L = links[i];
         REQUIRE(L.x && L.W && L.y, "gemv_chain_create: link %d: null buffer", i);
@@ -891,7 +890,6 @@ mgpu_gemv_chain* mgpu_gemv_chain_create(const mgpu_device* cd, const mgpu_gemv_l
             const size_t es = elem_size(L.x->type);
             REQUIRE(off % es == 0, "gemv_chain_create: link %d: x starts inside an element of link %d's y", i, j);
             src[i] = j;
-            src_off[i] = off / es;
             break;
         }
         // x is read four elements at a time
@@ -942,8 +940,6 @@ mgpu_gemv_chain* mgpu_gemv_chain_create(const mgpu_device* cd, const mgpu_gemv_l
         s.xtype = L.x->type;
         s.ytype = L.y->type;
         s.dep = src[i];
-        s.dep_off = src[i] >= 0 ? (int)src_off[i] : 0;
-        s.dep_n = src[i] >= 0 ? links[src[i]].N : 0;
         s.post = post[i];
     }
     e = cudaMemcpyAsync(c->d_stages, st.data(), sizeof(mgpu_k::ChainStage) * n, cudaMemcpyHostToDevice, d->stream);
